@@ -1,0 +1,102 @@
+/* Device-pointer seam of the sm_100a backend.
+ *
+ * These entry points take raw device pointers and a CUDA stream (passed as
+ * void*, NULL = the legacy default stream) and only enqueue work: they do not
+ * synchronise, allocate, or copy to or from the host. They are the CUDA
+ * counterparts of the reference's internal backend seam
+ * (src/backend_hip_direct/hip_backend.hpp:246 hip_direct_pack_i64_device,
+ * :346 hip_direct_gemm_rns_device, :758 hip_direct_gemm_finite_u8_resident_device,
+ * :835 hip_direct_export_i64_device, :933 hip_direct_export_exact_wide_*),
+ * exported with plain C types so a caller that already holds residue planes
+ * in HBM can drive the pipeline without host round trips.
+ *
+ * Layout: residue planes are modulus-major and compact; plane p of an
+ * R x C matrix is the int8 array base[p*R*C .. (p+1)*R*C) in row-major order.
+ * Plane p uses modulus rns8_default_modulus(p).
+ *
+ * Device status words: export and GEMM calls OR an error code into *d_status
+ * (5 = a value violated its range contract, 0x100 = a bounded device wait ran
+ * out). The caller zeroes the word before the call and reads it after
+ * synchronising. On a non-zero status the destination contents are
+ * unspecified.
+ *
+ * Return value: RNS8_SUCCESS when the work was enqueued, RNS8_INVALID_ARGUMENT
+ * for malformed arguments, RNS8_BACKEND_FAILURE for a CUDA launch error. */
+#ifndef RNS8_RNS8_CUDA_H
+#define RNS8_RNS8_CUDA_H
+
+#include <stdint.h>
+
+#include "rns8/rns8.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Kernel selection for the plane GEMM. AUTO uses the tcgen05 tensor-core
+ * kernel whenever K and N are multiples of 16 and the SIMT kernel otherwise. */
+#define RNS8_CUDA_GEMM_AUTO 0u
+#define RNS8_CUDA_GEMM_TENSOR_CORE 1u
+#define RNS8_CUDA_GEMM_SIMT 2u
+
+/* Native int64/uint64 (row-major, leading dimension ld >= cols) -> prefix
+ * centered residue planes. Replaces hip_backend.hpp:246 / :296. */
+RNS8_API rns8_status rns8_cuda_pack_i64_device(int device_id, const int64_t* d_src, int64_t rows, int64_t cols,
+                                               int64_t ld, uint32_t prefix, int8_t* d_planes, void* stream);
+RNS8_API rns8_status rns8_cuda_pack_u64_device(int device_id, const uint64_t* d_src, int64_t rows, int64_t cols,
+                                               int64_t ld, uint32_t prefix, int8_t* d_planes, void* stream);
+/* uint8 -> centered residues modulo `modulus` in [2, 256]. Replaces
+ * hip_backend.hpp pack_finite_u8. */
+RNS8_API rns8_status rns8_cuda_pack_finite_u8_device(int device_id, const uint8_t* d_src, int64_t rows, int64_t cols,
+                                                     int64_t ld, uint16_t modulus, int8_t* d_residues, void* stream);
+
+/* Scratch bytes the plane GEMM needs for split-K on this shape (0 = none). */
+RNS8_API uint64_t rns8_cuda_gemm_rns_scratch_bytes(int device_id, int64_t m, int64_t n, int64_t k, uint32_t prefix);
+
+/* Per plane p < prefix: C_p = (A_p x B_p) mod m_p, centered. A is m x k, B is
+ * k x n, C is m x n, all compact planes. Replaces hip_backend.hpp:346. */
+RNS8_API rns8_status rns8_cuda_gemm_rns_device(int device_id, const int8_t* d_a, const int8_t* d_b, int8_t* d_c,
+                                               int64_t m, int64_t n, int64_t k, uint32_t prefix, uint32_t gemm_path,
+                                               void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
+                                               void* stream);
+
+/* Same-shape batch of single-plane GEMMs modulo `modulus` (finite u8 ring or
+ * field). d_a/d_b/d_c are host arrays of task_count device pointers.
+ * Replaces hip_backend.hpp:758 and the grouped finite dispatch. */
+RNS8_API uint64_t rns8_cuda_gemm_finite_u8_scratch_bytes(int device_id, int64_t m, int64_t n, int64_t k,
+                                                         uint32_t task_count);
+RNS8_API rns8_status rns8_cuda_gemm_finite_u8_grouped_device(int device_id, const int8_t* const* d_a,
+                                                             const int8_t* const* d_b, int8_t* const* d_c,
+                                                             uint32_t task_count, int64_t m, int64_t n, int64_t k,
+                                                             uint16_t modulus, uint32_t gemm_path, void* d_scratch,
+                                                             uint64_t scratch_bytes, uint32_t* d_status,
+                                                             void* stream);
+
+/* Garner reconstruction + bounded export. The bound must satisfy the plan
+ * contract for the prefix (product > 2*bound signed, > bound unsigned).
+ * Replaces hip_backend.hpp:835 and the u64 variant. */
+RNS8_API rns8_status rns8_cuda_export_i64_device(int device_id, const int8_t* d_planes, int64_t m, int64_t n,
+                                                 uint32_t prefix, uint64_t bound, int64_t* d_dst, int64_t ld,
+                                                 uint32_t* d_status, void* stream);
+RNS8_API rns8_status rns8_cuda_export_u64_device(int device_id, const int8_t* d_planes, int64_t m, int64_t n,
+                                                 uint32_t prefix, uint64_t bound, uint64_t* d_dst, int64_t ld,
+                                                 uint32_t* d_status, void* stream);
+/* Exact-wide limbs: dst[(row*ld + col)*limb_count + limb]. Replaces
+ * hip_backend.hpp:933 and the unsigned variant. */
+RNS8_API rns8_status rns8_cuda_export_limbs_device(int device_id, const int8_t* d_planes, int64_t m, int64_t n,
+                                                   uint32_t prefix, uint32_t is_signed, uint32_t limb_count,
+                                                   uint64_t* d_dst, int64_t ld, uint32_t* d_status, void* stream);
+RNS8_API rns8_status rns8_cuda_export_finite_u8_device(int device_id, const int8_t* d_residues, int64_t m, int64_t n,
+                                                       uint16_t modulus, uint8_t* d_dst, int64_t ld, void* stream);
+
+/* Host-only: run the plan validation and prefix schedule of rns8_create_plan
+ * for a descriptor without a context (no device needed). Writes the selected
+ * and required prefix and the effective output bound on success. */
+RNS8_API rns8_status rns8_cuda_plan_probe(const rns8_gemm_desc* desc, uint32_t* selected_prefix,
+                                          uint32_t* required_prefix, uint64_t* effective_bound);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RNS8_RNS8_CUDA_H */

@@ -1,0 +1,661 @@
+// Pack, plane GEMM, export and one-shot entry points of the rns8 C ABI on the
+// sm_100a kernels.
+//
+// Reference behaviour followed here:
+//   src/core/api_pack.cpp:31-305      argument checks, same-source-version elision,
+//                                     exact-wide input proofs before packing
+//   src/core/api_gemm.cpp:1-345,838-1143,1267-1450
+//                                     operand validation, exact-wide admission,
+//                                     grouped execution, finite GEMM
+//   src/core/api_export.cpp:1-803     export validation; a RANGE_ERROR leaves dst untouched
+//   src/core/api_oneshot.cpp:61-677   one-shot contracts and orchestration
+// Host buffers are copied with cudaMemcpy2DAsync so caller leading dimensions
+// never reach the kernels, and every call ends with a stream synchronisation.
+#include <cstring>
+#include <limits>
+#include <vector>
+
+#include "api_internal.hpp"
+
+namespace rns8host {
+namespace {
+
+struct DeviceScope {
+  explicit DeviceScope(int dev) { ok = cudaSetDevice(dev) == cudaSuccess; }
+  bool ok;
+};
+
+rns8_status sync(rns8_context& ctx) { return cuda_status(cudaStreamSynchronize(ctx.stream)); }
+
+uint64_t combine_source_versions(uint64_t a, uint64_t b) {
+  if (a == 0 || b == 0) return 0;
+  uint64_t h = 1469598103934665603ull;
+  h = (h ^ a) * 1099511628211ull;
+  h = (h ^ b) * 1099511628211ull;
+  return h == 0 ? 1 : h;
+}
+
+// Device status word: zero, run, read back.
+rns8_status read_status(rns8_context& ctx, uint32_t* out) {
+  const cudaError_t e = cudaMemcpyAsync(out, ctx.dev_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, ctx.stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  return sync(ctx);
+}
+rns8_status clear_status(rns8_context& ctx) {
+  return cuda_status(cudaMemsetAsync(ctx.dev_status, 0, 4 * sizeof(uint32_t), ctx.stream));
+}
+rns8_status status_from_device(uint32_t word) {
+  if (word == 0) return RNS8_SUCCESS;
+  if (word & rns8cuda::kDevWaitTimeout) return RNS8_BACKEND_FAILURE;
+  return RNS8_RANGE_ERROR;
+}
+
+rns8_status copy_in_2d(rns8_context& ctx, void* dst, const void* src, int64_t rows, int64_t cols, int64_t ld,
+                       size_t elem) {
+  return cuda_status(cudaMemcpy2DAsync(dst, static_cast<size_t>(cols) * elem, src, static_cast<size_t>(ld) * elem,
+                                       static_cast<size_t>(cols) * elem, static_cast<size_t>(rows),
+                                       cudaMemcpyHostToDevice, ctx.stream));
+}
+rns8_status copy_out_2d(rns8_context& ctx, void* dst, int64_t ld, const void* src, int64_t rows, int64_t cols,
+                        size_t elem) {
+  return cuda_status(cudaMemcpy2DAsync(dst, static_cast<size_t>(ld) * elem, src, static_cast<size_t>(cols) * elem,
+                                       static_cast<size_t>(cols) * elem, static_cast<size_t>(rows),
+                                       cudaMemcpyDeviceToHost, ctx.stream));
+}
+
+bool plan_context_ok(const rns8_context& ctx, const rns8_plan& plan) {
+  return plan.backend == ctx.backend && plan.device_id == ctx.device_id;
+}
+
+// validate_plan_context_workspace (api_workspace_contracts_resources.inc:222-247).
+rns8_status validate_workspace(const rns8_context& ctx, const rns8_plan& plan, const rns8_workspace& ws) {
+  if (!plan_context_ok(ctx, plan) || ws.backend != plan.backend) return RNS8_INVALID_ARGUMENT;
+  if (ws.semantics != plan.desc.semantics) return RNS8_INVALID_ARGUMENT;
+  if (ws.m != plan.desc.m || ws.n != plan.desc.n || ws.k != plan.desc.k || ws.prefix != plan.prefix)
+    return RNS8_WORKSPACE_TOO_SMALL;
+  if (ws.plan_fingerprint != plan.fingerprint || ws.device_id != ctx.device_id) return RNS8_INVALID_ARGUMENT;
+  return RNS8_SUCCESS;
+}
+
+// matrix_descriptor_matches (api_matrix_currentness_storage.inc:1-23).
+bool descriptor_matches(const rns8_matrix& mtx, rns8_semantics s, rns8_bound_kind bk, int64_t rows, int64_t cols,
+                        uint32_t prefix) {
+  if (mtx.desc.semantics != s || mtx.desc.bound_kind != bk || mtx.desc.rows != rows || mtx.desc.cols != cols ||
+      mtx.desc.logical_layout != RNS8_LAYOUT_ROW_MAJOR || mtx.prefix < prefix || mtx.desc.max_prefix < prefix)
+    return false;
+  if (prefix == 0 && (mtx.prefix != 0 || mtx.desc.max_prefix != 0)) return false;
+  return mtx.residues != nullptr;
+}
+
+rns8_status validate_rns_operands(const rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& A,
+                                  const rns8_matrix& B, const rns8_matrix& C) {
+  if (!uses_rns_storage(plan.desc.semantics) || plan.prefix == 0) return RNS8_INVALID_ARGUMENT;
+  if (A.device_id != ctx.device_id || B.device_id != ctx.device_id || C.device_id != ctx.device_id)
+    return RNS8_INVALID_ARGUMENT;
+  const rns8_bound_kind bk = storage_bound_kind(plan);
+  const auto& d = plan.desc;
+  if (!descriptor_matches(A, d.semantics, bk, d.m, d.k, plan.prefix) ||
+      !descriptor_matches(B, d.semantics, bk, d.k, d.n, plan.prefix) ||
+      !descriptor_matches(C, d.semantics, bk, d.m, d.n, plan.prefix))
+    return RNS8_INVALID_ARGUMENT;
+  if (!A.device_current || !B.device_current) return RNS8_INVALID_ARGUMENT;
+  if (exact_wide(d.semantics) && (&A == &C || &B == &C)) return RNS8_INVALID_ARGUMENT;
+  return RNS8_SUCCESS;
+}
+
+rns8_status validate_finite_operands(const rns8_context& ctx, const rns8_plan& plan, uint16_t modulus,
+                                     const rns8_matrix& A, const rns8_matrix& B, const rns8_matrix& C) {
+  if (!uses_finite_storage(plan.desc.semantics) ||
+      !valid_finite_modulus_for_semantics(plan.desc.semantics, modulus) || plan.desc.finite_modulus != modulus)
+    return RNS8_INVALID_ARGUMENT;
+  if (A.device_id != ctx.device_id || B.device_id != ctx.device_id || C.device_id != ctx.device_id)
+    return RNS8_INVALID_ARGUMENT;
+  const auto& d = plan.desc;
+  if (!descriptor_matches(A, d.semantics, RNS8_BOUND_NONE, d.m, d.k, 0) ||
+      !descriptor_matches(B, d.semantics, RNS8_BOUND_NONE, d.k, d.n, 0) ||
+      !descriptor_matches(C, d.semantics, RNS8_BOUND_NONE, d.m, d.n, 0))
+    return RNS8_INVALID_ARGUMENT;
+  if (!A.device_current || !B.device_current || A.finite_modulus != modulus || B.finite_modulus != modulus)
+    return RNS8_INVALID_ARGUMENT;
+  return RNS8_SUCCESS;
+}
+
+rns8_status run_plane_gemm(rns8_context& ctx, const rns8cuda::PlaneGemmProblem& prob, rns8_workspace* ws) {
+  const uint64_t need = rns8cuda::plane_gemm_scratch_bytes(prob, ctx.sm_count);
+  void* scratch = nullptr;
+  if (need) {
+    if (!ws) return RNS8_INVALID_ARGUMENT;
+    const rns8_status s = ws->scratch.ensure(ctx.device_id, need);
+    if (s != RNS8_SUCCESS) return s;
+    scratch = ws->scratch.ptr;
+  }
+  rns8_status s = clear_status(ctx);
+  if (s != RNS8_SUCCESS) return s;
+  s = cuda_status(rns8cuda::plane_gemm(prob, rns8cuda::GemmPath::Auto, ctx.sm_count, scratch, need, ctx.dev_status,
+                                       ctx.stream));
+  if (s != RNS8_SUCCESS) return s;
+  uint32_t word = 0;
+  s = read_status(ctx, &word);
+  if (s != RNS8_SUCCESS) return s;
+  return word == 0 ? RNS8_SUCCESS : RNS8_BACKEND_FAILURE;
+}
+
+rns8cuda::PlaneGemmProblem rns_problem(const rns8_plan& plan, uint32_t planes, const rns8cuda::PlaneGemmTask* tasks,
+                                       uint32_t count, uint16_t finite_modulus) {
+  rns8cuda::PlaneGemmProblem prob{};
+  prob.m = plan.desc.m;
+  prob.n = plan.desc.n;
+  prob.k = plan.desc.k;
+  prob.planes = planes;
+  for (uint32_t p = 0; p < planes; ++p) prob.moduli[p] = finite_modulus ? finite_modulus : kLadder[p];
+  prob.task_count = count;
+  prob.tasks = tasks;
+  return prob;
+}
+
+template <typename T>
+rns8_status pack_native(rns8_context* ctx, rns8_matrix* matrix, const T* src, int64_t ld, uint64_t source_version) {
+  constexpr bool kSigned = std::numeric_limits<T>::is_signed;
+  if (!ctx || !matrix || !src || !valid_matrix_access(matrix->desc.rows, matrix->desc.cols, ld))
+    return RNS8_INVALID_ARGUMENT;
+  const rns8_semantics s = matrix->desc.semantics;
+  if (kSigned ? (s != RNS8_BOUNDED_I64 && s != RNS8_EXACT_WIDE_SIGNED)
+              : (s != RNS8_BOUNDED_U64 && s != RNS8_EXACT_WIDE_UNSIGNED && s != RNS8_WRAP_U64_MOD_2_64))
+    return RNS8_INVALID_ARGUMENT;
+  if (s == RNS8_WRAP_U64_MOD_2_64) return RNS8_UNSUPPORTED_BACKEND;
+  if (ctx->backend != matrix->backend || matrix->device_id != ctx->device_id || matrix->prefix == 0)
+    return RNS8_INVALID_ARGUMENT;
+  const bool same_source = source_version != 0 && matrix->source_version == source_version && matrix->device_current;
+  i256 exact_bound;
+  ExactRanges ranges;
+  if (exact_wide(s)) {
+    if (same_source) {
+      exact_bound = matrix->exact_max_magnitude;
+    } else {
+      native_exact_ranges<T>(src, matrix->desc.rows, matrix->desc.cols, ld, ranges, exact_bound);
+    }
+    if (!exact_range_fits(s, exact_bound, modulus_product(matrix->prefix))) return RNS8_RANGE_ERROR;
+  }
+  if (same_source) return RNS8_SUCCESS;
+  DeviceScope dev(ctx->device_id);
+  if (!dev.ok) return RNS8_BACKEND_FAILURE;
+  const int64_t rows = matrix->desc.rows, cols = matrix->desc.cols;
+  rns8_status st = matrix->upload.ensure(ctx->device_id, static_cast<uint64_t>(rows) * cols * sizeof(T));
+  if (st != RNS8_SUCCESS) return st;
+  matrix->device_current = false;
+  st = copy_in_2d(*ctx, matrix->upload.ptr, src, rows, cols, ld, sizeof(T));
+  if (st != RNS8_SUCCESS) return st;
+  const cudaError_t e =
+      kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(matrix->upload.ptr), rows, cols, cols,
+                                   matrix->prefix, matrix->residues, ctx->stream)
+              : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(matrix->upload.ptr), rows, cols, cols,
+                                   matrix->prefix, matrix->residues, ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  st = sync(*ctx);
+  if (st != RNS8_SUCCESS) return st;
+  matrix->device_current = true;
+  if (exact_wide(s)) {
+    matrix->exact_max_magnitude = exact_bound;
+    matrix->exact_axes.rows.swap(ranges.rows);
+    matrix->exact_axes.cols.swap(ranges.cols);
+    matrix->exact_range_prefix = matrix->prefix;
+  }
+  matrix->source_version = source_version;
+  return RNS8_SUCCESS;
+}
+
+// validate_export_matrix (api_export.cpp:5-52) for RNS outputs.
+rns8_status validate_rns_export(const rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& C,
+                                rns8_semantics semantics) {
+  if (!plan_context_ok(ctx, plan) || plan.desc.semantics != semantics) return RNS8_INVALID_ARGUMENT;
+  if (C.device_id != ctx.device_id || C.backend != plan.backend) return RNS8_INVALID_ARGUMENT;
+  if (!descriptor_matches(C, semantics, storage_bound_kind(plan), plan.desc.m, plan.desc.n, plan.prefix))
+    return RNS8_INVALID_ARGUMENT;
+  if (!C.device_current) return RNS8_INVALID_ARGUMENT;
+  if (exact_wide(semantics) && C.exact_range_prefix != 0 &&
+      (C.exact_range_prefix < plan.prefix || !exact_range_fits(semantics, C.exact_max_magnitude, plan.modulus_product)))
+    return RNS8_RANGE_ERROR;
+  return RNS8_SUCCESS;
+}
+
+enum class ExportKind { I64, U64, LimbsS, LimbsU };
+
+// Reconstruct into the matrix's staging buffer, check the status word, and
+// only then copy to the caller's buffer (dst untouched on RANGE_ERROR).
+rns8_status export_rns(rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& Cc, void* dst, int64_t ld,
+                       ExportKind kind, uint32_t limbs) {
+  rns8_matrix& C = const_cast<rns8_matrix&>(Cc);  // export staging is a documented mutable cache
+  DeviceScope dev(ctx.device_id);
+  if (!dev.ok) return RNS8_BACKEND_FAILURE;
+  const int64_t m = plan.desc.m, n = plan.desc.n;
+  const uint64_t per_cell = (kind == ExportKind::LimbsS || kind == ExportKind::LimbsU) ? 8ull * limbs : 8ull;
+  rns8_status st = C.staging.ensure(ctx.device_id, static_cast<uint64_t>(m) * n * per_cell);
+  if (st != RNS8_SUCCESS) return st;
+  st = clear_status(ctx);
+  if (st != RNS8_SUCCESS) return st;
+  cudaError_t e = cudaSuccess;
+  switch (kind) {
+    case ExportKind::I64:
+      e = rns8cuda::export_i64(C.residues, m, n, plan.prefix, plan.desc.bound, static_cast<int64_t*>(C.staging.ptr), n,
+                               ctx.dev_status, ctx.stream);
+      break;
+    case ExportKind::U64:
+      e = rns8cuda::export_u64(C.residues, m, n, plan.prefix, plan.desc.bound, static_cast<uint64_t*>(C.staging.ptr),
+                               n, ctx.dev_status, ctx.stream);
+      break;
+    case ExportKind::LimbsS:
+    case ExportKind::LimbsU:
+      e = rns8cuda::export_limbs(C.residues, m, n, plan.prefix, kind == ExportKind::LimbsS, limbs,
+                                 static_cast<uint64_t*>(C.staging.ptr), n, ctx.dev_status, ctx.stream);
+      break;
+  }
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  uint32_t word = 0;
+  st = read_status(ctx, &word);
+  if (st != RNS8_SUCCESS) return st;
+  st = status_from_device(word);
+  if (st != RNS8_SUCCESS) return st;
+  st = copy_out_2d(ctx, dst, ld * static_cast<int64_t>(per_cell / 8), C.staging.ptr, m, n * static_cast<int64_t>(per_cell / 8),
+                   sizeof(uint64_t));
+  if (st != RNS8_SUCCESS) return st;
+  return sync(ctx);
+}
+
+bool valid_limb_export_access(int64_t rows, int64_t cols, int64_t ld, uint32_t limbs) {
+  if (!valid_matrix_access(rows, cols, ld) || limbs == 0 || limbs > 32) return false;
+  const int64_t max = std::numeric_limits<int64_t>::max();
+  if (ld > max / static_cast<int64_t>(limbs)) return false;
+  return rows <= max / (ld * static_cast<int64_t>(limbs));
+}
+
+// ---- one-shot device arena -------------------------------------------------
+struct Carve {
+  uint8_t* base;
+  uint64_t off = 0;
+  void* take(uint64_t bytes) {
+    void* p = base + off;
+    off += (bytes + 255) & ~uint64_t(255);
+    return p;
+  }
+};
+uint64_t round256(uint64_t b) { return (b + 255) & ~uint64_t(255); }
+
+// validate_typed_oneshot_contract (api_oneshot.cpp:440-466).
+rns8_status validate_typed_oneshot(const rns8_gemm_desc& d, rns8_semantics expected, int64_t lda, int64_t ldb,
+                                   int64_t ldc) {
+  if (!valid_abi(d.struct_size, d.abi_version, sizeof(d)) || d.semantics != expected) return RNS8_INVALID_ARGUMENT;
+  const uint32_t prefix = d.max_prefix == 0 ? default_prefix_for_semantics(d.semantics) : d.max_prefix;
+  const rns8_status v = validate_gemm_desc(d, prefix);
+  if (v != RNS8_SUCCESS) return v;
+  if (!valid_matrix_access(d.m, d.k, lda) || !valid_matrix_access(d.k, d.n, ldb) || !valid_matrix_access(d.m, d.n, ldc))
+    return RNS8_INVALID_ARGUMENT;
+  if (!backend_request_ok(d.requested_backend)) return RNS8_UNSUPPORTED_BACKEND;
+  return RNS8_SUCCESS;
+}
+
+template <typename T>
+rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const T* A, int64_t lda, const T* B,
+                            int64_t ldb, T* C, int64_t ldc) {
+  constexpr bool kSigned = std::numeric_limits<T>::is_signed;
+  if (!ctx || !desc || !A || !B || !C) return RNS8_INVALID_ARGUMENT;
+  rns8_status st = validate_typed_oneshot(*desc, kSigned ? RNS8_BOUNDED_I64 : RNS8_BOUNDED_U64, lda, ldb, ldc);
+  if (st != RNS8_SUCCESS) return st;
+  rns8_plan plan;
+  plan.device_id = ctx->device_id;
+  st = build_plan(*desc, plan);
+  if (st != RNS8_SUCCESS) return st;
+  DeviceScope dev(ctx->device_id);
+  if (!dev.ok) return RNS8_BACKEND_FAILURE;
+  const int64_t m = plan.desc.m, n = plan.desc.n, k = plan.desc.k;
+  const uint32_t P = plan.prefix;
+  const uint64_t a_nat = static_cast<uint64_t>(m) * k * 8, b_nat = static_cast<uint64_t>(k) * n * 8;
+  const uint64_t a_res = static_cast<uint64_t>(P) * m * k, b_res = static_cast<uint64_t>(P) * k * n;
+  const uint64_t c_res = static_cast<uint64_t>(P) * m * n, c_nat = static_cast<uint64_t>(m) * n * 8;
+  rns8cuda::PlaneGemmTask task{nullptr, nullptr, nullptr};
+  rns8cuda::PlaneGemmProblem prob = rns_problem(plan, P, &task, 1, 0);
+  // Scratch size depends only on shape and alignment; the arena keeps 256-byte alignment.
+  task = {reinterpret_cast<const int8_t*>(256), reinterpret_cast<const int8_t*>(256), reinterpret_cast<int8_t*>(256)};
+  const uint64_t scratch = rns8cuda::plane_gemm_scratch_bytes(prob, ctx->sm_count);
+  const uint64_t total = round256(a_nat) + round256(b_nat) + round256(a_res) + round256(b_res) + round256(c_res) +
+                         round256(c_nat) + round256(scratch);
+  std::unique_lock<std::mutex> lock(ctx->oneshot_mutex, std::try_to_lock);
+  DevBuf local;
+  DevBuf& arena = lock.owns_lock() ? ctx->oneshot_arena : local;
+  st = arena.ensure(ctx->device_id, total);
+  if (st != RNS8_SUCCESS) return st;
+  Carve cv{static_cast<uint8_t*>(arena.ptr)};
+  T* dA = static_cast<T*>(cv.take(a_nat));
+  T* dB = static_cast<T*>(cv.take(b_nat));
+  int8_t* rA = static_cast<int8_t*>(cv.take(a_res));
+  int8_t* rB = static_cast<int8_t*>(cv.take(b_res));
+  int8_t* rC = static_cast<int8_t*>(cv.take(c_res));
+  T* dC = static_cast<T*>(cv.take(c_nat));
+  void* dS = scratch ? cv.take(scratch) : nullptr;
+  if ((st = copy_in_2d(*ctx, dA, A, m, k, lda, sizeof(T))) != RNS8_SUCCESS) return st;
+  if ((st = copy_in_2d(*ctx, dB, B, k, n, ldb, sizeof(T))) != RNS8_SUCCESS) return st;
+  cudaError_t e = kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(dA), m, k, k, P, rA, ctx->stream)
+                          : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(dA), m, k, k, P, rA, ctx->stream);
+  if (e == cudaSuccess)
+    e = kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(dB), k, n, n, P, rB, ctx->stream)
+                : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(dB), k, n, n, P, rB, ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  if ((st = clear_status(*ctx)) != RNS8_SUCCESS) return st;
+  task = {rA, rB, rC};
+  e = rns8cuda::plane_gemm(prob, rns8cuda::GemmPath::Auto, ctx->sm_count, dS, scratch, ctx->dev_status, ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  e = kSigned ? rns8cuda::export_i64(rC, m, n, P, plan.desc.bound, reinterpret_cast<int64_t*>(dC), n, ctx->dev_status,
+                                     ctx->stream)
+              : rns8cuda::export_u64(rC, m, n, P, plan.desc.bound, reinterpret_cast<uint64_t*>(dC), n, ctx->dev_status,
+                                     ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  uint32_t word = 0;
+  if ((st = read_status(*ctx, &word)) != RNS8_SUCCESS) return st;
+  if ((st = status_from_device(word)) != RNS8_SUCCESS) return st;
+  if ((st = copy_out_2d(*ctx, C, ldc, dC, m, n, sizeof(T))) != RNS8_SUCCESS) return st;
+  return sync(*ctx);
+}
+
+// validate_finite_u8_oneshot_contract (api_oneshot.cpp:78-106).
+rns8_status finite_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, rns8_semantics expected, uint16_t modulus,
+                           const uint8_t* A, int64_t lda, const uint8_t* B, int64_t ldb, uint8_t* C, int64_t ldc) {
+  if (!ctx || !desc || !A || !B || !C) return RNS8_INVALID_ARGUMENT;
+  const rns8_gemm_desc& d = *desc;
+  if (!valid_abi(d.struct_size, d.abi_version, sizeof(d)) || d.semantics != expected) return RNS8_INVALID_ARGUMENT;
+  if (!valid_finite_modulus_for_semantics(expected, modulus) || d.m <= 0 || d.n <= 0 || d.k <= 0 ||
+      d.bound_kind != RNS8_BOUND_NONE || d.bound != 0 || d.max_prefix != 0 || d.finite_modulus != modulus ||
+      d.flags != 0 || d.tile_bounds || d.tile_bounds_count != 0 || d.lhs_bound != 0 || d.rhs_bound != 0 ||
+      !valid_tile_size(d.tile_m) || !valid_tile_size(d.tile_n))
+    return RNS8_INVALID_ARGUMENT;
+  if (!valid_matrix_access(d.m, d.k, lda) || !valid_matrix_access(d.k, d.n, ldb) || !valid_matrix_access(d.m, d.n, ldc))
+    return RNS8_INVALID_ARGUMENT;
+  if (!backend_request_ok(d.requested_backend)) return RNS8_UNSUPPORTED_BACKEND;
+  DeviceScope dev(ctx->device_id);
+  if (!dev.ok) return RNS8_BACKEND_FAILURE;
+  const int64_t m = d.m, n = d.n, k = d.k;
+  const uint64_t a = static_cast<uint64_t>(m) * k, b = static_cast<uint64_t>(k) * n, c = static_cast<uint64_t>(m) * n;
+  rns8_plan plan;
+  plan.desc = d;
+  rns8cuda::PlaneGemmTask task{reinterpret_cast<const int8_t*>(256), reinterpret_cast<const int8_t*>(256),
+                               reinterpret_cast<int8_t*>(256)};
+  rns8cuda::PlaneGemmProblem prob = rns_problem(plan, 1, &task, 1, modulus);
+  const uint64_t scratch = rns8cuda::plane_gemm_scratch_bytes(prob, ctx->sm_count);
+  const uint64_t total =
+      2 * round256(a) + 2 * round256(b) + 2 * round256(c) + round256(scratch);
+  std::unique_lock<std::mutex> lock(ctx->oneshot_mutex, std::try_to_lock);
+  DevBuf local;
+  DevBuf& arena = lock.owns_lock() ? ctx->oneshot_arena : local;
+  rns8_status st = arena.ensure(ctx->device_id, total);
+  if (st != RNS8_SUCCESS) return st;
+  Carve cv{static_cast<uint8_t*>(arena.ptr)};
+  uint8_t* dA = static_cast<uint8_t*>(cv.take(a));
+  uint8_t* dB = static_cast<uint8_t*>(cv.take(b));
+  int8_t* rA = static_cast<int8_t*>(cv.take(a));
+  int8_t* rB = static_cast<int8_t*>(cv.take(b));
+  int8_t* rC = static_cast<int8_t*>(cv.take(c));
+  uint8_t* dC = static_cast<uint8_t*>(cv.take(c));
+  void* dS = scratch ? cv.take(scratch) : nullptr;
+  if ((st = copy_in_2d(*ctx, dA, A, m, k, lda, 1)) != RNS8_SUCCESS) return st;
+  if ((st = copy_in_2d(*ctx, dB, B, k, n, ldb, 1)) != RNS8_SUCCESS) return st;
+  cudaError_t e = rns8cuda::pack_finite_u8(dA, m, k, k, modulus, rA, ctx->stream);
+  if (e == cudaSuccess) e = rns8cuda::pack_finite_u8(dB, k, n, n, modulus, rB, ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  if ((st = clear_status(*ctx)) != RNS8_SUCCESS) return st;
+  task = {rA, rB, rC};
+  e = rns8cuda::plane_gemm(prob, rns8cuda::GemmPath::Auto, ctx->sm_count, dS, scratch, ctx->dev_status, ctx->stream);
+  if (e == cudaSuccess) e = rns8cuda::export_finite_u8(rC, m, n, modulus, dC, n, ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  uint32_t word = 0;
+  if ((st = read_status(*ctx, &word)) != RNS8_SUCCESS) return st;
+  if (word != 0) return RNS8_BACKEND_FAILURE;
+  if ((st = copy_out_2d(*ctx, C, ldc, dC, m, n, 1)) != RNS8_SUCCESS) return st;
+  return sync(*ctx);
+}
+
+rns8_status grouped_gemm(rns8_context* ctx, const rns8_plan* plan, const rns8_grouped_gemm_task* tasks,
+                         uint32_t count, bool finite, uint16_t modulus) {
+  if (!ctx || !plan) return RNS8_INVALID_ARGUMENT;
+  if ((finite && (!uses_finite_storage(plan->desc.semantics) || plan->desc.finite_modulus != modulus ||
+                  !valid_finite_modulus_for_semantics(plan->desc.semantics, modulus))) ||
+      (!finite && !uses_rns_storage(plan->desc.semantics)))
+    return RNS8_INVALID_ARGUMENT;
+  if (!tasks || count <= 1) return RNS8_INVALID_ARGUMENT;
+  for (uint32_t i = 0; i < count; ++i) {
+    const auto& t = tasks[i];
+    if (!valid_abi(t.struct_size, t.abi_version, sizeof(t)) || !t.a || !t.b || !t.c || !t.workspace)
+      return RNS8_INVALID_ARGUMENT;
+    const rns8_status ws = validate_workspace(*ctx, *plan, *t.workspace);
+    if (ws != RNS8_SUCCESS) return ws;
+  }
+  std::vector<i256> bounds(exact_wide(plan->desc.semantics) ? count : 0);
+  std::vector<ExactRanges> ranges(bounds.size());
+  for (uint32_t i = 0; i < count; ++i) {
+    const auto& t = tasks[i];
+    const rns8_status v = finite ? validate_finite_operands(*ctx, *plan, modulus, *t.a, *t.b, *t.c)
+                                 : validate_rns_operands(*ctx, *plan, *t.a, *t.b, *t.c);
+    if (v != RNS8_SUCCESS) return v;
+    // Outputs are written concurrently: no output may alias an input or another output.
+    for (uint32_t j = 0; j < count; ++j) {
+      if (t.c == tasks[j].a || t.c == tasks[j].b || (i != j && t.c == tasks[j].c)) return RNS8_INVALID_ARGUMENT;
+    }
+    if (!bounds.empty()) {
+      const rns8_status r = exact_gemm_range(*plan, *t.a, *t.b, bounds[i], &ranges[i]);
+      if (r != RNS8_SUCCESS) return r;
+    }
+  }
+  DeviceScope dev(ctx->device_id);
+  if (!dev.ok) return RNS8_BACKEND_FAILURE;
+  std::vector<rns8cuda::PlaneGemmTask> list(count);
+  for (uint32_t i = 0; i < count; ++i) list[i] = {tasks[i].a->residues, tasks[i].b->residues, tasks[i].c->residues};
+  for (uint32_t i = 0; i < count; ++i) tasks[i].c->device_current = false;
+  const rns8cuda::PlaneGemmProblem prob =
+      rns_problem(*plan, finite ? 1 : plan->prefix, list.data(), count, finite ? modulus : 0);
+  const rns8_status st = run_plane_gemm(*ctx, prob, tasks[0].workspace);
+  if (st != RNS8_SUCCESS) return st;
+  for (uint32_t i = 0; i < count; ++i) {
+    rns8_matrix& C = *tasks[i].c;
+    C.device_current = true;
+    C.source_version = combine_source_versions(tasks[i].a->source_version, tasks[i].b->source_version);
+    if (finite) C.finite_modulus = modulus;
+    if (!bounds.empty()) commit_exact_range(C, *plan, bounds[i], &ranges[i]);
+  }
+  return RNS8_SUCCESS;
+}
+
+}  // namespace
+}  // namespace rns8host
+
+using namespace rns8host;
+
+extern "C" rns8_status rns8_pack_i64(rns8_context* ctx, rns8_matrix* matrix, const int64_t* src, int64_t ld,
+                                     uint64_t source_version) {
+  return guard([&] { return pack_native<int64_t>(ctx, matrix, src, ld, source_version); });
+}
+
+extern "C" rns8_status rns8_pack_u64(rns8_context* ctx, rns8_matrix* matrix, const uint64_t* src, int64_t ld,
+                                     uint64_t source_version) {
+  return guard([&] { return pack_native<uint64_t>(ctx, matrix, src, ld, source_version); });
+}
+
+extern "C" rns8_status rns8_pack_finite_u8(rns8_context* ctx, rns8_matrix* matrix, uint16_t modulus,
+                                           const uint8_t* src, int64_t ld, uint64_t source_version) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !matrix || !src || !valid_matrix_access(matrix->desc.rows, matrix->desc.cols, ld) ||
+        !valid_finite_modulus_for_semantics(matrix->desc.semantics, modulus))
+      return RNS8_INVALID_ARGUMENT;
+    if (ctx->backend != matrix->backend || matrix->device_id != ctx->device_id) return RNS8_INVALID_ARGUMENT;
+    if (!uses_finite_storage(matrix->desc.semantics) || matrix->prefix != 0) return RNS8_INVALID_ARGUMENT;
+    if (source_version != 0 && matrix->source_version == source_version && matrix->finite_modulus == modulus &&
+        matrix->device_current)
+      return RNS8_SUCCESS;
+    DeviceScope dev(ctx->device_id);
+    if (!dev.ok) return RNS8_BACKEND_FAILURE;
+    const int64_t rows = matrix->desc.rows, cols = matrix->desc.cols;
+    rns8_status st = matrix->upload.ensure(ctx->device_id, static_cast<uint64_t>(rows) * cols);
+    if (st != RNS8_SUCCESS) return st;
+    matrix->device_current = false;
+    if ((st = copy_in_2d(*ctx, matrix->upload.ptr, src, rows, cols, ld, 1)) != RNS8_SUCCESS) return st;
+    if (rns8cuda::pack_finite_u8(static_cast<const uint8_t*>(matrix->upload.ptr), rows, cols, cols, modulus,
+                                 matrix->residues, ctx->stream) != cudaSuccess)
+      return RNS8_BACKEND_FAILURE;
+    if ((st = sync(*ctx)) != RNS8_SUCCESS) return st;
+    matrix->device_current = true;
+    matrix->finite_modulus = modulus;
+    matrix->source_version = source_version;
+    return RNS8_SUCCESS;
+  });
+}
+
+extern "C" rns8_status rns8_gemm_rns(rns8_context* ctx, const rns8_plan* plan, const rns8_matrix* A,
+                                     const rns8_matrix* B, rns8_matrix* C, rns8_workspace* workspace) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !A || !B || !C || !workspace) return RNS8_INVALID_ARGUMENT;
+    rns8_status st = validate_workspace(*ctx, *plan, *workspace);
+    if (st != RNS8_SUCCESS) return st;
+    st = validate_rns_operands(*ctx, *plan, *A, *B, *C);
+    if (st != RNS8_SUCCESS) return st;
+    i256 bound;
+    ExactRanges ranges;
+    if (exact_wide(plan->desc.semantics)) {
+      st = exact_gemm_range(*plan, *A, *B, bound, &ranges);
+      if (st != RNS8_SUCCESS) return st;
+    }
+    DeviceScope dev(ctx->device_id);
+    if (!dev.ok) return RNS8_BACKEND_FAILURE;
+    C->device_current = false;
+    rns8cuda::PlaneGemmTask task{A->residues, B->residues, C->residues};
+    const rns8cuda::PlaneGemmProblem prob = rns_problem(*plan, plan->prefix, &task, 1, 0);
+    st = run_plane_gemm(*ctx, prob, workspace);
+    if (st != RNS8_SUCCESS) return st;
+    C->device_current = true;
+    C->source_version = combine_source_versions(A->source_version, B->source_version);
+    if (exact_wide(plan->desc.semantics)) commit_exact_range(*C, *plan, bound, &ranges);
+    return RNS8_SUCCESS;
+  });
+}
+
+extern "C" rns8_status rns8_gemm_rns_grouped(rns8_context* ctx, const rns8_plan* plan,
+                                             const rns8_grouped_gemm_task* tasks, uint32_t task_count) {
+  return guard([&] { return grouped_gemm(ctx, plan, tasks, task_count, false, 0); });
+}
+
+extern "C" rns8_status rns8_gemm_finite_u8(rns8_context* ctx, const rns8_plan* plan, uint16_t modulus,
+                                           const rns8_matrix* A, const rns8_matrix* B, rns8_matrix* C,
+                                           rns8_workspace* workspace) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !A || !B || !C || !workspace) return RNS8_INVALID_ARGUMENT;
+    rns8_status st = validate_workspace(*ctx, *plan, *workspace);
+    if (st != RNS8_SUCCESS) return st;
+    st = validate_finite_operands(*ctx, *plan, modulus, *A, *B, *C);
+    if (st != RNS8_SUCCESS) return st;
+    DeviceScope dev(ctx->device_id);
+    if (!dev.ok) return RNS8_BACKEND_FAILURE;
+    C->device_current = false;
+    rns8cuda::PlaneGemmTask task{A->residues, B->residues, C->residues};
+    const rns8cuda::PlaneGemmProblem prob = rns_problem(*plan, 1, &task, 1, modulus);
+    st = run_plane_gemm(*ctx, prob, workspace);
+    if (st != RNS8_SUCCESS) return st;
+    C->device_current = true;
+    C->finite_modulus = modulus;
+    C->source_version = combine_source_versions(A->source_version, B->source_version);
+    return RNS8_SUCCESS;
+  });
+}
+
+extern "C" rns8_status rns8_gemm_finite_u8_grouped(rns8_context* ctx, const rns8_plan* plan, uint16_t modulus,
+                                                   const rns8_grouped_gemm_task* tasks, uint32_t task_count) {
+  return guard([&] { return grouped_gemm(ctx, plan, tasks, task_count, true, modulus); });
+}
+
+extern "C" rns8_status rns8_export_i64(rns8_context* ctx, const rns8_plan* plan, const rns8_matrix* C, int64_t* dst,
+                                       int64_t ld) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !C || !dst || !valid_matrix_access(plan->desc.m, plan->desc.n, ld))
+      return RNS8_INVALID_ARGUMENT;
+    const rns8_status v = validate_rns_export(*ctx, *plan, *C, RNS8_BOUNDED_I64);
+    if (v != RNS8_SUCCESS) return v;
+    return export_rns(*ctx, *plan, *C, dst, ld, ExportKind::I64, 1);
+  });
+}
+
+extern "C" rns8_status rns8_export_u64(rns8_context* ctx, const rns8_plan* plan, const rns8_matrix* C, uint64_t* dst,
+                                       int64_t ld) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !C || !dst || !valid_matrix_access(plan->desc.m, plan->desc.n, ld))
+      return RNS8_INVALID_ARGUMENT;
+    const rns8_status v = validate_rns_export(*ctx, *plan, *C, RNS8_BOUNDED_U64);
+    if (v != RNS8_SUCCESS) return v;
+    return export_rns(*ctx, *plan, *C, dst, ld, ExportKind::U64, 1);
+  });
+}
+
+extern "C" rns8_status rns8_export_exact_wide_signed_limbs(rns8_context* ctx, const rns8_plan* plan,
+                                                           const rns8_matrix* C, uint64_t* dst, int64_t ld,
+                                                           uint32_t limb_count) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !C || !dst || !valid_limb_export_access(plan->desc.m, plan->desc.n, ld, limb_count))
+      return RNS8_INVALID_ARGUMENT;
+    const rns8_status v = validate_rns_export(*ctx, *plan, *C, RNS8_EXACT_WIDE_SIGNED);
+    if (v != RNS8_SUCCESS) return v;
+    return export_rns(*ctx, *plan, *C, dst, ld, ExportKind::LimbsS, limb_count);
+  });
+}
+
+extern "C" rns8_status rns8_export_exact_wide_unsigned_limbs(rns8_context* ctx, const rns8_plan* plan,
+                                                             const rns8_matrix* C, uint64_t* dst, int64_t ld,
+                                                             uint32_t limb_count) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !C || !dst || !valid_limb_export_access(plan->desc.m, plan->desc.n, ld, limb_count))
+      return RNS8_INVALID_ARGUMENT;
+    const rns8_status v = validate_rns_export(*ctx, *plan, *C, RNS8_EXACT_WIDE_UNSIGNED);
+    if (v != RNS8_SUCCESS) return v;
+    return export_rns(*ctx, *plan, *C, dst, ld, ExportKind::LimbsU, limb_count);
+  });
+}
+
+extern "C" rns8_status rns8_export_finite_u8(rns8_context* ctx, const rns8_plan* plan, uint16_t modulus,
+                                             const rns8_matrix* Cc, uint8_t* dst, int64_t ld) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !Cc || !dst || !valid_matrix_access(plan->desc.m, plan->desc.n, ld))
+      return RNS8_INVALID_ARGUMENT;
+    if (!uses_finite_storage(plan->desc.semantics) ||
+        !valid_finite_modulus_for_semantics(plan->desc.semantics, modulus) || plan->desc.finite_modulus != modulus)
+      return RNS8_INVALID_ARGUMENT;
+    if (!plan_context_ok(*ctx, *plan) || Cc->device_id != ctx->device_id) return RNS8_INVALID_ARGUMENT;
+    if (!descriptor_matches(*Cc, plan->desc.semantics, RNS8_BOUND_NONE, plan->desc.m, plan->desc.n, 0) ||
+        !Cc->device_current || Cc->finite_modulus != modulus)
+      return RNS8_INVALID_ARGUMENT;
+    rns8_matrix& C = const_cast<rns8_matrix&>(*Cc);
+    DeviceScope dev(ctx->device_id);
+    if (!dev.ok) return RNS8_BACKEND_FAILURE;
+    const int64_t m = plan->desc.m, n = plan->desc.n;
+    rns8_status st = C.staging.ensure(ctx->device_id, static_cast<uint64_t>(m) * n);
+    if (st != RNS8_SUCCESS) return st;
+    if (rns8cuda::export_finite_u8(C.residues, m, n, modulus, static_cast<uint8_t*>(C.staging.ptr), n, ctx->stream) !=
+        cudaSuccess)
+      return RNS8_BACKEND_FAILURE;
+    if ((st = copy_out_2d(*ctx, dst, ld, C.staging.ptr, m, n, 1)) != RNS8_SUCCESS) return st;
+    return sync(*ctx);
+  });
+}
+
+extern "C" rns8_status rns8_gemm_i64_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const int64_t* A,
+                                             int64_t lda, const int64_t* B, int64_t ldb, int64_t* C, int64_t ldc) {
+  return guard([&] { return bounded_oneshot<int64_t>(ctx, desc, A, lda, B, ldb, C, ldc); });
+}
+
+extern "C" rns8_status rns8_gemm_u64_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const uint64_t* A,
+                                             int64_t lda, const uint64_t* B, int64_t ldb, uint64_t* C, int64_t ldc) {
+  return guard([&] { return bounded_oneshot<uint64_t>(ctx, desc, A, lda, B, ldb, C, ldc); });
+}
+
+extern "C" rns8_status rns8_gemm_finite_ring_u8_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc,
+                                                        uint16_t modulus, const uint8_t* A, int64_t lda,
+                                                        const uint8_t* B, int64_t ldb, uint8_t* C, int64_t ldc) {
+  return guard([&] { return finite_oneshot(ctx, desc, RNS8_FINITE_RING_U8, modulus, A, lda, B, ldb, C, ldc); });
+}
+
+extern "C" rns8_status rns8_gemm_finite_field_u8_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc,
+                                                         uint16_t modulus, const uint8_t* A, int64_t lda,
+                                                         const uint8_t* B, int64_t ldb, uint8_t* C, int64_t ldc) {
+  return guard([&] { return finite_oneshot(ctx, desc, RNS8_FINITE_FIELD_U8, modulus, A, lda, B, ldb, C, ldc); });
+}

@@ -1,0 +1,158 @@
+// Host-side state behind the rns8 C ABI handles (reference counterpart:
+// src/core/internal.hpp:13-251). Device buffers are plain cudaMalloc
+// allocations owned by the handle that created them.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <exception>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "kernels.hpp"
+#include "ladder.hpp"
+#include "rns8/rns8.h"
+#include "rns8/rns8_cuda.h"
+#include "wide_int.hpp"
+
+namespace rns8host {
+
+using rns8ladder::kLadder;
+
+// One growable device allocation.
+struct DevBuf {
+  void* ptr = nullptr;
+  uint64_t bytes = 0;
+  int device = -1;
+  rns8_status ensure(int dev, uint64_t need);
+  void release();
+  ~DevBuf() { release(); }
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+};
+
+// Exact-wide range proof of one axis (row or column), reference
+// src/core/internal.hpp:74-87. Magnitudes and sums of int64/uint64 values
+// over at most 2^63 elements fit in 128 bits; products fit in 256 bits.
+struct AxisRange {
+  i256 max_magnitude, absolute_sum, sum, minimum, maximum, deviation_sum;
+  bool sum_known = false;
+};
+struct ExactRanges {
+  std::vector<AxisRange> rows, cols;
+};
+
+}  // namespace rns8host
+
+struct rns8_context {
+  rns8_backend_kind backend = RNS8_BACKEND_CUDA_SM100;
+  int device_id = 0;
+  int sm_count = 148;
+  cudaStream_t stream = nullptr;
+  rns8_device_info info{};
+  uint32_t* dev_status = nullptr;  // 4 status words
+  // Device arena reused by the one-shot entry points (serialised by the mutex).
+  std::mutex oneshot_mutex;
+  rns8host::DevBuf oneshot_arena;
+};
+
+struct rns8_plan {
+  rns8_gemm_desc desc{};          // normalised: tile sizes and max_prefix filled in, pointers dropped
+  uint32_t prefix = 0;            // selected prefix (0 for finite / wrap)
+  uint32_t requested_max_prefix = 0;
+  rns8host::i256 modulus_product;
+  rns8_backend_kind backend = RNS8_BACKEND_CUDA_SM100;
+  int device_id = 0;
+  uint64_t tile_rows = 0, tile_cols = 0, tile_count = 0;
+  uint32_t min_required = 0, max_required = 0, min_selected = 0, max_selected = 0;
+  uint32_t group_count = 0, range_bit_length = 0, adaptive_prefix = 0, adaptive_skip = 0, schedule_flags = 0;
+  uint64_t fingerprint = 0;
+};
+
+struct rns8_matrix {
+  rns8_matrix_desc desc{};
+  rns8_backend_kind backend = RNS8_BACKEND_CUDA_SM100;
+  uint64_t id = 0;
+  uint32_t prefix = 0;          // allocated planes (1 for finite storage)
+  uint16_t finite_modulus = 0;  // stamped by finite pack / GEMM
+  uint64_t source_version = 0;
+  int device_id = 0;
+  int8_t* residues = nullptr;   // device, prefix * rows * cols bytes
+  uint64_t residue_bytes = 0;
+  bool device_current = false;
+  rns8host::DevBuf upload;      // native input staging
+  rns8host::DevBuf staging;     // export staging
+  // Exact-wide proof (reference internal.hpp:96-99); zero prefix = unknown.
+  rns8host::i256 exact_max_magnitude;
+  uint32_t exact_range_prefix = 0;
+  rns8host::ExactRanges exact_axes;
+};
+
+struct rns8_workspace {
+  rns8_backend_kind backend = RNS8_BACKEND_CUDA_SM100;
+  int device_id = 0;
+  uint64_t plan_fingerprint = 0;
+  rns8_semantics semantics = RNS8_BOUNDED_I64;
+  int64_t m = 0, n = 0, k = 0;
+  uint32_t prefix = 0;
+  rns8host::DevBuf scratch;  // split-K partial sums
+};
+
+namespace rns8host {
+
+// Runs body, mapping exceptions to RNS8_INTERNAL_ERROR (reference guard_api,
+// src/core/api_internal.hpp:34-42).
+template <typename F>
+rns8_status guard(F&& body) {
+  try {
+    return body();
+  } catch (const std::bad_alloc&) {
+    return RNS8_INTERNAL_ERROR;
+  } catch (...) {
+    return RNS8_INTERNAL_ERROR;
+  }
+}
+
+bool valid_abi(uint64_t struct_size, uint32_t abi_version, size_t expected);
+void set_text(char* dst, size_t cap, const std::string& s);
+rns8_status cuda_status(cudaError_t e);
+
+// Contract arithmetic (reference src/core/moduli.cpp).
+i256 modulus_product(uint32_t prefix);
+uint32_t required_prefix_for_range(const i256& range);
+uint32_t default_prefix_for_semantics(rns8_semantics s);
+bool known_semantics(uint32_t s);
+bool known_bound_kind(uint32_t b);
+bool known_layout(uint32_t l);
+bool valid_tile_size(uint32_t v);
+bool valid_finite_modulus_for_semantics(rns8_semantics s, uint32_t m);
+bool uses_rns_storage(rns8_semantics s);
+bool uses_finite_storage(rns8_semantics s);
+bool exact_wide(rns8_semantics s);
+bool input_range_output_bound(const rns8_gemm_desc& d, uint64_t& out);
+rns8_status validate_bound_contract(rns8_semantics s, rns8_bound_kind bk, uint64_t bound, uint32_t prefix);
+rns8_status validate_gemm_desc(const rns8_gemm_desc& d, uint32_t prefix);
+rns8_status validate_matrix_desc(const rns8_matrix_desc& d, uint32_t prefix);
+rns8_bound_kind storage_bound_kind(const rns8_plan& plan);
+bool valid_matrix_access(int64_t rows, int64_t cols, int64_t ld);
+bool backend_request_ok(rns8_backend_kind requested);
+
+// Plan construction shared by rns8_create_plan and rns8_cuda_plan_probe.
+rns8_status build_plan(const rns8_gemm_desc& desc, rns8_plan& plan);
+
+// Exact-wide proofs (reference src/core/exact_range.hpp).
+template <typename T>
+void native_exact_ranges(const T* src, int64_t rows, int64_t cols, int64_t ld, ExactRanges& out, i256& maximum);
+bool exact_range_fits(rns8_semantics s, const i256& bound, const i256& product);
+rns8_status exact_gemm_range(const rns8_plan& plan, const rns8_matrix& A, const rns8_matrix& B, i256& bound,
+                             ExactRanges* out_ranges);
+void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, ExactRanges* ranges);
+
+uint64_t next_matrix_id();
+uint64_t plan_fingerprint(const rns8_plan& plan);
+
+}  // namespace rns8host

@@ -1,0 +1,26 @@
+// Shared declarations between the plane-GEMM implementations.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "kernels.hpp"
+
+namespace rns8cuda {
+
+struct PlaneModuli {
+  uint16_t m[20];
+};
+
+cudaError_t simt_plane_gemm(const PlaneGemmProblem& prob, cudaStream_t stream);
+
+// Split-K decomposition chosen for the tensor-core kernel.
+struct TcSchedule {
+  uint32_t m_tiles, n_tiles, total_kb, splits, kb_per_split;
+  uint64_t units;
+};
+TcSchedule tc_schedule(const PlaneGemmProblem& prob, int sm_count);
+cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
+                          uint32_t* dev_status, cudaStream_t stream);
+
+}  // namespace rns8cuda

@@ -1,0 +1,448 @@
+// Tensor-core plane GEMM for sm_100a: C_p = (A_p x B_p) mod m_p over every
+// plane p of every task, in one persistent launch.
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      one thread issues TMA loads of A (128 x 128, K-major) and B
+//               (128 x 256, N-major, two 128-column boxes) into a 4-stage
+//               shared-memory ring, completion tracked by mbarriers;
+//   warp 1      one thread issues tcgen05.mma.kind::i8 (M=128, N=256, K=32)
+//               into one of two 256-column int32 accumulators in tensor memory;
+//   warps 2-5   epilogue: tcgen05.ld the accumulator, reduce every int32 to
+//               the centered residue modulo the plane's modulus, store int8.
+// Work unit = (task, plane, K split, 128 x 256 output tile). A unit never
+// spans more than RNS8_SAFE_INT32_K_BLOCK products, so its int32 accumulator
+// is exact (|sum| <= 65536 * 128 * 128 = 2^30). When K is longer, or when the
+// output tiles alone cannot fill the GPU, K is split: each unit adds its
+// centered partial residue into an int32 scratch plane and a finalize pass
+// reduces the sum modulo m (reference: cpu_reference.cpp:171-174 folds each
+// 65536 block into the running residue; the sum of per-block residues is
+// congruent, so the results are identical).
+//
+// Every mbarrier wait is bounded; a wait that runs out sets the device status
+// word and the CTA drains its own in-flight copies and MMAs, frees its tensor
+// memory and exits.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "device_common.cuh"
+#include "gemm_internal.hpp"
+
+namespace rns8cuda {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4, UMMA_K = 32;
+constexpr int GROUP_M = 16;  // raster: 16 M-tiles per column sweep for L2 reuse
+constexpr uint32_t A_BYTES = BM * BK;
+constexpr uint32_t B_HALF_BYTES = BK * 128;
+constexpr uint32_t B_BYTES = BK * BN;
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t ACC_COLS = BN;
+constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+constexpr int THREADS = 192;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+constexpr int kMaxKbPerUnit = static_cast<int>(kSafeKBlock / BK);  // 512
+
+struct __align__(64) TcParams {
+  CUtensorMap tmA[kMaxGroupTasks];
+  CUtensorMap tmB[kMaxGroupTasks];
+  int8_t* C[kMaxGroupTasks];
+  int32_t* scratch;  // split-K partial sums, [task][plane][m][n]
+  int64_t m, n, k;
+  uint32_t planes, tasks;
+  uint32_t m_tiles, n_tiles, total_kb, splits, kb_per_split;
+  uint64_t units;
+  uint32_t* status;
+  uint16_t moduli[20];
+};
+
+struct Unit {
+  uint32_t t, p, mt, nt, kb0, kb1;
+};
+
+__device__ __forceinline__ Unit decode_unit(const TcParams& prm, uint64_t u) {
+  const uint64_t tiles = static_cast<uint64_t>(prm.m_tiles) * prm.n_tiles;
+  const uint64_t tile = u % tiles;
+  const uint64_t rest = u / tiles;
+  const uint32_t s = static_cast<uint32_t>(rest % prm.splits);
+  const uint32_t tp = static_cast<uint32_t>(rest / prm.splits);
+  Unit w;
+  w.t = tp / prm.planes;
+  w.p = tp - w.t * prm.planes;
+  const uint32_t span = GROUP_M * prm.n_tiles;
+  const uint32_t group = static_cast<uint32_t>(tile / span);
+  const uint32_t first_m = group * GROUP_M;
+  const uint32_t gsize = min(prm.m_tiles - first_m, static_cast<uint32_t>(GROUP_M));
+  const uint32_t in_group = static_cast<uint32_t>(tile % span);
+  w.mt = first_m + in_group % gsize;
+  w.nt = in_group / gsize;
+  w.kb0 = s * prm.kb_per_split;
+  w.kb1 = min(prm.total_kb, w.kb0 + prm.kb_per_split);
+  return w;
+}
+
+__device__ __forceinline__ void report_timeout(const TcParams& prm, volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicOr(prm.status, kDevWaitTimeout);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_constant__ TcParams prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (uint32_t t = 0; t < prm.tasks; ++t) {
+      tma_prefetch_desc(&prm.tmA[t]);
+      tma_prefetch_desc(&prm.tmB[t]);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      uint32_t stage = 0, phase = 0;
+      uint32_t pending = 0, pending_parity = 0;
+      bool ok = true;
+      for (uint64_t u = blockIdx.x; ok && u < prm.units; u += gridDim.x) {
+        const Unit w = decode_unit(prm, u);
+        for (uint32_t kb = w.kb0; kb < w.kb1; ++kb) {
+          if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
+            if (!*abort_flag) report_timeout(prm, abort_flag);
+            ok = false;
+            break;
+          }
+          pending &= ~(1u << stage);
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          const int32_t kc = static_cast<int32_t>(kb * BK);
+          tma_load_3d(sa, &prm.tmA[w.t], &full[stage], kc, static_cast<int32_t>(w.mt * BM), static_cast<int32_t>(w.p));
+          tma_load_3d(sb, &prm.tmB[w.t], &full[stage], static_cast<int32_t>(w.nt * BN), kc, static_cast<int32_t>(w.p));
+          tma_load_3d(sb + B_HALF_BYTES, &prm.tmB[w.t], &full[stage], static_cast<int32_t>(w.nt * BN + 128), kc,
+                      static_cast<int32_t>(w.p));
+          pending |= 1u << stage;
+          pending_parity = (pending_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Loads issued but never consumed (abort path) must land before exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (pending & (1u << s)) (void)mbar_wait_bounded(&full[s], (pending_parity >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = make_idesc_i8(BM, BN, /*b_mn_major=*/true);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (uint64_t u = blockIdx.x; ok && u < prm.units; u += gridDim.x) {
+        const Unit w = decode_unit(prm, u);
+        if (*abort_flag || !mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u)) {
+          if (!*abort_flag) report_timeout(prm, abort_flag);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+        for (uint32_t kb = w.kb0; kb < w.kb1; ++kb) {
+          if (*abort_flag || !mbar_wait_bounded(&full[stage], phase)) {
+            if (!*abort_flag) report_timeout(prm, abort_flag);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            // A: K-major rows of 128 B, 8-row swizzle atoms 1 KiB apart.
+            const uint64_t adesc = make_smem_desc_sw128(sa + kk * UMMA_K, 16, 1024);
+            // B: N-major, two 128-column chunks 16 KiB apart, 8 K-rows per 1 KiB atom.
+            const uint64_t bdesc = make_smem_desc_sw128(sb + kk * UMMA_K * 128, B_HALF_BYTES, 1024);
+            tc_mma_i8(d_tmem, adesc, bdesc, idesc, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA this thread issued completes before tensor memory is freed.
+      tc_commit(drain);
+      (void)mbar_wait_bounded(drain, 0);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const uint32_t quarter = static_cast<uint32_t>(warp & 3);  // TMEM lanes this warp may read
+    uint32_t acc = 0, acc_phase = 0;
+    for (uint64_t u = blockIdx.x; u < prm.units; u += gridDim.x) {
+      const Unit w = decode_unit(prm, u);
+      if (*abort_flag || !mbar_wait_bounded(&acc_full[acc], acc_phase)) {
+        if (!*abort_flag) report_timeout(prm, abort_flag);
+        break;
+      }
+      tc_fence_after();
+      const ModConst mc = make_mod_const(prm.moduli[w.p]);
+      const int64_t row = static_cast<int64_t>(w.mt) * BM + quarter * 32 + lane;
+      const bool row_ok = row < prm.m;
+      const int64_t plane_elems = prm.m * prm.n;
+      int8_t* crow = prm.C[w.t] + static_cast<int64_t>(w.p) * plane_elems + row * prm.n;
+      int32_t* srow = prm.scratch
+                          ? prm.scratch + (static_cast<int64_t>(w.t) * prm.planes + w.p) * plane_elems + row * prm.n
+                          : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS + c * 32, v);
+        tmem_wait_ld();
+        const int64_t col = static_cast<int64_t>(w.nt) * BN + c * 32;
+        if (!row_ok || col >= prm.n) continue;
+        if (srow) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col + j < prm.n) atomicAdd(srow + col + j, reduce_i32_centered(static_cast<int32_t>(v[j]), mc));
+        } else {
+          uint32_t packed[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint32_t r0 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 0]), mc)) & 0xFFu;
+            const uint32_t r1 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 1]), mc)) & 0xFFu;
+            const uint32_t r2 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 2]), mc)) & 0xFFu;
+            const uint32_t r3 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 3]), mc)) & 0xFFu;
+            packed[q] = r0 | (r1 << 8) | (r2 << 16) | (r3 << 24);
+          }
+          // n is a multiple of 16, so a 32-column chunk is whole, half, or absent.
+          uint4* dst = reinterpret_cast<uint4*>(crow + col);
+          dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          if (col + 32 <= prm.n) dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// Split-K finalize: C = centered(sum of partial residues mod m).
+__global__ void __launch_bounds__(256) split_finalize_kernel(const int32_t* __restrict__ scratch, int64_t plane_elems,
+                                                             uint32_t planes, PlaneModuli moduli,
+                                                             int8_t* __restrict__ c) {
+  const int64_t total = plane_elems * planes;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t p = static_cast<uint32_t>(i / plane_elems);
+    c[i] = static_cast<int8_t>(reduce_i32_centered(scratch[i], make_mod_const(moduli.m[p])));
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D int8 tensor (inner, outer, plane) with a 128 x 128 box, 128-byte swizzle.
+bool encode_planes(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t planes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {inner, outer, planes};
+  const cuuint64_t strides[2] = {inner, inner * outer};  // bytes, dims 1 and 2
+  const cuuint32_t box[3] = {128, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+TcSchedule tc_schedule(const PlaneGemmProblem& prob, int sm_count) {
+  TcSchedule s{};
+  s.m_tiles = static_cast<uint32_t>((prob.m + BM - 1) / BM);
+  s.n_tiles = static_cast<uint32_t>((prob.n + BN - 1) / BN);
+  s.total_kb = static_cast<uint32_t>((prob.k + BK - 1) / BK);
+  const uint64_t tiles = static_cast<uint64_t>(prob.task_count) * prob.planes * s.m_tiles * s.n_tiles;
+  uint32_t splits = (s.total_kb + kMaxKbPerUnit - 1) / kMaxKbPerUnit;
+  if (tiles * splits < static_cast<uint64_t>(sm_count) && s.total_kb >= 8) {
+    // Too few output tiles to occupy every SM: split K until about one wave,
+    // keeping at least four K blocks per unit.
+    const uint64_t want = (static_cast<uint64_t>(sm_count) + tiles - 1) / tiles;
+    const uint32_t cap = s.total_kb / 4;
+    uint32_t target = static_cast<uint32_t>(want < cap ? want : cap);
+    if (target > splits) splits = target;
+  }
+  s.kb_per_split = (s.total_kb + splits - 1) / splits;
+  s.splits = (s.total_kb + s.kb_per_split - 1) / s.kb_per_split;
+  s.units = tiles * s.splits;
+  return s;
+}
+
+cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
+                          uint32_t* dev_status, cudaStream_t stream) {
+  if (prob.task_count == 0 || prob.task_count > kMaxGroupTasks || prob.planes == 0 || prob.planes > 20)
+    return cudaErrorInvalidValue;
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(tc_plane_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(SMEM_BYTES));
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+
+  const TcSchedule s = tc_schedule(prob, sm_count);
+  const bool split = s.splits > 1;
+  const uint64_t plane_elems = static_cast<uint64_t>(prob.m) * prob.n;
+  const uint64_t need = split ? plane_elems * prob.planes * prob.task_count * sizeof(int32_t) : 0;
+  if (split && (scratch == nullptr || scratch_bytes < need)) return cudaErrorInvalidValue;
+
+  static thread_local TcParams prm;  // 8+ KiB: keep it off the stack
+  std::memset(&prm, 0, sizeof(prm));
+  for (uint32_t t = 0; t < prob.task_count; ++t) {
+    if (!encode_planes(&prm.tmA[t], prob.tasks[t].a, prob.k, prob.m, prob.planes) ||
+        !encode_planes(&prm.tmB[t], prob.tasks[t].b, prob.n, prob.k, prob.planes))
+      return cudaErrorInvalidValue;
+    prm.C[t] = prob.tasks[t].c;
+  }
+  prm.scratch = split ? static_cast<int32_t*>(scratch) : nullptr;
+  prm.m = prob.m;
+  prm.n = prob.n;
+  prm.k = prob.k;
+  prm.planes = prob.planes;
+  prm.tasks = prob.task_count;
+  prm.m_tiles = s.m_tiles;
+  prm.n_tiles = s.n_tiles;
+  prm.total_kb = s.total_kb;
+  prm.splits = s.splits;
+  prm.kb_per_split = s.kb_per_split;
+  prm.units = s.units;
+  prm.status = dev_status;
+  for (uint32_t p = 0; p < prob.planes; ++p) prm.moduli[p] = prob.moduli[p];
+
+  if (split) {
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, need, stream);
+    if (e != cudaSuccess) return e;
+  }
+  const uint64_t grid = s.units < static_cast<uint64_t>(sm_count) ? s.units : static_cast<uint64_t>(sm_count);
+  tc_plane_gemm_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM_BYTES, stream>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !split) return e;
+  PlaneModuli pm{};
+  for (uint32_t p = 0; p < prob.planes; ++p) pm.m[p] = prob.moduli[p];
+  for (uint32_t t = 0; t < prob.task_count; ++t) {
+    int64_t blocks = static_cast<int64_t>((plane_elems * prob.planes + 255) / 256);
+    if (blocks > sm_count * 8) blocks = sm_count * 8;
+    split_finalize_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const int32_t*>(scratch) + static_cast<uint64_t>(t) * prob.planes * plane_elems,
+        static_cast<int64_t>(plane_elems), prob.planes, pm, prob.tasks[t].c);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// ---- dispatch --------------------------------------------------------------
+bool tensor_core_path_supported(const PlaneGemmProblem& prob) {
+  if (prob.m <= 0 || prob.n <= 0 || prob.k <= 0) return false;
+  if (prob.k % 16 != 0 || prob.n % 16 != 0) return false;  // TMA row strides must be 16-byte multiples
+  if (prob.task_count == 0 || prob.planes == 0 || prob.planes > 20) return false;
+  if (prob.m > (int64_t(1) << 31) || prob.n > (int64_t(1) << 31) || prob.k > (int64_t(1) << 31)) return false;
+  for (uint32_t t = 0; t < prob.task_count; ++t) {
+    if (reinterpret_cast<uintptr_t>(prob.tasks[t].a) % 16 || reinterpret_cast<uintptr_t>(prob.tasks[t].b) % 16 ||
+        reinterpret_cast<uintptr_t>(prob.tasks[t].c) % 16)
+      return false;
+  }
+  return encode_fn() != nullptr;
+}
+
+uint64_t plane_gemm_scratch_bytes(const PlaneGemmProblem& prob, int sm_count) {
+  if (!tensor_core_path_supported(prob)) return 0;
+  const uint32_t chunk = prob.task_count < kMaxGroupTasks ? prob.task_count : kMaxGroupTasks;
+  PlaneGemmProblem one = prob;
+  one.task_count = chunk;
+  const TcSchedule s = tc_schedule(one, sm_count);
+  if (s.splits <= 1) return 0;
+  return static_cast<uint64_t>(prob.m) * prob.n * prob.planes * chunk * sizeof(int32_t);
+}
+
+cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count, void* scratch,
+                       uint64_t scratch_bytes, uint32_t* dev_status, cudaStream_t stream, GemmPath* used) {
+  const bool tc_ok = tensor_core_path_supported(prob);
+  if (path == GemmPath::TensorCore && !tc_ok) return cudaErrorInvalidValue;
+  if (path == GemmPath::Simt || !tc_ok) {
+    if (used) *used = GemmPath::Simt;
+    return simt_plane_gemm(prob, stream);
+  }
+  if (used) *used = GemmPath::TensorCore;
+  for (uint32_t t0 = 0; t0 < prob.task_count; t0 += kMaxGroupTasks) {
+    PlaneGemmProblem chunk = prob;
+    chunk.tasks = prob.tasks + t0;
+    chunk.task_count = prob.task_count - t0 < static_cast<uint32_t>(kMaxGroupTasks) ? prob.task_count - t0
+                                                                                   : static_cast<uint32_t>(kMaxGroupTasks);
+    const cudaError_t e = tc_plane_gemm(chunk, sm_count, scratch, scratch_bytes, dev_status, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace rns8cuda

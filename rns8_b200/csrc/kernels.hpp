@@ -1,0 +1,68 @@
+// Internal launch API of the sm_100a kernels. Every function enqueues work on
+// `stream` and returns the launch's cudaError_t; none synchronises. Pointers
+// are device pointers. Residue planes are modulus-major and compact:
+// plane p of an R x C matrix holds int8 centered residues at
+// base[p * R * C + r * C + c].
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rns8cuda {
+
+// Maximum number of same-shape tasks one grouped plane-GEMM launch covers.
+constexpr int kMaxGroupTasks = 32;
+
+// Error codes kernels OR into their device status word.
+constexpr uint32_t kDevOk = 0;
+constexpr uint32_t kDevRangeError = 5;       // == RNS8_RANGE_ERROR
+constexpr uint32_t kDevWaitTimeout = 0x100;  // a bounded device wait ran out
+
+// ---- pack (native -> centered int8 residue planes) ------------------------
+cudaError_t pack_i64(const int64_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t prefix, int8_t* planes,
+                     cudaStream_t stream);
+cudaError_t pack_u64(const uint64_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t prefix, int8_t* planes,
+                     cudaStream_t stream);
+cudaError_t pack_finite_u8(const uint8_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t modulus,
+                           int8_t* residues, cudaStream_t stream);
+
+// ---- plane GEMM -------------------------------------------------------------
+// One GEMM family: tasks[t] x planes[p]; every plane of every task has the
+// same shape. Plane p reduces modulo moduli[p].
+struct PlaneGemmTask {
+  const int8_t* a;  // plane 0 of A (m x k), planes at stride m*k
+  const int8_t* b;  // plane 0 of B (k x n), planes at stride k*n
+  int8_t* c;        // plane 0 of C (m x n), planes at stride m*n
+};
+struct PlaneGemmProblem {
+  int64_t m, n, k;
+  uint32_t planes;
+  uint16_t moduli[20];
+  uint32_t task_count;
+  const PlaneGemmTask* tasks;  // host array of task_count entries
+};
+enum class GemmPath : int { Auto = 0, TensorCore = 1, Simt = 2 };
+
+// Scratch the tensor-core path needs for split-K (int32 per output element
+// of the largest chunk). Returns 0 when the problem runs without split-K.
+uint64_t plane_gemm_scratch_bytes(const PlaneGemmProblem& prob, int sm_count);
+// Runs the plane GEMM. scratch may be null when plane_gemm_scratch_bytes()
+// is 0. dev_status receives kDevWaitTimeout if a bounded wait ran out.
+cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count, void* scratch,
+                       uint64_t scratch_bytes, uint32_t* dev_status, cudaStream_t stream, GemmPath* used = nullptr);
+bool tensor_core_path_supported(const PlaneGemmProblem& prob);
+
+// ---- export (residue planes -> native values) ------------------------------
+// Bounded i64: every cell must reconstruct to a value v with |v| <= bound;
+// otherwise *dev_status is set to kDevRangeError (dst contents unspecified).
+cudaError_t export_i64(const int8_t* planes, int64_t m, int64_t n, uint32_t prefix, uint64_t bound, int64_t* dst,
+                       int64_t ld, uint32_t* dev_status, cudaStream_t stream);
+cudaError_t export_u64(const int8_t* planes, int64_t m, int64_t n, uint32_t prefix, uint64_t bound, uint64_t* dst,
+                       int64_t ld, uint32_t* dev_status, cudaStream_t stream);
+// Exact-wide: limb_count 64-bit limbs per element at dst[(r*ld + c)*limbs + l].
+cudaError_t export_limbs(const int8_t* planes, int64_t m, int64_t n, uint32_t prefix, bool is_signed,
+                         uint32_t limb_count, uint64_t* dst, int64_t ld, uint32_t* dev_status, cudaStream_t stream);
+cudaError_t export_finite_u8(const int8_t* residues, int64_t m, int64_t n, uint32_t modulus, uint8_t* dst, int64_t ld,
+                             cudaStream_t stream);
+
+}  // namespace rns8cuda
