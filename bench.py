@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=64, help="rows of the CPU baseline slab sample")
+    ap.add_argument("--size", type=int, default=8192,
+                    help="M = N = K of the run (8192 is the benchmark; smaller sizes are for ncu captures)")
     return ap.parse_args()
 
 
@@ -211,6 +213,8 @@ def reference_arm(args) -> None:
 # --------------------------------------------------------------------- our arm
 def main():
     args = parse()
+    global M, N, K
+    M = N = K = args.size
     if args.impl == "reference":
         reference_arm(args)
         return
