@@ -60,6 +60,23 @@ RNS8_API rns8_status rns8_cuda_gemm_rns_device(int device_id, const int8_t* d_a,
                                                void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
                                                void* stream);
 
+/* The plane GEMM above for callers that cannot allocate device memory (a
+ * host whose device memory belongs to a fixed-budget allocator, a foreign-
+ * language caller holding only its input and output buffers, or a loop where
+ * cudaMalloc/cudaFree would synchronise the device). It has no counterpart in
+ * the reference. Scratch and the status word come from a file-scope device
+ * array of 8 MiB (+256 B) that every GPU loading the library holds until
+ * exit; the call allocates nothing. Shapes whose split-K sums need more than
+ * 8 MiB (prefix * m * n * 4 bytes when K is split) return
+ * RNS8_WORKSPACE_TOO_SMALL. The first call on a device looks up the array's
+ * device address (make it before any stream capture). All calls share the
+ * array: each clears what must start at zero, and calls that overlap on the
+ * GPU race. The call enqueues on `stream`, then synchronises that stream and
+ * returns RNS8_BACKEND_FAILURE if a bounded device wait ran out. */
+RNS8_API rns8_status rns8_cuda_gemm_rns_device_no_alloc(int device_id, const int8_t* d_a, const int8_t* d_b,
+                                                        int8_t* d_c, int64_t m, int64_t n, int64_t k,
+                                                        uint32_t prefix, void* stream);
+
 /* Same-shape batch of single-plane GEMMs modulo `modulus` (finite u8 ring or
  * field). d_a/d_b/d_c are host arrays of task_count device pointers.
  * Replaces hip_backend.hpp:758 and the grouped finite dispatch. */
