@@ -7,11 +7,15 @@
 // RANGE_ERROR). The device status word replaces the reference's
 // atomicCAS(status, 0, 5) (hip_direct_export_kernels.cuh:137-177).
 //
-// Mixed-radix digits: x = sum_i c_i * M_i with M_i = m_0 * ... * m_{i-1}.
-// Digit i needs x_{<i} mod m_i = sum_{j<i} c_j * (M_j mod m_i); with every
-// factor below 2^8 the sum stays under 2^21 and one mul-hi reduction gives
-// it. c_i = (r_i - that) * (M_i mod m_i)^-1 mod m_i. All tables are
-// compile-time constants of the prefix P, so they fold into immediates.
+// Mixed-radix digits: x = sum_i c_i * M_i with M_i = m_0 * ... * m_{i-1}, so
+//   c_i = (r_i - sum_{j<i} c_j * (M_j mod m_i)) * (M_i mod m_i)^-1  (mod m_i)
+//       = (r_i * inv_i + sum_{j<i} c_j * w'_ij)                      (mod m_i)
+// with w'_ij = -(M_j mod m_i) * inv_i mod m_i. Every digit and weight is a
+// byte, so the sum is a chain of dp4a over digits packed four per word; it
+// stays below 2^21, where q = mulhi(S, ceil(2^32/m)) is the exact quotient,
+// so each digit costs one reduction. x is rebuilt by Horner in 32-bit limbs,
+// each step touching only the limbs the partial product can occupy. All
+// tables are compile-time constants of the prefix P.
 #include "device_common.cuh"
 #include "kernels.hpp"
 
@@ -21,7 +25,6 @@ namespace {
 __host__ __device__ constexpr uint32_t ladder_at(int i) { return kLadder[i]; }
 
 __host__ __device__ constexpr uint32_t inv_mod(uint32_t a, uint32_t m) {
-  // a^-1 mod m by extended Euclid (compile time only).
   int64_t t = 0, nt = 1, r = m, nr = a % m;
   while (nr != 0) {
     const int64_t q = r / nr;
@@ -35,109 +38,124 @@ __host__ __device__ constexpr uint32_t inv_mod(uint32_t a, uint32_t m) {
   return static_cast<uint32_t>(t < 0 ? t + m : t);
 }
 
-struct Limbs3 {
-  uint64_t w[3];
-};
-__host__ __device__ constexpr Limbs3 limbs_mul_small(Limbs3 a, uint32_t m) {
-  Limbs3 r{{0, 0, 0}};
-  uint64_t carry = 0;
-  for (int i = 0; i < 3; ++i) {
-    const uint64_t lo = a.w[i] & 0xFFFFFFFFull, hi = a.w[i] >> 32;
-    const uint64_t plo = lo * m + (carry & 0xFFFFFFFFull);
-    const uint64_t phi = hi * m + (carry >> 32) + (plo >> 32);
-    r.w[i] = (plo & 0xFFFFFFFFull) | (phi << 32);
-    carry = phi >> 32;
-  }
-  return r;
+// ceil(2^32 / m): q = mulhi(S, it) is floor(S / m) exactly for S < 2^32 / m.
+__host__ __device__ constexpr uint32_t ceil_magic(uint32_t m) {
+  return static_cast<uint32_t>(((1ull << 32) + m - 1) / m);
 }
+
+constexpr int kLimbs32 = 5;  // M_20 < 2^155
 
 template <int P>
 struct GarnerTable {
   uint32_t m[P];
   uint32_t magic[P];
-  uint32_t inv[P];    // (M_i mod m_i)^-1 mod m_i
-  uint32_t w[P][P];   // w[i][j] = M_j mod m_i, j < i
-  uint32_t off[P];    // multiple of m_i above any digit sum, keeps differences non-negative
-  Limbs3 product;     // M_P
-  Limbs3 half;        // ceil(M_P / 2)
+  uint32_t inv[P];                   // (M_i mod m_i)^-1 mod m_i
+  uint32_t off[P];                   // multiple of m_i making r_i * inv_i + off_i >= 0
+  uint32_t wpack[P][(P + 3) / 4];    // w'_ij packed four per word (zero for j >= i)
+  uint32_t product[kLimbs32];        // M_P in 32-bit limbs
+  uint32_t half[kLimbs32];           // ceil(M_P / 2)
 };
 
 template <int P>
 __host__ __device__ constexpr GarnerTable<P> make_table() {
   GarnerTable<P> t{};
   for (int i = 0; i < P; ++i) {
-    t.m[i] = ladder_at(i);
-    t.magic[i] = floor_magic(t.m[i]);
-    uint32_t Mi = 1;  // M_i mod m_i, built incrementally
+    const uint32_t mi = ladder_at(i);
+    t.m[i] = mi;
+    t.magic[i] = ceil_magic(mi);
+    uint32_t Mj = 1;  // M_j mod m_i
+    uint32_t w[P] = {};
     for (int j = 0; j < i; ++j) {
-      t.w[i][j] = Mi;
-      Mi = (Mi * ladder_at(j)) % t.m[i];
+      w[j] = Mj;
+      Mj = (Mj * ladder_at(j)) % mi;
     }
-    t.inv[i] = inv_mod(Mi, t.m[i]);
-    t.off[i] = t.m[i] * ((1u << 22) / t.m[i] + 1u);
+    const uint32_t inv = inv_mod(Mj, mi);
+    t.inv[i] = inv;
+    t.off[i] = mi * ((32768u + mi - 1) / mi);
+    for (int g = 0; g < (P + 3) / 4; ++g) t.wpack[i][g] = 0;
+    for (int j = 0; j < i; ++j) {
+      const uint32_t wp = ((mi - w[j]) % mi) * inv % mi;
+      t.wpack[i][j / 4] |= wp << (8 * (j % 4));
+    }
   }
-  Limbs3 prod{{1, 0, 0}};
-  for (int i = 0; i < P; ++i) prod = limbs_mul_small(prod, ladder_at(i));
-  t.product = prod;
-  // half = (M + 1) / 2
-  Limbs3 h = prod;
+  uint64_t prod[kLimbs32] = {1, 0, 0, 0, 0};
+  for (int i = 0; i < P; ++i) {
+    uint64_t carry = 0;
+    for (int l = 0; l < kLimbs32; ++l) {
+      const uint64_t v = prod[l] * ladder_at(i) + carry;
+      prod[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+  }
+  for (int l = 0; l < kLimbs32; ++l) t.product[l] = static_cast<uint32_t>(prod[l]);
+  // half = (M + 1) >> 1
   uint64_t c = 1;
-  for (int i = 0; i < 3; ++i) {
-    const uint64_t s = h.w[i] + c;
-    c = (s < h.w[i]) ? 1 : 0;
-    h.w[i] = s;
+  uint32_t h[kLimbs32] = {};
+  for (int l = 0; l < kLimbs32; ++l) {
+    const uint64_t v = prod[l] + c;
+    h[l] = static_cast<uint32_t>(v);
+    c = v >> 32;
   }
-  for (int i = 0; i < 3; ++i) h.w[i] = (h.w[i] >> 1) | (i < 2 ? (h.w[i + 1] << 63) : 0);
-  t.half = h;
+  for (int l = 0; l < kLimbs32; ++l) t.half[l] = (h[l] >> 1) | (l + 1 < kLimbs32 ? (h[l + 1] << 31) : 0u);
   return t;
 }
 
-// Limb count needed for M_P: 1 for P <= 8 (M_8 < 2^64), 2 for P <= 16, else 3.
+// 32-bit limbs that M_P needs.
 template <int P>
-constexpr int limbs_for() { return P <= 8 ? 1 : (P <= 16 ? 2 : 3); }
+constexpr int limbs32_for() {
+  constexpr GarnerTable<P> T = make_table<P>();
+  int n = kLimbs32;
+  while (n > 1 && T.product[n - 1] == 0) --n;
+  return n;
+}
 
+// Digits of the mixed-radix representation, packed four per word.
 template <int P>
-__device__ __forceinline__ void garner_digits(const int (&r)[P], uint32_t (&c)[P]) {
+__device__ __forceinline__ void garner_digits(const int (&r)[P], uint32_t (&cp)[(P + 3) / 4],
+                                              uint32_t (&c)[P]) {
   constexpr GarnerTable<P> T = make_table<P>();
 #pragma unroll
-  for (int i = 0; i < P; ++i) {
-    const uint32_t mi = T.m[i];
-    const uint32_t ri = static_cast<uint32_t>(r[i] < 0 ? r[i] + static_cast<int>(mi) : r[i]);
-    if (i == 0) {
-      c[0] = ri;
-      continue;
-    }
-    uint32_t s = 0;
+  for (int g = 0; g < (P + 3) / 4; ++g) cp[g] = 0;
+  c[0] = static_cast<uint32_t>(r[0]) & 0xFFu;  // m_0 = 256: the low byte is the canonical residue
+  cp[0] = c[0];
 #pragma unroll
-    for (int j = 0; j < i; ++j) s += c[j] * T.w[i][j];
-    const uint32_t diff = umod_u32(ri + T.off[i] - s, mi, T.magic[i]);
-    c[i] = umod_u32(diff * T.inv[i], mi, T.magic[i]);
+  for (int i = 1; i < P; ++i) {
+    uint32_t s = static_cast<uint32_t>(r[i] * static_cast<int>(T.inv[i]) + static_cast<int>(T.off[i]));
+#pragma unroll
+    for (int g = 0; g < (i + 3) / 4; ++g) s = __dp4a(cp[g], T.wpack[i][g], s);
+    const uint32_t q = __umulhi(s, T.magic[i]);
+    c[i] = s - q * T.m[i];
+    cp[i / 4] |= c[i] << (8 * (i % 4));
   }
 }
 
-// x = sum c_i M_i by Horner from the top digit, L 64-bit limbs.
+// x = sum c_i M_i by Horner from the top digit, 32-bit limbs.
 template <int P, int L>
-__device__ __forceinline__ void horner(const uint32_t (&c)[P], uint64_t (&x)[L]) {
+__device__ __forceinline__ void horner32(const uint32_t (&c)[P], uint32_t (&x)[L]) {
   constexpr GarnerTable<P> T = make_table<P>();
 #pragma unroll
   for (int l = 0; l < L; ++l) x[l] = 0;
   x[0] = c[P - 1];
 #pragma unroll
   for (int i = P - 2; i >= 0; --i) {
+    // Before this step x < 2^(8(P-1-i)); after it x < 2^(8(P-i)).
+    constexpr int dummy = 0;
+    (void)dummy;
+    const int used = (8 * (P - i) + 31) / 32;
     uint64_t carry = c[i];
 #pragma unroll
     for (int l = 0; l < L; ++l) {
-      const uint64_t lo = x[l] * T.m[i];
-      const uint64_t hi = __umul64hi(x[l], static_cast<uint64_t>(T.m[i]));
-      const uint64_t s = lo + carry;
-      carry = hi + (s < lo ? 1 : 0);
-      x[l] = s;
+      if (l < used) {
+        const uint64_t t = static_cast<uint64_t>(x[l]) * T.m[i] + carry;
+        x[l] = static_cast<uint32_t>(t);
+        carry = t >> 32;
+      }
     }
   }
 }
 
 template <int L>
-__device__ __forceinline__ bool geq(const uint64_t (&x)[L], const uint64_t* y) {
+__device__ __forceinline__ bool geq32(const uint32_t (&x)[L], const uint32_t* y) {
 #pragma unroll
   for (int l = L - 1; l >= 0; --l) {
     if (x[l] != y[l]) return x[l] > y[l];
@@ -151,75 +169,82 @@ struct ExportArgs {
   const int8_t* planes;
   int64_t m, n;
   int64_t ld;
-  uint64_t bound;         // I64/U64
-  uint64_t low_limit;     // I64: min(bound, INT64_MAX)
-  uint64_t high_limit[3]; // I64: M_P - bound (cells at or above it are negative values)
-  uint32_t limb_count;    // limb modes
+  uint64_t bound;                 // U64
+  uint64_t low_limit;             // I64: min(bound, INT64_MAX)
+  uint32_t high_limit[kLimbs32];  // I64: M_P - bound, 32-bit limbs
+  uint32_t limb_count;            // limb modes
   void* dst;
   uint32_t* status;
 };
 
+__device__ __forceinline__ int64_t dst_index(const ExportArgs& a, int64_t cell) {
+  if (a.ld == a.n) return cell;
+  const int64_t row = cell / a.n;
+  return row * a.ld + (cell - row * a.n);
+}
+
+// Reconstructs one cell into *out (one int64/uint64) or the limb array.
 template <int P, Mode kMode>
 __device__ __forceinline__ bool export_cell(const ExportArgs& a, int64_t cell, const int (&r)[P]) {
-  constexpr int L = limbs_for<P>();
+  constexpr int L = limbs32_for<P>();
   constexpr GarnerTable<P> T = make_table<P>();
   uint32_t c[P];
-  garner_digits<P>(r, c);
-  uint64_t x[L];
-  horner<P, L>(c, x);
-  const int64_t row = cell / a.n, col = cell - row * a.n;
-  if (kMode == Mode::I64) {
-    bool upper_zero = true;
+  uint32_t cp[(P + 3) / 4];
+  garner_digits<P>(r, cp, c);
+  uint32_t x[L];
+  horner32<P, L>(c, x);
+  const uint64_t lo64 = static_cast<uint64_t>(x[0]) | (L > 1 ? static_cast<uint64_t>(x[L > 1 ? 1 : 0]) << 32 : 0ull);
+  bool upper_zero = true;
 #pragma unroll
-    for (int l = 1; l < L; ++l) upper_zero = upper_zero && x[l] == 0;
+  for (int l = 2; l < L; ++l) upper_zero = upper_zero && x[l] == 0;
+  if (kMode == Mode::I64) {
     int64_t v;
-    if (upper_zero && x[0] <= a.low_limit) {
-      v = static_cast<int64_t>(x[0]);
-    } else if (geq<L>(x, a.high_limit)) {
-      v = static_cast<int64_t>(x[0] - T.product.w[0]);  // x - M_P, exact in 64 bits
+    if (upper_zero && lo64 <= a.low_limit) {
+      v = static_cast<int64_t>(lo64);
+    } else if (geq32<L>(x, a.high_limit)) {
+      const uint64_t m64 = static_cast<uint64_t>(T.product[0]) | (static_cast<uint64_t>(T.product[1]) << 32);
+      v = static_cast<int64_t>(lo64 - m64);  // x - M_P, exact in 64 bits
     } else {
       return false;
     }
-    static_cast<int64_t*>(a.dst)[row * a.ld + col] = v;
+    static_cast<int64_t*>(a.dst)[dst_index(a, cell)] = v;
     return true;
   } else if (kMode == Mode::U64) {
-    bool upper_zero = true;
-#pragma unroll
-    for (int l = 1; l < L; ++l) upper_zero = upper_zero && x[l] == 0;
-    if (!upper_zero || x[0] > a.bound) return false;
-    static_cast<uint64_t*>(a.dst)[row * a.ld + col] = x[0];
+    if (!upper_zero || lo64 > a.bound) return false;
+    static_cast<uint64_t*>(a.dst)[dst_index(a, cell)] = lo64;
     return true;
   } else {
-    // 192-bit two's complement working value.
-    uint64_t v[3] = {0, 0, 0};
+    // 192-bit two's-complement working value in 64-bit limbs.
+    uint32_t w32[6] = {0, 0, 0, 0, 0, 0};
 #pragma unroll
-    for (int l = 0; l < L; ++l) v[l] = x[l];
-    if (kMode == Mode::LimbsSigned && geq<L>(x, T.half.w)) {
+    for (int l = 0; l < L; ++l) w32[l] = x[l];
+    if (kMode == Mode::LimbsSigned && geq32<L>(x, T.half)) {
       uint64_t borrow = 0;
 #pragma unroll
-      for (int l = 0; l < 3; ++l) {
-        const uint64_t sub = T.product.w[l] + borrow;
-        const uint64_t nb = (sub < borrow) || (v[l] < sub) ? 1 : 0;
-        v[l] = v[l] - sub;
-        borrow = nb;
+      for (int l = 0; l < 6; ++l) {
+        const uint64_t sub = static_cast<uint64_t>(l < kLimbs32 ? T.product[l] : 0u) + borrow;
+        const uint64_t cur = w32[l];
+        borrow = cur < sub ? 1 : 0;
+        w32[l] = static_cast<uint32_t>(cur - sub);
       }
     }
+    uint64_t v[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l) v[l] = static_cast<uint64_t>(w32[2 * l]) | (static_cast<uint64_t>(w32[2 * l + 1]) << 32);
     const uint32_t limbs = a.limb_count;
     const uint64_t sign_fill = (kMode == Mode::LimbsSigned && (v[2] >> 63)) ? ~0ull : 0ull;
-    if (limbs < 3) {
-      if (kMode == Mode::LimbsSigned) {
-        // Value must equal the sign extension of its low `limbs` limbs.
-        const uint64_t top = v[limbs - 1];
-        const uint64_t ext = (top >> 63) ? ~0ull : 0ull;
-        for (uint32_t l = limbs; l < 3; ++l)
-          if (v[l] != ext) return false;
-      } else {
-        for (uint32_t l = limbs; l < 3; ++l)
-          if (v[l] != 0) return false;
-      }
+    if (limbs == 1) {
+      const uint64_t ext = (kMode == Mode::LimbsSigned && (v[0] >> 63)) ? ~0ull : 0ull;
+      if (v[1] != ext || v[2] != ext) return false;
+    } else if (limbs == 2) {
+      const uint64_t ext = (kMode == Mode::LimbsSigned && (v[1] >> 63)) ? ~0ull : 0ull;
+      if (v[2] != ext) return false;
     }
-    uint64_t* out = static_cast<uint64_t*>(a.dst) + (row * a.ld + col) * static_cast<int64_t>(limbs);
-    for (uint32_t l = 0; l < limbs; ++l) out[l] = l < 3 ? v[l] : sign_fill;
+    uint64_t* out = static_cast<uint64_t*>(a.dst) + dst_index(a, cell) * static_cast<int64_t>(limbs);
+    out[0] = v[0];
+    if (limbs > 1) out[1] = v[1];
+    if (limbs > 2) out[2] = v[2];
+    for (uint32_t l = 3; l < limbs; ++l) out[l] = sign_fill;
     return true;
   }
 }
@@ -233,15 +258,16 @@ __global__ void __launch_bounds__(256) export_kernel(ExportArgs a) {
   if (kVec4) {
     const int64_t groups = cells >> 2;
     for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += step) {
-      int r[4][P];
+      uint32_t w[P];
 #pragma unroll
-      for (int p = 0; p < P; ++p) {
-        const uint32_t w = __ldcs(reinterpret_cast<const uint32_t*>(a.planes + static_cast<int64_t>(p) * cells) + g);
+      for (int p = 0; p < P; ++p) w[p] = __ldcs(reinterpret_cast<const uint32_t*>(a.planes + static_cast<int64_t>(p) * cells) + g);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) r[e][p] = static_cast<int8_t>((w >> (8 * e)) & 0xFFu);
+      for (int e = 0; e < 4; ++e) {
+        int r[P];
+#pragma unroll
+        for (int p = 0; p < P; ++p) r[p] = static_cast<int>(static_cast<int8_t>(w[p] >> (8 * e)));
+        bad |= !export_cell<P, kMode>(a, 4 * g + e, r);
       }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) bad |= !export_cell<P, kMode>(a, 4 * g + e, r[e]);
     }
   } else {
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < cells; i += step) {
@@ -283,13 +309,18 @@ cudaError_t dispatch_export(const ExportArgs& a, uint32_t prefix, cudaStream_t s
   }
 }
 
-// Host-side M_P as three limbs.
-void host_product(uint32_t prefix, uint64_t out[3]) {
-  Limbs3 p{{1, 0, 0}};
-  for (uint32_t i = 0; i < prefix; ++i) p = limbs_mul_small(p, kLadder[i]);
-  out[0] = p.w[0];
-  out[1] = p.w[1];
-  out[2] = p.w[2];
+// Host-side M_P as 32-bit limbs.
+void host_product32(uint32_t prefix, uint32_t out[kLimbs32]) {
+  uint64_t prod[kLimbs32] = {1, 0, 0, 0, 0};
+  for (uint32_t i = 0; i < prefix; ++i) {
+    uint64_t carry = 0;
+    for (int l = 0; l < kLimbs32; ++l) {
+      const uint64_t v = prod[l] * kLadder[i] + carry;
+      prod[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+  }
+  for (int l = 0; l < kLimbs32; ++l) out[l] = static_cast<uint32_t>(prod[l]);
 }
 
 __global__ void __launch_bounds__(256) export_u8_kernel(const int8_t* __restrict__ res, int64_t m, int64_t n,
@@ -314,16 +345,15 @@ cudaError_t export_i64(const int8_t* planes, int64_t m, int64_t n, uint32_t pref
   a.ld = ld;
   a.bound = bound;
   a.low_limit = bound < 0x7FFFFFFFFFFFFFFFull ? bound : 0x7FFFFFFFFFFFFFFFull;
-  uint64_t prod[3];
-  host_product(prefix, prod);
+  uint32_t prod[kLimbs32];
+  host_product32(prefix, prod);
   // high_limit = M_P - bound (bound < M_P / 2 is guaranteed by plan validation).
+  const uint32_t b[kLimbs32] = {static_cast<uint32_t>(bound), static_cast<uint32_t>(bound >> 32), 0, 0, 0};
   uint64_t borrow = 0;
-  const uint64_t b[3] = {bound, 0, 0};
-  for (int l = 0; l < 3; ++l) {
-    const uint64_t sub = b[l] + borrow;
-    const uint64_t nb = (sub < borrow) || (prod[l] < sub) ? 1 : 0;
-    a.high_limit[l] = prod[l] - sub;
-    borrow = nb;
+  for (int l = 0; l < kLimbs32; ++l) {
+    const uint64_t sub = static_cast<uint64_t>(b[l]) + borrow;
+    borrow = prod[l] < sub ? 1 : 0;
+    a.high_limit[l] = static_cast<uint32_t>(static_cast<uint64_t>(prod[l]) - sub);
   }
   a.dst = dst;
   a.status = dev_status;

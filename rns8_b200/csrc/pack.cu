@@ -2,13 +2,17 @@
 // residue planes (reference behaviour: src/cpu/cpu_reference.cpp:26-130,
 // layout res[p*rows*cols + r*cols + c] from :46-51).
 //
-// Reduction of a 64-bit value u modulo a ladder modulus m (m <= 256):
-// u = d3*2^48 + d2*2^32 + d1*2^16 + d0 with 16-bit digits, so
-// u = d0 + d1*w1 + d2*w2 + d3*w3 (mod m) with w_j = 2^(16j) mod m < 256.
-// The folded sum is below 2^26 and one mul-hi reduction finishes it. A signed
-// value x < 0 is u - 2^64, so its residue adds (-2^64) mod m. The digits are
-// computed once per element and shared by every plane; the per-plane
-// constants fold to immediates because the prefix is a template parameter.
+// Reduction of a 64-bit value modulo a ladder modulus m (m <= 256): with the
+// eight bytes b_j of its two's-complement bits u,
+//   u = sum_j b_j * 2^(8j)  =  sum_j b_j * w_j  (mod m),  w_j = 2^(8j) mod m < 256,
+// which is two dp4a instructions. A negative value x = u - 2^64 adds
+// (-2^64) mod m. Centering is folded in: with h = ceil(m/2),
+//   centered(x mod m) = ((x + m - h) mod m) - (m - h),
+// so the constant m - h joins the dp4a accumulator. The folded sum is below
+// 2^19, where q = mulhi(S, ceil(2^32/m)) is the exact quotient, so each
+// residue costs two dp4a, one mul-hi and two integer ops. The byte split is
+// shared by every plane; per-plane constants are immediates because the
+// prefix is a template parameter.
 #include "device_common.cuh"
 #include "kernels.hpp"
 
@@ -25,41 +29,45 @@ __host__ __device__ __forceinline__ uint32_t ladder_modulus(int i) {
   }
 }
 
-struct Digits {
-  uint32_t d0, d1, d2, d3, neg;
+struct Words {
+  uint32_t lo, hi, neg;
 };
 
 template <typename T>
-__device__ __forceinline__ Digits split_digits(T v) {
+__device__ __forceinline__ Words split_words(T v) {
   const uint64_t u = static_cast<uint64_t>(v);
-  const uint32_t lo = static_cast<uint32_t>(u), hi = static_cast<uint32_t>(u >> 32);
-  Digits d;
-  d.d0 = lo & 0xFFFFu;
-  d.d1 = lo >> 16;
-  d.d2 = hi & 0xFFFFu;
-  d.d3 = hi >> 16;
-  d.neg = (static_cast<T>(-1) < 0) ? (hi >> 31) : 0u;
-  return d;
+  Words w;
+  w.lo = static_cast<uint32_t>(u);
+  w.hi = static_cast<uint32_t>(u >> 32);
+  w.neg = (static_cast<T>(-1) < 0) ? (w.hi >> 31) : 0u;
+  return w;
 }
 
-// Centered residue of the element with digits d modulo ladder entry p.
+// Low byte of the centered residue of the element modulo ladder entry p.
 template <bool kSigned>
-__device__ __forceinline__ int residue_of(const Digits& d, int p) {
+__device__ __forceinline__ uint32_t residue_byte(const Words& w, int p) {
   const uint32_t m = ladder_modulus(p);
-  const uint32_t w1 = static_cast<uint32_t>((1ull << 16) % m);
-  const uint32_t w2 = static_cast<uint32_t>((1ull << 32) % m);
-  const uint32_t w3 = static_cast<uint32_t>((1ull << 48) % m);
-  // (-2^64) mod m, computed without 128-bit arithmetic: 2^64 mod m = (w3 * 2^16) mod m.
-  const uint32_t t64 = static_cast<uint32_t>((static_cast<uint64_t>(w3) << 16) % m);
-  const uint32_t wneg = (m - t64) % m;
-  uint32_t s = d.d0 + d.d1 * w1 + d.d2 * w2 + d.d3 * w3;
-  if (kSigned) s += d.neg * wneg;
-  return center_residue(umod_u32(s, m, floor_magic(m)), m);
+  const uint32_t shift = m - (m + 1) / 2;  // m - ceil(m/2)
+  uint32_t wl = 0, wh = 0;
+  uint64_t pow = 1;  // 2^(8j) mod m
+  for (int j = 0; j < 8; ++j) {
+    if (j < 4)
+      wl |= static_cast<uint32_t>(pow) << (8 * j);
+    else
+      wh |= static_cast<uint32_t>(pow) << (8 * (j - 4));
+    pow = (pow * 256) % m;
+  }
+  const uint32_t wneg = (m - static_cast<uint32_t>(pow)) % m;  // pow == 2^64 mod m here
+  uint32_t s = kSigned ? shift + w.neg * wneg : shift;
+  s = __dp4a(w.hi, wh, s);
+  s = __dp4a(w.lo, wl, s);
+  const uint32_t q = __umulhi(s, static_cast<uint32_t>(((1ull << 32) + m - 1) / m));
+  return s - q * m - shift;  // low byte = centered residue
 }
 
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
-         ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
+// Bytes 0 of a, b, c, d -> one word.
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 // Vector path: each thread converts 8 consecutive elements of one row
@@ -77,24 +85,24 @@ __global__ void __launch_bounds__(256) pack_vec8_kernel(const T* __restrict__ sr
     const int64_t row = g / groups_per_row;
     const int64_t col = (g - row * groups_per_row) << 3;
     const int4* in = reinterpret_cast<const int4*>(src + row * ld + col);
-    Digits d[8];
+    Words d[8];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int4 v = __ldcs(in + q);  // streamed once: do not keep in L1/L2
       const uint64_t e0 = (static_cast<uint64_t>(static_cast<uint32_t>(v.y)) << 32) | static_cast<uint32_t>(v.x);
       const uint64_t e1 = (static_cast<uint64_t>(static_cast<uint32_t>(v.w)) << 32) | static_cast<uint32_t>(v.z);
-      d[2 * q] = split_digits<T>(static_cast<T>(e0));
-      d[2 * q + 1] = split_digits<T>(static_cast<T>(e1));
+      d[2 * q] = split_words<T>(static_cast<T>(e0));
+      d[2 * q + 1] = split_words<T>(static_cast<T>(e1));
     }
     int8_t* out = planes + row * cols + col;
 #pragma unroll
     for (int p = 0; p < P; ++p) {
       uint2 w;
-      w.x = pack4(residue_of<kSigned>(d[0], p), residue_of<kSigned>(d[1], p), residue_of<kSigned>(d[2], p),
-                  residue_of<kSigned>(d[3], p));
-      w.y = pack4(residue_of<kSigned>(d[4], p), residue_of<kSigned>(d[5], p), residue_of<kSigned>(d[6], p),
-                  residue_of<kSigned>(d[7], p));
-      *reinterpret_cast<uint2*>(out + static_cast<int64_t>(p) * plane_elems) = w;
+      w.x = pack4(residue_byte<kSigned>(d[0], p), residue_byte<kSigned>(d[1], p), residue_byte<kSigned>(d[2], p),
+                  residue_byte<kSigned>(d[3], p));
+      w.y = pack4(residue_byte<kSigned>(d[4], p), residue_byte<kSigned>(d[5], p), residue_byte<kSigned>(d[6], p),
+                  residue_byte<kSigned>(d[7], p));
+      __stcs(reinterpret_cast<uint2*>(out + static_cast<int64_t>(p) * plane_elems), w);
     }
   }
 }
@@ -108,9 +116,10 @@ __global__ void __launch_bounds__(256) pack_scalar_kernel(const T* __restrict__ 
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = i / cols, col = i - row * cols;
-    const Digits d = split_digits<T>(src[row * ld + col]);
+    const Words d = split_words<T>(src[row * ld + col]);
 #pragma unroll
-    for (int p = 0; p < P; ++p) planes[static_cast<int64_t>(p) * total + i] = static_cast<int8_t>(residue_of<kSigned>(d, p));
+    for (int p = 0; p < P; ++p)
+      planes[static_cast<int64_t>(p) * total + i] = static_cast<int8_t>(residue_byte<kSigned>(d, p) & 0xFFu);
   }
 }
 
@@ -161,9 +170,10 @@ __global__ void __launch_bounds__(256) pack_u8_vec16_kernel(const uint8_t* __res
     uint32_t* ow = &o.x;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      int r[4];
+      uint32_t r[4];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) r[b] = center_residue(umod_u32((words[w] >> (8 * b)) & 0xFFu, m, magic), m);
+      for (int b = 0; b < 4; ++b)
+        r[b] = static_cast<uint32_t>(center_residue(umod_u32((words[w] >> (8 * b)) & 0xFFu, m, magic), m));
       ow[w] = pack4(r[0], r[1], r[2], r[3]);
     }
     *reinterpret_cast<uint4*>(out + row * cols + col) = o;
