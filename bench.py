@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-rows", type=int, default=64, help="rows of the CPU baseline slab sample")
+    ap.add_argument("--cpu-rows", type=int, default=128, help="rows of the CPU baseline slab sample")
     ap.add_argument("--size", type=int, default=8192,
                     help="M = N = K of the run (8192 is the benchmark; smaller sizes are for ncu captures)")
     return ap.parse_args()
@@ -194,7 +194,7 @@ def reference_arm(args) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    rows = max(8, args.cpu_rows // 2)
+    rows = max(8, args.cpu_rows // 4)
     for _ in range(args.warmup):
         cpu_baseline(rows)
     vals = [cpu_baseline(rows) for _ in range(args.steps)]
