@@ -60,6 +60,22 @@ RNS8_API rns8_status rns8_cuda_gemm_rns_device(int device_id, const int8_t* d_a,
                                                void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
                                                void* stream);
 
+/* Plane GEMM followed by the bounded Garner export, in one call: per plane
+ * p < prefix, C_p = A_p x B_p mod m_p into planes held in d_scratch, then
+ * every cell is reconstructed and written to d_out[row * ld + col] as int64
+ * (is_signed) or uint64, with the bound contract of
+ * rns8_cuda_export_i64_device. d_scratch must hold
+ * rns8_cuda_gemm_export_bounded_scratch_bytes() bytes. This is
+ * hip_backend.hpp:346 followed by :835 for callers that do not keep the
+ * residue planes of C. */
+RNS8_API uint64_t rns8_cuda_gemm_export_bounded_scratch_bytes(int device_id, int64_t m, int64_t n, int64_t k,
+                                                              uint32_t prefix);
+RNS8_API rns8_status rns8_cuda_gemm_export_bounded_device(int device_id, const int8_t* d_a, const int8_t* d_b,
+                                                          int64_t m, int64_t n, int64_t k, uint32_t prefix,
+                                                          uint32_t is_signed, uint64_t bound, void* d_out, int64_t ld,
+                                                          void* d_scratch, uint64_t scratch_bytes,
+                                                          uint32_t* d_status, void* stream);
+
 /* The plane GEMM above for callers that cannot allocate device memory (a
  * host whose device memory belongs to a fixed-budget allocator, a foreign-
  * language caller holding only its input and output buffers, or a loop where

@@ -233,6 +233,9 @@ SIGNATURES = {
     "rns8_cuda_pack_finite_u8_device": (c_status, [C.c_int, vp, i64, i64, i64, u16, vp, vp]),
     "rns8_cuda_gemm_rns_scratch_bytes": (u64, [C.c_int, i64, i64, i64, u32]),
     "rns8_cuda_gemm_rns_device": (c_status, [C.c_int, vp, vp, vp, i64, i64, i64, u32, u32, vp, u64, vp, vp]),
+    "rns8_cuda_gemm_export_bounded_scratch_bytes": (u64, [C.c_int, i64, i64, i64, u32]),
+    "rns8_cuda_gemm_export_bounded_device": (c_status, [C.c_int, vp, vp, i64, i64, i64, u32, u32, u64, vp, i64, vp,
+                                                        u64, vp, vp]),
     "rns8_cuda_gemm_finite_u8_scratch_bytes": (u64, [C.c_int, i64, i64, i64, u32]),
     "rns8_cuda_gemm_finite_u8_grouped_device": (c_status, [C.c_int, vp, vp, vp, u32, i64, i64, i64, u16, u32, vp,
                                                            u64, vp, vp]),

@@ -310,14 +310,13 @@ rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const
   const uint32_t P = plan.prefix;
   const uint64_t a_nat = static_cast<uint64_t>(m) * k * 8, b_nat = static_cast<uint64_t>(k) * n * 8;
   const uint64_t a_res = static_cast<uint64_t>(P) * m * k, b_res = static_cast<uint64_t>(P) * k * n;
-  const uint64_t c_res = static_cast<uint64_t>(P) * m * n, c_nat = static_cast<uint64_t>(m) * n * 8;
-  rns8cuda::PlaneGemmTask task{nullptr, nullptr, nullptr};
-  rns8cuda::PlaneGemmProblem prob = rns_problem(plan, P, &task, 1, 0);
+  const uint64_t c_nat = static_cast<uint64_t>(m) * n * 8;
   // Scratch size depends only on shape and alignment; the arena keeps 256-byte alignment.
-  task = {reinterpret_cast<const int8_t*>(256), reinterpret_cast<const int8_t*>(256), reinterpret_cast<int8_t*>(256)};
-  const uint64_t scratch = rns8cuda::plane_gemm_scratch_bytes(prob, ctx->sm_count);
-  const uint64_t total = round256(a_nat) + round256(b_nat) + round256(a_res) + round256(b_res) + round256(c_res) +
-                         round256(c_nat) + round256(scratch);
+  rns8cuda::PlaneGemmTask task{reinterpret_cast<const int8_t*>(256), reinterpret_cast<const int8_t*>(256), nullptr};
+  rns8cuda::PlaneGemmProblem prob = rns_problem(plan, P, &task, 1, 0);
+  const uint64_t scratch = rns8cuda::gemm_export_bounded_scratch_bytes(prob, ctx->sm_count);
+  const uint64_t total = round256(a_nat) + round256(b_nat) + round256(a_res) + round256(b_res) + round256(c_nat) +
+                         round256(scratch);
   std::unique_lock<std::mutex> lock(ctx->oneshot_mutex, std::try_to_lock);
   DevBuf local;
   DevBuf& arena = lock.owns_lock() ? ctx->oneshot_arena : local;
@@ -328,9 +327,8 @@ rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const
   T* dB = static_cast<T*>(cv.take(b_nat));
   int8_t* rA = static_cast<int8_t*>(cv.take(a_res));
   int8_t* rB = static_cast<int8_t*>(cv.take(b_res));
-  int8_t* rC = static_cast<int8_t*>(cv.take(c_res));
   T* dC = static_cast<T*>(cv.take(c_nat));
-  void* dS = scratch ? cv.take(scratch) : nullptr;
+  void* dS = cv.take(scratch);
   if ((st = copy_in_2d(*ctx, dA, A, m, k, lda, sizeof(T))) != RNS8_SUCCESS) return st;
   if ((st = copy_in_2d(*ctx, dB, B, k, n, ldb, sizeof(T))) != RNS8_SUCCESS) return st;
   cudaError_t e = kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(dA), m, k, k, P, rA, ctx->stream)
@@ -340,13 +338,10 @@ rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const
                 : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(dB), k, n, n, P, rB, ctx->stream);
   if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
   if ((st = clear_status(*ctx)) != RNS8_SUCCESS) return st;
-  task = {rA, rB, rC};
-  e = rns8cuda::plane_gemm(prob, rns8cuda::GemmPath::Auto, ctx->sm_count, dS, scratch, ctx->dev_status, ctx->stream);
-  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
-  e = kSigned ? rns8cuda::export_i64(rC, m, n, P, plan.desc.bound, reinterpret_cast<int64_t*>(dC), n, ctx->dev_status,
-                                     ctx->stream)
-              : rns8cuda::export_u64(rC, m, n, P, plan.desc.bound, reinterpret_cast<uint64_t*>(dC), n, ctx->dev_status,
-                                     ctx->stream);
+  // GEMM and Garner export; fused into the GEMM epilogue when the shape allows.
+  task = {rA, rB, nullptr};
+  e = rns8cuda::gemm_export_bounded(prob, kSigned, plan.desc.bound, dC, n, ctx->sm_count, dS, scratch, ctx->dev_status,
+                                    ctx->stream);
   if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
   uint32_t word = 0;
   if ((st = read_status(*ctx, &word)) != RNS8_SUCCESS) return st;

@@ -92,6 +92,34 @@ extern "C" rns8_status rns8_cuda_gemm_rns_device(int device_id, const int8_t* d_
                                             as_stream(stream)));
 }
 
+extern "C" uint64_t rns8_cuda_gemm_export_bounded_scratch_bytes(int device_id, int64_t m, int64_t n, int64_t k,
+                                                                uint32_t prefix) {
+  if (m <= 0 || n <= 0 || k <= 0 || !valid_prefix(prefix)) return 0;
+  const rns8cuda::PlaneGemmTask task{reinterpret_cast<const int8_t*>(256), reinterpret_cast<const int8_t*>(256),
+                                     reinterpret_cast<int8_t*>(256)};
+  return rns8cuda::gemm_export_bounded_scratch_bytes(seam_problem(m, n, k, prefix, 0, &task, 1),
+                                                     sm_count_of(device_id));
+}
+
+extern "C" rns8_status rns8_cuda_gemm_export_bounded_device(int device_id, const int8_t* d_a, const int8_t* d_b,
+                                                            int64_t m, int64_t n, int64_t k, uint32_t prefix,
+                                                            uint32_t is_signed, uint64_t bound, void* d_out,
+                                                            int64_t ld, void* d_scratch, uint64_t scratch_bytes,
+                                                            uint32_t* d_status, void* stream) {
+  if (!d_a || !d_b || !d_out || !d_status || m <= 0 || n <= 0 || k <= 0 || !valid_prefix(prefix) || ld < n)
+    return RNS8_INVALID_ARGUMENT;
+  const rns8_status c = is_signed ? rns8host::validate_bound_contract(RNS8_BOUNDED_I64, RNS8_BOUND_GLOBAL_MAX_ABS,
+                                                                      bound, prefix)
+                                  : rns8host::validate_bound_contract(RNS8_BOUNDED_U64,
+                                                                      RNS8_BOUND_GLOBAL_MAX_UNSIGNED, bound, prefix);
+  if (c != RNS8_SUCCESS) return c;
+  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  const rns8cuda::PlaneGemmTask task{d_a, d_b, nullptr};
+  const auto prob = seam_problem(m, n, k, prefix, 0, &task, 1);
+  return launch_result(rns8cuda::gemm_export_bounded(prob, is_signed != 0, bound, d_out, ld, sm_count_of(device_id),
+                                                     d_scratch, scratch_bytes, d_status, as_stream(stream)));
+}
+
 extern "C" uint64_t rns8_cuda_gemm_finite_u8_scratch_bytes(int device_id, int64_t m, int64_t n, int64_t k,
                                                            uint32_t task_count) {
   if (m <= 0 || n <= 0 || k <= 0 || task_count == 0) return 0;

@@ -1,0 +1,342 @@
+// Residue-to-integer reconstruction used by the export kernels: the exact
+// mixed-radix (Garner) path, and the fractional CRT for bounded values.
+//
+// x = sum_i c_i * M_i with M_i = m_0 * ... * m_{i-1}, so
+//   c_i = (r_i - sum_{j<i} c_j * (M_j mod m_i)) * (M_i mod m_i)^-1  (mod m_i)
+//       = (r_i * inv_i + sum_{j<i} c_j * w'_ij)                      (mod m_i)
+// with w'_ij = -(M_j mod m_i) * inv_i mod m_i. Every digit and weight is a
+// byte, so the sum is a chain of dp4a over digits packed four per word; it
+// stays below 2^21, where q = mulhi(S, ceil(2^32/m)) is the exact quotient,
+// so each digit costs one reduction. x is rebuilt by Horner in 32-bit limbs,
+// each step touching only the limbs the partial product can occupy. All
+// tables are compile-time constants of the prefix P. Reference order:
+// src/reconstruct/crt.cpp:54-76 (the digits of a mixed-radix representation
+// are unique, so any digit recurrence yields the same x).
+#pragma once
+
+#include "device_common.cuh"
+
+namespace rns8cuda {
+namespace garner {
+
+__host__ __device__ constexpr uint32_t ladder_at(int i) { return kLadder[i]; }
+
+__host__ __device__ constexpr uint32_t inv_mod(uint32_t a, uint32_t m) {
+  int64_t t = 0, nt = 1, r = m, nr = a % m;
+  while (nr != 0) {
+    const int64_t q = r / nr;
+    const int64_t tt = t - q * nt;
+    t = nt;
+    nt = tt;
+    const int64_t rr = r - q * nr;
+    r = nr;
+    nr = rr;
+  }
+  return static_cast<uint32_t>(t < 0 ? t + m : t);
+}
+
+// ceil(2^32 / m): q = mulhi(S, it) is floor(S / m) exactly for S < 2^32 / m.
+__host__ __device__ constexpr uint32_t ceil_magic(uint32_t m) {
+  return static_cast<uint32_t>(((1ull << 32) + m - 1) / m);
+}
+
+constexpr int kLimbs32 = 5;  // M_20 < 2^155
+
+template <int P>
+struct GarnerTable {
+  uint32_t m[P];
+  uint32_t magic[P];
+  uint32_t inv[P];                   // (M_i mod m_i)^-1 mod m_i
+  uint32_t off[P];                   // multiple of m_i making r_i * inv_i + off_i >= 0
+  uint32_t wpack[P][(P + 3) / 4];    // w'_ij packed four per word (zero for j >= i)
+  uint32_t product[kLimbs32];        // M_P in 32-bit limbs
+  uint32_t half[kLimbs32];           // ceil(M_P / 2)
+};
+
+template <int P>
+__host__ __device__ constexpr GarnerTable<P> make_table() {
+  GarnerTable<P> t{};
+  for (int i = 0; i < P; ++i) {
+    const uint32_t mi = ladder_at(i);
+    t.m[i] = mi;
+    t.magic[i] = ceil_magic(mi);
+    uint32_t Mj = 1;  // M_j mod m_i
+    uint32_t w[P] = {};
+    for (int j = 0; j < i; ++j) {
+      w[j] = Mj;
+      Mj = (Mj * ladder_at(j)) % mi;
+    }
+    const uint32_t inv = inv_mod(Mj, mi);
+    t.inv[i] = inv;
+    t.off[i] = mi * ((32768u + mi - 1) / mi);
+    for (int g = 0; g < (P + 3) / 4; ++g) t.wpack[i][g] = 0;
+    for (int j = 0; j < i; ++j) {
+      const uint32_t wp = ((mi - w[j]) % mi) * inv % mi;
+      t.wpack[i][j / 4] |= wp << (8 * (j % 4));
+    }
+  }
+  uint64_t prod[kLimbs32] = {1, 0, 0, 0, 0};
+  for (int i = 0; i < P; ++i) {
+    uint64_t carry = 0;
+    for (int l = 0; l < kLimbs32; ++l) {
+      const uint64_t v = prod[l] * ladder_at(i) + carry;
+      prod[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+  }
+  for (int l = 0; l < kLimbs32; ++l) t.product[l] = static_cast<uint32_t>(prod[l]);
+  // half = (M + 1) >> 1
+  uint64_t c = 1;
+  uint32_t h[kLimbs32] = {};
+  for (int l = 0; l < kLimbs32; ++l) {
+    const uint64_t v = prod[l] + c;
+    h[l] = static_cast<uint32_t>(v);
+    c = v >> 32;
+  }
+  for (int l = 0; l < kLimbs32; ++l) t.half[l] = (h[l] >> 1) | (l + 1 < kLimbs32 ? (h[l + 1] << 31) : 0u);
+  return t;
+}
+
+// 32-bit limbs that M_P needs.
+template <int P>
+constexpr int limbs32_for() {
+  constexpr GarnerTable<P> T = make_table<P>();
+  int n = kLimbs32;
+  while (n > 1 && T.product[n - 1] == 0) --n;
+  return n;
+}
+
+// Digits of the mixed-radix representation, packed four per word.
+template <int P>
+__device__ __forceinline__ void garner_digits(const int (&r)[P], uint32_t (&cp)[(P + 3) / 4],
+                                              uint32_t (&c)[P]) {
+  constexpr GarnerTable<P> T = make_table<P>();
+#pragma unroll
+  for (int g = 0; g < (P + 3) / 4; ++g) cp[g] = 0;
+  c[0] = static_cast<uint32_t>(r[0]) & 0xFFu;  // m_0 = 256: the low byte is the canonical residue
+  cp[0] = c[0];
+#pragma unroll
+  for (int i = 1; i < P; ++i) {
+    uint32_t s = static_cast<uint32_t>(r[i] * static_cast<int>(T.inv[i]) + static_cast<int>(T.off[i]));
+#pragma unroll
+    for (int g = 0; g < (i + 3) / 4; ++g) s = __dp4a(cp[g], T.wpack[i][g], s);
+    const uint32_t q = __umulhi(s, T.magic[i]);
+    c[i] = s - q * T.m[i];
+    cp[i / 4] |= c[i] << (8 * (i % 4));
+  }
+}
+
+// x = sum c_i M_i by Horner from the top digit, 32-bit limbs.
+template <int P, int L>
+__device__ __forceinline__ void horner32(const uint32_t (&c)[P], uint32_t (&x)[L]) {
+  constexpr GarnerTable<P> T = make_table<P>();
+#pragma unroll
+  for (int l = 0; l < L; ++l) x[l] = 0;
+  x[0] = c[P - 1];
+#pragma unroll
+  for (int i = P - 2; i >= 0; --i) {
+    // Before this step x < 2^(8(P-1-i)); after it x < 2^(8(P-i)).
+    const int used = (8 * (P - i) + 31) / 32;
+    uint64_t carry = c[i];
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+      if (l < used) {
+        const uint64_t t = static_cast<uint64_t>(x[l]) * T.m[i] + carry;
+        x[l] = static_cast<uint32_t>(t);
+        carry = t >> 32;
+      }
+    }
+  }
+}
+
+template <int L>
+__device__ __forceinline__ bool geq32(const uint32_t (&x)[L], const uint32_t* y) {
+#pragma unroll
+  for (int l = L - 1; l >= 0; --l) {
+    if (x[l] != y[l]) return x[l] > y[l];
+  }
+  return true;
+}
+
+
+// Bounded int64 / uint64 decision on the reconstructed value (crt.cpp:78-121):
+// signed: x <= low_limit -> x; x >= M_P - bound -> x - M_P; otherwise a range
+// error. Plans guarantee M_P > 2 * bound, which makes this identical to
+// centering at ceil(M_P/2) followed by the |v| <= bound check.
+struct BoundedLimits {
+  uint64_t bound;                 // unsigned: x <= bound
+  uint64_t low_limit;             // signed: min(bound, INT64_MAX)
+  uint32_t high_limit[kLimbs32];  // signed: M_P - bound
+};
+
+template <int P, bool kSigned>
+__device__ __forceinline__ bool reconstruct_bounded(const int (&r)[P], const BoundedLimits& lim, uint64_t* out) {
+  constexpr int L = limbs32_for<P>();
+  constexpr GarnerTable<P> T = make_table<P>();
+  uint32_t c[P];
+  uint32_t cp[(P + 3) / 4];
+  garner_digits<P>(r, cp, c);
+  uint32_t x[L];
+  horner32<P, L>(c, x);
+  const uint64_t lo64 = static_cast<uint64_t>(x[0]) | (L > 1 ? static_cast<uint64_t>(x[L > 1 ? 1 : 0]) << 32 : 0ull);
+  bool upper_zero = true;
+#pragma unroll
+  for (int l = 2; l < L; ++l) upper_zero = upper_zero && x[l] == 0;
+  if (kSigned) {
+    if (upper_zero && lo64 <= lim.low_limit) {
+      *out = lo64;
+      return true;
+    }
+    if (geq32<L>(x, lim.high_limit)) {
+      const uint64_t m64 = static_cast<uint64_t>(T.product[0]) | (static_cast<uint64_t>(T.product[1]) << 32);
+      *out = lo64 - m64;  // x - M_P, exact in 64 bits
+      return true;
+    }
+    return false;
+  }
+  if (!upper_zero || lo64 > lim.bound) return false;
+  *out = lo64;
+  return true;
+}
+
+// ---- fractional CRT for bounded values ---------------------------------------
+// With E_i = M/m_i and inv_i = E_i^-1 mod m_i, every residue vector r
+// satisfies sum_i r_i * E_i * inv_i = x + q*M for the value x it represents,
+// and sum_i r_i * inv_i / m_i = x/M + q. When |x| is small against M (a
+// bounded export), the fraction x/M is close to 0, so q is the nearest
+// integer to that sum, which a fixed-point accumulation with 2^-31 resolution
+// gives, and x = sum_i r_i * (E_i * inv_i) - q*M is then exact modulo 2^64.
+// (Approximate-quotient CRT of Shenoy and Kumaresan; the same reconstruction
+// is used by the Ozaki-II integer emulation of floating-point GEMM.) Cells
+// whose fraction lies within the rounding error of the bound's edge are left
+// to the exact Garner path.
+template <int P>
+struct FracTable {
+  uint32_t F[P];     // round(2^31 * inv_i / m_i)
+  uint64_t G[P];     // (E_i * inv_i) mod 2^64
+  uint64_t C0;       // 128 * sum G_i mod 2^64: residues enter as u_i = r_i + 128
+  int64_t sumF128;   // 128 * sum F_i
+  uint64_t M64;      // M mod 2^64
+};
+
+template <int P>
+__host__ __device__ constexpr FracTable<P> make_frac_table() {
+  FracTable<P> t{};
+  uint64_t m64 = 1;
+  for (int i = 0; i < P; ++i) m64 *= ladder_at(i);
+  t.M64 = m64;
+  uint64_t c0 = 0;
+  int64_t sf = 0;
+  for (int i = 0; i < P; ++i) {
+    const uint32_t mi = ladder_at(i);
+    uint64_t e64 = 1;      // E_i mod 2^64
+    uint32_t emod = 1;     // E_i mod m_i
+    for (int j = 0; j < P; ++j) {
+      if (j == i) continue;
+      e64 *= ladder_at(j);
+      emod = (emod * ladder_at(j)) % mi;
+    }
+    const uint32_t inv = inv_mod(emod, mi);
+    t.F[i] = static_cast<uint32_t>(((static_cast<uint64_t>(inv) << 31) + mi / 2) / mi);
+    t.G[i] = e64 * inv;
+    c0 += 128ull * t.G[i];
+    sf += 128ll * t.F[i];
+  }
+  t.C0 = c0;
+  t.sumF128 = sf;
+  return t;
+}
+
+// Per-call thresholds in units of 2^-31 of M. Accepting |frac| <= t_in
+// implies the quotient is right and the value is in range; |frac| >= t_out
+// implies it is out of range; the band between goes to the exact path. A
+// wrong quotient needs |frac| >= 2^30 - err, which exceeds t_in because the
+// bound is below M/2 (signed) or M (unsigned).
+struct FracLimits {
+  int enabled;      // 0: use the exact path for every cell
+  int64_t offset;   // 128 * sum F_i + center of the accepted interval
+  int64_t t_in;     // |fraction| <= t_in: in range
+  int64_t t_out;    // |fraction| >= t_out: out of range
+};
+
+// 1 = value written to *out, 0 = out of range, -1 = undecided (use exact path).
+template <int P>
+__device__ __forceinline__ int frac_reconstruct(const uint32_t (&u)[P], const FracLimits& fl, uint64_t* out) {
+  constexpr FracTable<P> T = make_frac_table<P>();
+  int64_t s = -fl.offset;
+  uint64_t v = 0ull - T.C0;
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    s += static_cast<int64_t>(static_cast<uint64_t>(u[i]) * T.F[i]);
+    v += static_cast<uint64_t>(u[i]) * T.G[i];
+  }
+  const int64_t q = (s + (1ll << 30)) >> 31;
+  const int64_t frac = s - q * (1ll << 31);
+  const int64_t afrac = frac < 0 ? -frac : frac;
+  if (afrac >= fl.t_out) return 0;
+  if (afrac > fl.t_in) return -1;
+  v -= static_cast<uint64_t>(q) * T.M64;
+  *out = v;
+  return 1;
+}
+
+// Host: M_P as 32-bit limbs, and the limits for a bounded export.
+inline void host_product32(uint32_t prefix, uint32_t out[kLimbs32]) {
+  uint64_t prod[kLimbs32] = {1, 0, 0, 0, 0};
+  for (uint32_t i = 0; i < prefix; ++i) {
+    uint64_t carry = 0;
+    for (int l = 0; l < kLimbs32; ++l) {
+      const uint64_t v = prod[l] * kLadder[i] + carry;
+      prod[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+  }
+  for (int l = 0; l < kLimbs32; ++l) out[l] = static_cast<uint32_t>(prod[l]);
+}
+
+// Thresholds of the fractional path for prefix P and bound. The accepted
+// interval is [-bound, bound] (signed) or [0, bound] (unsigned), i.e. a
+// half-width W = bound/M (or bound/2M) around center 0 (or bound/2M). The
+// fixed-point sum errs by at most 64*P + 1 units (F_i rounding with |r_i| <=
+// 128, plus the rounded center); the path is enabled only when the undecided
+// band is small against W.
+inline FracLimits host_frac_limits(uint32_t prefix, uint64_t bound, bool is_signed, int64_t sum_f128) {
+  FracLimits fl{};
+  uint32_t prod[kLimbs32];
+  host_product32(prefix, prod);
+  if (prod[4] != 0 || (prod[3] >> 31) != 0) return fl;  // M >= 2^127: fraction too fine for 2^-31 units
+  unsigned __int128 M = 0;
+  for (int l = 3; l >= 0; --l) M = (M << 32) | prod[l];
+  const unsigned __int128 num = static_cast<unsigned __int128>(bound) << 31;
+  const unsigned __int128 den = is_signed ? M : 2 * M;
+  const int64_t w = static_cast<int64_t>(num / den);
+  const int64_t center = is_signed ? 0 : static_cast<int64_t>((num + M) / (2 * M));  // round(2^31 * bound / 2M)
+  const int64_t err = 64 * static_cast<int64_t>(prefix) + 2;
+  fl.offset = sum_f128 + center;
+  fl.t_in = w - err - 1;
+  fl.t_out = w + err + 1;
+  fl.enabled = fl.t_in > 4 * err ? 1 : 0;
+  // A signed bound of 2^63 admits -2^63 but not +2^63, an asymmetry the
+  // fraction does not see: such calls take the exact path.
+  if (is_signed && bound > 0x7FFFFFFFFFFFFFFFull) fl.enabled = 0;
+  return fl;
+}
+
+inline BoundedLimits host_limits(uint32_t prefix, uint64_t bound) {
+  BoundedLimits lim{};
+  lim.bound = bound;
+  lim.low_limit = bound < 0x7FFFFFFFFFFFFFFFull ? bound : 0x7FFFFFFFFFFFFFFFull;
+  uint32_t prod[kLimbs32];
+  host_product32(prefix, prod);
+  const uint32_t b[kLimbs32] = {static_cast<uint32_t>(bound), static_cast<uint32_t>(bound >> 32), 0, 0, 0};
+  uint64_t borrow = 0;
+  for (int l = 0; l < kLimbs32; ++l) {
+    const uint64_t sub = static_cast<uint64_t>(b[l]) + borrow;
+    borrow = prod[l] < sub ? 1 : 0;
+    lim.high_limit[l] = static_cast<uint32_t>(static_cast<uint64_t>(prod[l]) - sub);
+  }
+  return lim;
+}
+
+}  // namespace garner
+}  // namespace rns8cuda

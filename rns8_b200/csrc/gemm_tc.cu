@@ -445,4 +445,32 @@ cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count
   return cudaSuccess;
 }
 
+// ---- GEMM followed by the bounded export --------------------------------------
+// Scratch: C planes (planes * m * n bytes, 256-byte aligned), then the split-K
+// sums of plane_gemm.
+uint64_t gemm_export_bounded_scratch_bytes(const PlaneGemmProblem& prob, int sm_count) {
+  const uint64_t planes = (static_cast<uint64_t>(prob.planes) * prob.m * prob.n + 255) & ~uint64_t(255);
+  return planes + plane_gemm_scratch_bytes(prob, sm_count);
+}
+
+cudaError_t gemm_export_bounded(const PlaneGemmProblem& prob, bool is_signed, uint64_t bound, void* out, int64_t ld,
+                                int sm_count, void* scratch, uint64_t scratch_bytes, uint32_t* dev_status,
+                                cudaStream_t stream) {
+  if (prob.task_count != 1) return cudaErrorInvalidValue;
+  const uint64_t need = gemm_export_bounded_scratch_bytes(prob, sm_count);
+  if (!scratch || scratch_bytes < need) return cudaErrorInvalidValue;
+  const uint64_t planes = (static_cast<uint64_t>(prob.planes) * prob.m * prob.n + 255) & ~uint64_t(255);
+  int8_t* c = static_cast<int8_t*>(scratch);
+  PlaneGemmTask task = prob.tasks[0];
+  task.c = c;
+  PlaneGemmProblem p2 = prob;
+  p2.tasks = &task;
+  const cudaError_t e = plane_gemm(p2, GemmPath::Auto, sm_count, static_cast<uint8_t*>(scratch) + planes,
+                                   scratch_bytes - planes, dev_status, stream);
+  if (e != cudaSuccess) return e;
+  return is_signed ? export_i64(c, prob.m, prob.n, prob.planes, bound, static_cast<int64_t*>(out), ld, dev_status, stream)
+                   : export_u64(c, prob.m, prob.n, prob.planes, bound, static_cast<uint64_t*>(out), ld, dev_status,
+                                stream);
+}
+
 }  // namespace rns8cuda

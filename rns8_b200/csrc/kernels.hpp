@@ -52,6 +52,13 @@ cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count
                        uint64_t scratch_bytes, uint32_t* dev_status, cudaStream_t stream, GemmPath* used = nullptr);
 bool tensor_core_path_supported(const PlaneGemmProblem& prob);
 
+// Plane GEMM into scratch planes followed by export_i64/u64 (one task).
+// scratch must hold gemm_export_bounded_scratch_bytes().
+uint64_t gemm_export_bounded_scratch_bytes(const PlaneGemmProblem& prob, int sm_count);
+cudaError_t gemm_export_bounded(const PlaneGemmProblem& prob, bool is_signed, uint64_t bound, void* out, int64_t ld,
+                                int sm_count, void* scratch, uint64_t scratch_bytes, uint32_t* dev_status,
+                                cudaStream_t stream);
+
 // ---- export (residue planes -> native values) ------------------------------
 // Bounded i64: every cell must reconstruct to a value v with |v| <= bound;
 // otherwise *dev_status is set to kDevRangeError (dst contents unspecified).

@@ -170,6 +170,50 @@ def test_finite_grouped_gemm_matches_oracle(lib, oracle):
         np.testing.assert_array_equal(got[t], oracle.ring_gemm(a[t], b[t], mod))
 
 
+# ---- GEMM + export in one call --------------------------------------------------------
+def run_gemm_export(lib, a, b, prefix, bound, signed=True, ld=None):
+    _, m, k = a.shape
+    n = b.shape[2]
+    ld = ld or n
+    d_a, d_b = dev(a), dev(b)
+    out = torch.full((m, ld), -7, dtype=torch.int64, device="cuda")
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    sb = lib.rns8_cuda_gemm_export_bounded_scratch_bytes(0, m, n, k, prefix)
+    scratch = torch.empty(max(sb, 1), dtype=torch.uint8, device="cuda")
+    st = lib.rns8_cuda_gemm_export_bounded_device(0, d_a.data_ptr(), d_b.data_ptr(), m, n, k, prefix, int(signed),
+                                                  bound, out.data_ptr(), ld, scratch.data_ptr(), sb, status.data_ptr(),
+                                                  stream())
+    torch.cuda.synchronize()
+    return st, host(out, None if signed else np.uint64), int(status[0].item())
+
+
+@pytest.mark.parametrize("m,n,k,prefix,signed", [
+    (2048, 4096, 64, 9, True),
+    (1920, 4352, 48, 5, False),    # ragged M, unsigned
+    (512, 512, 64, 9, True),
+])
+def test_gemm_export_bounded_matches_oracle(lib, oracle, m, n, k, prefix, signed):
+    rng = np.random.default_rng(m + n + k)
+    lim = 2**12 if prefix == 5 else 2**26
+    if signed:
+        A = rng.integers(-lim, lim, (m, k), dtype=np.int64, endpoint=True)
+        B = rng.integers(-lim, lim, (k, n), dtype=np.int64, endpoint=True)
+    else:
+        A = rng.integers(0, lim, (m, k), dtype=np.uint64, endpoint=True)
+        B = rng.integers(0, lim, (k, n), dtype=np.uint64, endpoint=True)
+    bound = k * lim * lim
+    a, b = oracle.pack(A, prefix), oracle.pack(B, prefix)
+    planes = oracle.gemm_rns(a, b, prefix)
+    ost, want = oracle.export_i64(planes, prefix, bound) if signed else oracle.export_u64(planes, prefix, bound)
+    assert ost == OK
+    st, got, word = run_gemm_export(lib, a, b, prefix, bound, signed)
+    assert st == OK and word == 0
+    np.testing.assert_array_equal(got, want)
+    # A bound the values exceed: RANGE_ERROR through the status word.
+    st, _, word = run_gemm_export(lib, a, b, prefix, 1, signed)
+    assert st == OK and word == RANGE
+
+
 # ---- export -------------------------------------------------------------------------
 def product_planes(oracle, rng, m, n, k, prefix, lo, hi, dtype=np.int64):
     A = rng.integers(lo, hi, (m, k), dtype=dtype, endpoint=True)
@@ -229,6 +273,70 @@ def test_export_i64_boundaries(lib, oracle):
         assert (RANGE if int(status[0].item()) else OK) == ost
         if ost == OK:
             np.testing.assert_array_equal(host(d_out), owant)
+
+
+def planes_of(values, prefix):
+    """Centered residue planes (prefix, 1, len) of Python integers."""
+    out = np.empty((prefix, 1, len(values)), dtype=np.int8)
+    for p, m in enumerate(LADDER[:prefix]):
+        for j, v in enumerate(values):
+            r = v % m
+            out[p, 0, j] = r - m if r >= (m + 1) // 2 else r
+    return out
+
+
+def modulus_product(prefix):
+    out = 1
+    for m in LADDER[:prefix]:
+        out *= m
+    return out
+
+
+@pytest.mark.parametrize("prefix", [3, 5, 8, 9, 12, 18, 20])
+@pytest.mark.parametrize("signed", [True, False])
+def test_export_bounded_decision_edges(lib, oracle, prefix, signed):
+    """Bounded export at the edges of the accepted interval, for bounds near
+    the plan limit and far below it: every cell within a few thousand of +-bound
+    (the fixed-point quotient's undecided band), random cells, and out-of-range
+    cells anywhere in [0, M). Each call must match the oracle bit for bit."""
+    rng = np.random.default_rng(prefix * 2 + signed)
+    M = modulus_product(prefix)
+    top = min((M - 1) // 2, 2**63) if signed else min(M - 1, 2**64 - 1)
+    for bound in sorted({top, top // 3 + 1, max(top >> 20, 1), 1000}):
+        lo = -bound if signed else 0
+        hi = min(bound, 2**63 - 1) if signed else bound  # +2^63 does not fit int64
+        edge = [x for c in ([lo, bound] if signed else [bound]) for x in range(c - 3000, c + 3001, 3)]
+        inside = [x for x in edge if lo <= x <= hi]
+        inside += [int(v) for v in rng.integers(0, 2**62, 2048)]
+        inside = [lo + (x - lo) % (hi - lo + 1) for x in inside]
+        inside = inside[: len(inside) // 4 * 4]
+        outside = sorted((x for x in edge if not lo <= x <= hi), key=lambda x: min(abs(x - lo), abs(x - hi)))[:6]
+        outside += [int(rng.integers(0, 2**62)) * M // 2**62 for _ in range(4)]
+        base = planes_of(inside, prefix)
+        cases = [(base, True)]
+        for x in outside:
+            xm = x % M
+            if signed and (xm <= hi or xm >= M - bound):
+                continue
+            if not signed and xm <= bound:
+                continue
+            bad = base.copy()
+            bad[:, :, -1:] = planes_of([x], prefix)
+            cases.append((bad, False))
+        for planes, ok in cases:
+            values = inside
+            ost, owant = (oracle.export_i64 if signed else oracle.export_u64)(planes, prefix, bound)
+            assert (ost == OK) == ok
+            d_p = dev(planes)
+            d_out = torch.zeros((1, len(values)), dtype=torch.int64, device="cuda")
+            status = torch.zeros(4, dtype=torch.int32, device="cuda")
+            fn = lib.rns8_cuda_export_i64_device if signed else lib.rns8_cuda_export_u64_device
+            assert fn(0, d_p.data_ptr(), 1, len(values), prefix, bound, d_out.data_ptr(), len(values),
+                      status.data_ptr(), stream()) == OK
+            torch.cuda.synchronize()
+            assert (RANGE if int(status[0].item()) else OK) == ost, (prefix, signed, bound)
+            if ok:
+                np.testing.assert_array_equal(host(d_out, None if signed else np.uint64), owant)
 
 
 @pytest.mark.parametrize("prefix", [1, 9, 18, 20])
@@ -462,8 +570,8 @@ def exact_i64_matmul_fp64(A, B):
     return hh * (sh * sh) + hl * sh + ll
 
 
-@pytest.mark.parametrize("n,forced", [(2048, False), (8192, True)])
-def test_full_size_bounded_i64_exact(lib, n, forced):
+@pytest.mark.parametrize("n,forced,one_call", [(2048, False, False), (8192, True, False), (8192, True, True)])
+def test_full_size_bounded_i64_exact(lib, n, forced, one_call):
     """BASELINE config 3 shape (8192^3, U[-2^24, 2^24], bound 2^61, prefix 9
     forced) through the device seam, against an independent exact product."""
     g = torch.Generator(device="cuda").manual_seed(n)
@@ -478,10 +586,17 @@ def test_full_size_bounded_i64_exact(lib, n, forced):
     s = stream()
     assert lib.rns8_cuda_pack_i64_device(0, A.data_ptr(), n, n, n, P, ra.data_ptr(), s) == OK
     assert lib.rns8_cuda_pack_i64_device(0, B.data_ptr(), n, n, n, P, rb.data_ptr(), s) == OK
-    assert lib.rns8_cuda_gemm_rns_device(0, ra.data_ptr(), rb.data_ptr(), rc.data_ptr(), n, n, n, P, 1, None, 0,
-                                         status.data_ptr(), s) == OK
-    assert lib.rns8_cuda_export_i64_device(0, rc.data_ptr(), n, n, P, 2**61, out.data_ptr(), n, status.data_ptr(),
-                                           s) == OK
+    if one_call:
+        sb = lib.rns8_cuda_gemm_export_bounded_scratch_bytes(0, n, n, n, P)
+        scratch = torch.empty(sb, dtype=torch.uint8, device="cuda")
+        assert lib.rns8_cuda_gemm_export_bounded_device(0, ra.data_ptr(), rb.data_ptr(), n, n, n, P, 1, 2**61,
+                                                        out.data_ptr(), n, scratch.data_ptr(), sb, status.data_ptr(),
+                                                        s) == OK
+    else:
+        assert lib.rns8_cuda_gemm_rns_device(0, ra.data_ptr(), rb.data_ptr(), rc.data_ptr(), n, n, n, P, 1, None, 0,
+                                             status.data_ptr(), s) == OK
+        assert lib.rns8_cuda_export_i64_device(0, rc.data_ptr(), n, n, P, 2**61, out.data_ptr(), n,
+                                               status.data_ptr(), s) == OK
     torch.cuda.synchronize()
     assert int(status[0].item()) == 0
     want = exact_i64_matmul_fp64(A, B)
