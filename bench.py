@@ -1,27 +1,38 @@
 """Benchmark of the RNS8 hot path on B200: effective exact int64 GOPS.
 
-Workload: C = A x B over int64, M = N = K = 8192, inputs
-uniform in [-2^24, 2^24] from a seed, declared bound 2^61, RNS8_BOUNDED_I64
-with the prefix forced to 9 (RNS8_PLAN_FORCE_FIXED_PREFIX; the default plan
-would select 8). One step = pack A + pack B into 9 centered int8 planes, nine
-int8 plane GEMMs (one persistent tcgen05 launch), Garner export to int64.
+Default workload: C = A x B over int64, M = N = K = 8192,
+inputs uniform in [-2^24, 2^24] from a seed, declared bound 2^61,
+RNS8_BOUNDED_I64 with the prefix forced to 9 (RNS8_PLAN_FORCE_FIXED_PREFIX;
+the default plan would select 8). One step = pack A + pack B into 9 centered
+int8 planes, nine int8 plane GEMMs (one persistent tcgen05 launch), export to
+int64 (fractional CRT, exact Garner for undecided cells).
+
+The other BASELINE configs run with --config C1|C2|C4|C5 (same metric, same
+JSON line; they are measurements for the record, the driver runs C3):
+  C1  int64 512^3, U[-2^20, 2^20], bound 2^49, prefix 7 (default plan)
+  C2  finite field 251, 64 independent 2048^3 pairs, grouped GEMM
+  C4  uint64 256 x 256 x 262144, U[0, 2^22), bound 2^62, prefix 8 (split-K)
+  C5  exact-wide signed int64 4096^3, full int64 range, 3 limbs, prefix 20 forced
 
   value  device-resident: inputs already in HBM, output left in HBM, timed
          with CUDA events on the launching stream (max over ranks).
-  e2e    the same step through the public C ABI (rns8_gemm_i64_oneshot) from
-         pinned host buffers: H2D of A and B and D2H of C inside the timing.
+  e2e    the same work through the public C ABI from pinned host buffers
+         (the oneshot call for C1/C3/C4, the matrix API for C2/C5): H2D of
+         the inputs and D2H of the result inside the timing.
 
-Multi-GPU (torchrun, one rank per GPU): rows are sharded, each rank owns an
-8192-row slab of A and C and a full B (weak scaling, no collective on the
-data path); value = all ranks' 2*M*N*K / max-over-ranks time.
+Multi-GPU (torchrun, one rank per GPU): rows are sharded, each rank owns a
+slab of A and C of the config's size and a full B (weak scaling, no collective
+on the data path); value = all ranks' work / max-over-ranks time.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config C1..C5] [--size S (C3 only: M = N = K = S)]
 """
 
 from __future__ import annotations
 
 import argparse
 import ctypes as C
+import dataclasses
 import json
 import os
 import statistics
@@ -34,12 +45,50 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-M = N = K = 8192
-PREFIX = 9
-BOUND = 2**61
-LO, HI = -(2**24), 2**24
 METRIC = "effective exact int64 GOPS (2MNK/t) at 1/2/4/8 B200; int8 tensor-pipe % of peak"
-WORKLOAD = "RNS8_BOUNDED_I64 8192^3 prefix-9 forced, U[-2^24,2^24], bound 2^61 (BASELINE config 3)"
+
+
+@dataclasses.dataclass
+class Config:
+    name: str
+    kind: str            # "i64" | "u64" | "finite" | "exact"
+    m: int
+    n: int
+    k: int
+    lo: int
+    hi: int
+    prefix: int          # residue planes per matrix (1 for finite)
+    forced: bool         # RNS8_PLAN_FORCE_FIXED_PREFIX
+    workload: str
+    bound: int = 0
+    batch: int = 1
+    modulus: int = 0
+    limbs: int = 0
+    cpu_rows: int = 128  # rows of A in the CPU sample
+
+    @property
+    def ops(self) -> float:
+        """Effective exact ops of one step: 2*M*N*K per product."""
+        return self.batch * 2.0 * self.m * self.n * self.k
+
+
+CONFIGS = {
+    "C1": Config("C1", "i64", 512, 512, 512, -(2**20), 2**20, 7, False,
+                 "RNS8_BOUNDED_I64 512^3, U[-2^20,2^20], bound 2^49, prefix 7 default (BASELINE config 1)",
+                 bound=2**49, cpu_rows=512),
+    "C2": Config("C2", "finite", 2048, 2048, 2048, 0, 250, 1, False,
+                 "RNS8_FINITE_FIELD_U8 modulus 251, 64 x 2048^3 grouped, U[0,250] (BASELINE config 2)",
+                 batch=64, modulus=251, cpu_rows=256),
+    "C3": Config("C3", "i64", 8192, 8192, 8192, -(2**24), 2**24, 9, True,
+                 "RNS8_BOUNDED_I64 8192^3 prefix-9 forced, U[-2^24,2^24], bound 2^61 (BASELINE config 3)",
+                 bound=2**61, cpu_rows=128),
+    "C4": Config("C4", "u64", 256, 256, 262144, 0, 2**22 - 1, 8, False,
+                 "RNS8_BOUNDED_U64 256x256x262144, U[0,2^22), bound 2^62, prefix 8 default (BASELINE config 4)",
+                 bound=2**62, cpu_rows=16),
+    "C5": Config("C5", "exact", 4096, 4096, 4096, -(2**63), 2**63 - 1, 20, True,
+                 "RNS8_EXACT_WIDE_SIGNED 4096^3, U[INT64_MIN,INT64_MAX], 3 limbs, prefix 20 forced "
+                 "(BASELINE config 5)", limbs=3, cpu_rows=16),
+}
 
 
 def parse():
@@ -48,12 +97,21 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="C3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-rows", type=int, default=128, help="rows of the CPU baseline slab sample")
-    ap.add_argument("--size", type=int, default=8192,
-                    help="M = N = K of the run (8192 is the benchmark; smaller sizes are for ncu captures)")
-    return ap.parse_args()
+    ap.add_argument("--cpu-rows", type=int, default=0, help="rows of A in the CPU baseline sample (0: the config's)")
+    ap.add_argument("--size", type=int, default=0,
+                    help="C3 only: M = N = K = size (8192 is the benchmark; smaller sizes are for ncu captures)")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.size:
+        if cfg.name != "C3":
+            ap.error("--size applies to C3 only")
+        cfg = dataclasses.replace(cfg, m=args.size, n=args.size, k=args.size)
+    if args.cpu_rows:
+        cfg = dataclasses.replace(cfg, cpu_rows=args.cpu_rows)
+    return args, cfg
 
 
 def dist_env():
@@ -154,56 +212,95 @@ def int8_peak_tops(torch, peaks) -> tuple[float, str]:
         return derived, f"{source} ({derived:.0f}); cuBLASLt int8 unavailable: {type(exc).__name__}"
 
 
-def profile_traffic() -> int | None:
-    """dram bytes per GEMM launch from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "tc_plane_gemm_c3.json"
-    if p.exists():
-        try:
-            return int(json.loads(p.read_text())["traffic_bytes_per_launch"])
-        except Exception:
-            return None
-    return None
+def profile_traffic(cfg: Config, kernel: str) -> int | None:
+    """dram bytes per launch of `kernel` on this config, from the committed ncu
+    summary (profiles/traffic.json), if it holds that pair."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return int(json.loads(p.read_text())[cfg.name][kernel]["dram_bytes_per_launch"])
+    except Exception:
+        return None
 
 
 # ----------------------------------------------------------------- CPU baseline
-def cpu_baseline(rows: int) -> dict:
-    """The CPU oracle (a restatement of the reference's src/cpu path, OpenMP over
-    all host cores) on a row slab of the workload: rows x 8192 by 8192 x 8192,
-    pack + 9 plane GEMMs + export."""
+def host_inputs(cfg: Config, rows: int, seed: int):
+    """Seeded host inputs for the CPU sample: a rows-row slab of A and all of B."""
     import numpy as np
 
+    rng = np.random.default_rng(seed)
+    if cfg.kind == "finite":
+        A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.uint8, endpoint=True)
+        B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.uint8, endpoint=True)
+    elif cfg.kind == "u64":
+        A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.uint64, endpoint=True)
+        B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.uint64, endpoint=True)
+    else:
+        A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.int64, endpoint=True)
+        B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.int64, endpoint=True)
+    return A, B
+
+
+def cpu_baseline(cfg: Config, rows: int) -> dict:
+    """The CPU oracle (a restatement of the reference's src/cpu path, OpenMP over
+    all host cores) on a row slab of the workload, scaled to the whole step.
+
+    B is packed once, as in the full workload; the slab's own stages (pack A,
+    the plane GEMMs, the export) are timed on `rows` rows. The full step is
+    t_pack_B + (M / rows) * t_slab per product (x batch for C2), and value is
+    the workload's effective ops over that time."""
     from oracle import bridge
 
     lib = bridge.lib()
     threads = lib.oracle_max_threads()
-    rng = np.random.default_rng(123)
-    A = rng.integers(LO, HI, (rows, K), dtype=np.int64, endpoint=True)
-    B = rng.integers(LO, HI, (K, N), dtype=np.int64, endpoint=True)
-    Cout = np.zeros((rows, N), np.int64)
+    A, B = host_inputs(cfg, rows, 123)
+    P = cfg.prefix
     t0 = time.perf_counter()
-    st, _, used = bridge.gemm_bounded_oneshot(A, B, BOUND, max_prefix=PREFIX, flags=1, out=Cout)
-    dt = time.perf_counter() - t0
-    assert st == 0 and used == PREFIX
-    return {"value": 2.0 * rows * N * K / dt / 1e9, "unit": "GOPS", "cores": threads, "kind": "port",
-            "sample": f"oracle oneshot on a {rows}x{K} by {K}x{N} row slab of the workload "
-                      f"(pack A and B, {PREFIX} plane GEMMs, export), {dt:.1f} s, {threads} threads",
-            "seconds": dt}
+    if cfg.kind == "finite":
+        b = bridge.pack_finite_u8(B, cfg.modulus)
+    else:
+        b = bridge.pack(B, P)
+    t_b = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    if cfg.kind == "finite":
+        c = bridge.ring_gemm(bridge.pack_finite_u8(A, cfg.modulus), b, cfg.modulus)
+        out = (c.astype("int16") % cfg.modulus).astype("uint8")  # centered -> canonical, a1/a15
+        st = 0
+        what = f"oracle pack, GEMM mod {cfg.modulus}, export"
+    else:
+        c = bridge.gemm_rns(bridge.pack(A, P), b, P)
+        if cfg.kind == "i64":
+            st, out = bridge.export_i64(c, P, cfg.bound)
+        elif cfg.kind == "u64":
+            st, out = bridge.export_u64(c, P, cfg.bound)
+        else:
+            st, out = bridge.export_limbs(c, P, cfg.limbs, True)
+        what = f"oracle pack, {P} plane GEMMs, " + (f"{cfg.limbs}-limb export" if cfg.kind == "exact" else "export")
+    t_slab = time.perf_counter() - t0
+    assert st == 0 and out.shape[0] == rows
+    full = cfg.batch * (t_b + cfg.m / rows * t_slab)
+    return {"value": cfg.ops / full / 1e9, "unit": "GOPS", "cores": threads, "kind": "port",
+            "sample": f"{what}: B ({cfg.k}x{cfg.n}) packed once in {t_b:.2f} s, a {rows}-row slab of A through "
+                      f"the remaining stages in {t_slab:.2f} s; step = {cfg.batch} x (t_B + {cfg.m}/{rows} x t_slab)"
+                      f" = {full:.1f} s; {threads} threads",
+            "seconds": t_b + t_slab, "step_seconds": full}
 
 
-def reference_arm(args) -> None:
+def reference_arm(args, cfg: Config) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    rows = max(8, args.cpu_rows // 4)
+    rows = max(8, cfg.cpu_rows // 4)
     for _ in range(args.warmup):
-        cpu_baseline(rows)
-    vals = [cpu_baseline(rows) for _ in range(args.steps)]
+        cpu_baseline(cfg, rows)
+    vals = [cpu_baseline(cfg, rows) for _ in range(args.steps)]
     v = statistics.median(x["value"] for x in vals)
-    sec = sum(x["seconds"] for x in vals)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GOPS", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sec / args.steps,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * statistics.median(x["step_seconds"] for x in vals),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample_rows": rows, "note": "reference CPU path (oracle port; the "
+            "config": {"workload": cfg.workload, "sample_rows": rows, "note": "reference CPU path (oracle port; the "
                        "reference's own src/cpu needs Boost.Multiprecision, absent here)"},
             "cpu_baseline": {**{k: vals[0][k] for k in ("unit", "cores", "kind", "sample")}, "value": v},
             "e2e": {"value": v, "unit": "GOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -211,12 +308,196 @@ def reference_arm(args) -> None:
 
 
 # --------------------------------------------------------------------- our arm
+class DevicePipeline:
+    """Device-resident buffers and the three stages of one step (pack, plane
+    GEMM, export), launched through the C-ABI device seam on one stream."""
+
+    def __init__(self, torch, lib, cfg: Config, dev: int, rank: int, sptr):
+        self.torch, self.lib, self.cfg, self.dev, self.sptr = torch, lib, cfg, dev, sptr
+        m, n, k, P, bt = cfg.m, cfg.n, cfg.k, cfg.prefix, cfg.batch
+        g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+        gb = torch.Generator(device="cuda").manual_seed(999)
+        if cfg.kind == "finite":
+            self.A = torch.randint(cfg.lo, cfg.hi + 1, (bt, m, k), dtype=torch.uint8, device="cuda", generator=g)
+            self.B = torch.randint(cfg.lo, cfg.hi + 1, (bt, k, n), dtype=torch.uint8, device="cuda", generator=gb)
+            self.ra = torch.empty((bt, m, k), dtype=torch.int8, device="cuda")
+            self.rb = torch.empty((bt, k, n), dtype=torch.int8, device="cuda")
+            self.rc = torch.empty((bt, m, n), dtype=torch.int8, device="cuda")
+            self.out = torch.empty((bt, m, n), dtype=torch.uint8, device="cuda")
+            vp = C.c_void_p * bt
+            self.pa = vp(*[self.ra[t].data_ptr() for t in range(bt)])
+            self.pb = vp(*[self.rb[t].data_ptr() for t in range(bt)])
+            self.pc = vp(*[self.rc[t].data_ptr() for t in range(bt)])
+            self.sbytes = lib.rns8_cuda_gemm_finite_u8_scratch_bytes(dev, m, n, k, bt)
+        else:
+            if cfg.kind == "exact":  # full int64 range: uniform random bytes
+                self.A = torch.randint(0, 256, (m, k, 8), dtype=torch.uint8, device="cuda", generator=g).view(
+                    torch.int64).reshape(m, k)
+                self.B = torch.randint(0, 256, (k, n, 8), dtype=torch.uint8, device="cuda", generator=gb).view(
+                    torch.int64).reshape(k, n)
+            else:  # u64 values below 2^63 share int64's bit pattern
+                self.A = torch.randint(cfg.lo, cfg.hi + 1, (m, k), dtype=torch.int64, device="cuda", generator=g)
+                self.B = torch.randint(cfg.lo, cfg.hi + 1, (k, n), dtype=torch.int64, device="cuda", generator=gb)
+            self.ra = torch.empty((P, m, k), dtype=torch.int8, device="cuda")
+            self.rb = torch.empty((P, k, n), dtype=torch.int8, device="cuda")
+            self.rc = torch.empty((P, m, n), dtype=torch.int8, device="cuda")
+            shape = (m, n, cfg.limbs) if cfg.kind == "exact" else (m, n)
+            self.out = torch.empty(shape, dtype=torch.int64, device="cuda")
+            self.sbytes = lib.rns8_cuda_gemm_rns_scratch_bytes(dev, m, n, k, P)
+        self.scratch = torch.empty(max(1, self.sbytes), dtype=torch.uint8, device="cuda")
+        self.status = torch.zeros(4, dtype=torch.int32, device="cuda")
+        gemm_launches = (1 + (1 if self.sbytes > 0 else 0)) * ((bt + 31) // 32 if cfg.kind == "finite" else 1)
+        self.launches_per_step = 2 + gemm_launches + 1
+        footprint = sum(t.numel() * t.element_size() for t in (self.A, self.B, self.ra, self.rb, self.rc, self.out))
+        self.fits_l2 = footprint < (512 << 20)  # L2 is 126 MB: below this, flush it between steps
+
+    @staticmethod
+    def _check(st, what):
+        if st != 0:
+            raise RuntimeError(f"{what} failed with status {st}")
+
+    def pack(self):
+        cfg, lib, d, s = self.cfg, self.lib, self.dev, self.sptr
+        m, n, k, bt = cfg.m, cfg.n, cfg.k, cfg.batch
+        if cfg.kind == "finite":
+            self._check(lib.rns8_cuda_pack_finite_u8_device(d, self.A.data_ptr(), bt * m, k, k, cfg.modulus,
+                                                            self.ra.data_ptr(), s), "pack A")
+            self._check(lib.rns8_cuda_pack_finite_u8_device(d, self.B.data_ptr(), bt * k, n, n, cfg.modulus,
+                                                            self.rb.data_ptr(), s), "pack B")
+            return
+        fn = lib.rns8_cuda_pack_u64_device if cfg.kind == "u64" else lib.rns8_cuda_pack_i64_device
+        self._check(fn(d, self.A.data_ptr(), m, k, k, cfg.prefix, self.ra.data_ptr(), s), "pack A")
+        self._check(fn(d, self.B.data_ptr(), k, n, n, cfg.prefix, self.rb.data_ptr(), s), "pack B")
+
+    def gemm(self):
+        cfg, lib, d, s = self.cfg, self.lib, self.dev, self.sptr
+        if cfg.kind == "finite":
+            self._check(lib.rns8_cuda_gemm_finite_u8_grouped_device(
+                d, self.pa, self.pb, self.pc, cfg.batch, cfg.m, cfg.n, cfg.k, cfg.modulus, 0,
+                self.scratch.data_ptr(), self.sbytes, self.status.data_ptr(), s), "grouped gemm")
+            return
+        self._check(lib.rns8_cuda_gemm_rns_device(d, self.ra.data_ptr(), self.rb.data_ptr(), self.rc.data_ptr(),
+                                                  cfg.m, cfg.n, cfg.k, cfg.prefix, 0, self.scratch.data_ptr(),
+                                                  self.sbytes, self.status.data_ptr(), s), "gemm")
+
+    def export(self):
+        cfg, lib, d, s = self.cfg, self.lib, self.dev, self.sptr
+        m, n = cfg.m, cfg.n
+        if cfg.kind == "finite":
+            st = lib.rns8_cuda_export_finite_u8_device(d, self.rc.data_ptr(), cfg.batch * m, n, cfg.modulus,
+                                                       self.out.data_ptr(), n, s)
+        elif cfg.kind == "exact":
+            st = lib.rns8_cuda_export_limbs_device(d, self.rc.data_ptr(), m, n, cfg.prefix, 1, cfg.limbs,
+                                                   self.out.data_ptr(), n, self.status.data_ptr(), s)
+        else:
+            fn = lib.rns8_cuda_export_u64_device if cfg.kind == "u64" else lib.rns8_cuda_export_i64_device
+            st = fn(d, self.rc.data_ptr(), m, n, cfg.prefix, cfg.bound, self.out.data_ptr(), n,
+                    self.status.data_ptr(), s)
+        self._check(st, "export")
+
+    def step(self, events=None):
+        stream = self.torch.cuda.current_stream()
+        for i, stage in enumerate((self.pack, self.gemm, self.export)):
+            if events:
+                events[i].record(stream)
+            stage()
+        if events:
+            events[3].record(stream)
+
+    def device_status(self) -> int:
+        return int(self.status[0].item())
+
+    # Algorithmic work of each stage (ops for the GEMM, HBM bytes for pack and export).
+    def stage_work(self) -> dict:
+        cfg = self.cfg
+        m, n, k, P, bt = cfg.m, cfg.n, cfg.k, cfg.prefix, cfg.batch
+        elem_in = 1 if cfg.kind == "finite" else 8
+        out_bytes = {"finite": 1, "exact": 8 * cfg.limbs}.get(cfg.kind, 8)
+        return {
+            "pack": ("hbm", bt * (elem_in + P) * (m * k + k * n)),
+            "plane_gemm": ("tensor", bt * P * 2.0 * m * n * k),
+            "export": ("hbm", bt * (P + out_bytes) * m * n),
+        }
+
+
+class EndToEnd:
+    """The same work through the public C ABI from pinned host buffers."""
+
+    def __init__(self, torch, r8, lib, cfg: Config, dev: int, pipe: DevicePipeline):
+        self.cfg, self.lib, self.r8 = cfg, lib, r8
+        self.ctx = r8.Context(dev)
+        m, n, k = cfg.m, cfg.n, cfg.k
+        self.hA = pipe.A.cpu().pin_memory()
+        self.hB = pipe.B.cpu().pin_memory()
+        self.hC = torch.empty(tuple(pipe.out.shape), dtype=pipe.out.dtype).pin_memory()
+        S = r8.Semantics
+        if cfg.kind in ("i64", "u64"):
+            signed = cfg.kind == "i64"
+            self.desc = r8.gemm_desc(S.BOUNDED_I64 if signed else S.BOUNDED_U64,
+                                     r8.BoundKind.GLOBAL_MAX_ABS if signed else r8.BoundKind.GLOBAL_MAX_UNSIGNED,
+                                     m, n, k, bound=cfg.bound, max_prefix=cfg.prefix if cfg.forced else 0,
+                                     flags=r8.PLAN_FORCE_FIXED_PREFIX if cfg.forced else 0)
+            self.oneshot = lib.rns8_gemm_i64_oneshot if signed else lib.rns8_gemm_u64_oneshot
+            self.api = ("rns8_gemm_i64_oneshot" if signed else "rns8_gemm_u64_oneshot") + " (pinned host buffers)"
+        elif cfg.kind == "finite":
+            desc = r8.gemm_desc(S.FINITE_FIELD_U8, r8.BoundKind.NONE, m, n, k, finite_modulus=cfg.modulus)
+            self.plan = r8.Plan(self.ctx, desc)
+            self.tasks = []
+            for _ in range(cfg.batch):
+                a, b, c = (r8.Matrix.for_plan(self.ctx, self.plan, r) for r in "abc")
+                self.tasks.append((a, b, c, r8.Workspace(self.ctx, self.plan)))
+            self.nA, self.nB, self.nC = self.hA.numpy(), self.hB.numpy(), self.hC.numpy()
+            self.api = ("rns8_pack_finite_u8 x 128, rns8_gemm_finite_u8_grouped (64 tasks), rns8_export_finite_u8 x 64 "
+                        "(pinned host buffers)")
+        else:
+            desc = r8.gemm_desc(S.EXACT_WIDE_SIGNED, r8.BoundKind.NONE, m, n, k, max_prefix=cfg.prefix,
+                                flags=r8.PLAN_FORCE_FIXED_PREFIX)
+            self.plan = r8.Plan(self.ctx, desc)
+            assert self.plan.prefix == cfg.prefix
+            self.a, self.b, self.c = (r8.Matrix.for_plan(self.ctx, self.plan, r) for r in "abc")
+            self.ws = r8.Workspace(self.ctx, self.plan)
+            self.nA, self.nB = self.hA.numpy(), self.hB.numpy()
+            self.nC = self.hC.numpy().view("uint64")
+            self.api = ("rns8_pack_i64 x 2, rns8_gemm_rns, rns8_export_exact_wide_signed_limbs "
+                        "(pinned host buffers; includes the host exact-range admission proof)")
+        elem_in = 1 if cfg.kind == "finite" else 8
+        self.h2d = cfg.batch * elem_in * (m * k + k * n)
+        self.d2h = self.hC.numel() * self.hC.element_size()
+
+    def run(self):
+        cfg, r8, lib = self.cfg, self.r8, self.lib
+        if cfg.kind in ("i64", "u64"):
+            st = self.oneshot(self.ctx.handle, C.byref(self.desc), self.hA.data_ptr(), cfg.k, self.hB.data_ptr(),
+                              cfg.n, self.hC.data_ptr(), cfg.n)
+            DevicePipeline._check(st, self.api)
+        elif cfg.kind == "finite":
+            for t, (a, b, _, _) in enumerate(self.tasks):
+                a.pack_finite_u8(cfg.modulus, self.nA[t])
+                b.pack_finite_u8(cfg.modulus, self.nB[t])
+            r8.gemm_finite_u8_grouped(self.ctx, self.plan, cfg.modulus, self.tasks)
+            for t, (_, _, c, _) in enumerate(self.tasks):
+                r8.export_finite_u8(self.ctx, self.plan, cfg.modulus, c, out=self.nC[t])
+        else:
+            self.a.pack_i64(self.nA)
+            self.b.pack_i64(self.nB)
+            r8.gemm_rns(self.ctx, self.plan, self.a, self.b, self.c, self.ws)
+            r8.export_exact_wide_limbs(self.ctx, self.plan, self.c, cfg.limbs, signed=True, out=self.nC)
+
+    def close(self):
+        for obj in getattr(self, "tasks", []):
+            for h in obj:
+                h.close()
+        for name in ("a", "b", "c", "ws", "plan"):
+            h = getattr(self, name, None)
+            if h is not None:
+                h.close()
+        self.ctx.close()
+
+
 def main():
-    args = parse()
-    global M, N, K
-    M = N = K = args.size
+    args, cfg = parse()
     if args.impl == "reference":
-        reference_arm(args)
+        reference_arm(args, cfg)
         return
     import torch
     import torch.distributed as dist
@@ -230,143 +511,117 @@ def main():
     import rns8_b200 as r8
 
     lib = r8.lib()
-    dev = local
     stream = torch.cuda.current_stream()
     sptr = C.c_void_p(stream.cuda_stream)
-
-    # Inputs: this rank's 8192-row slab of A and all of B, generated on device.
-    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    A = torch.randint(LO, HI + 1, (M, K), dtype=torch.int64, device="cuda", generator=g)
-    gb = torch.Generator(device="cuda").manual_seed(999)
-    B = torch.randint(LO, HI + 1, (K, N), dtype=torch.int64, device="cuda", generator=gb)
-    ra = torch.empty((PREFIX, M, K), dtype=torch.int8, device="cuda")
-    rb = torch.empty((PREFIX, K, N), dtype=torch.int8, device="cuda")
-    rc = torch.empty((PREFIX, M, N), dtype=torch.int8, device="cuda")
-    out = torch.empty((M, N), dtype=torch.int64, device="cuda")
-    status = torch.zeros(4, dtype=torch.int32, device="cuda")
-    sbytes = lib.rns8_cuda_gemm_rns_scratch_bytes(dev, M, N, K, PREFIX)
-    scratch = torch.empty(max(1, sbytes), dtype=torch.uint8, device="cuda")
-
-    ev = {k: [torch.cuda.Event(enable_timing=True) for _ in range(5)] for k in ("s",)}
-
-    def check(st, what):
-        if st != 0:
-            raise RuntimeError(f"{what} failed with status {st}")
-
-    def step(record=None):
-        if record:
-            record[0].record(stream)
-        check(lib.rns8_cuda_pack_i64_device(dev, A.data_ptr(), M, K, K, PREFIX, ra.data_ptr(), sptr), "pack A")
-        check(lib.rns8_cuda_pack_i64_device(dev, B.data_ptr(), K, N, N, PREFIX, rb.data_ptr(), sptr), "pack B")
-        if record:
-            record[1].record(stream)
-        check(lib.rns8_cuda_gemm_rns_device(dev, ra.data_ptr(), rb.data_ptr(), rc.data_ptr(), M, N, K, PREFIX, 0,
-                                            scratch.data_ptr(), sbytes, status.data_ptr(), sptr), "gemm")
-        if record:
-            record[2].record(stream)
-        check(lib.rns8_cuda_export_i64_device(dev, rc.data_ptr(), M, N, PREFIX, BOUND, out.data_ptr(), N,
-                                              status.data_ptr(), sptr), "export")
-        if record:
-            record[3].record(stream)
+    pipe = DevicePipeline(torch, lib, cfg, local, rank, sptr)
 
     for _ in range(max(3, args.warmup)):
-        step()
+        pipe.step()
     torch.cuda.synchronize()
-    if int(status[0].item()) != 0:
-        raise RuntimeError(f"device status {int(status[0].item()):#x} after warm-up")
+    if pipe.device_status() != 0:
+        raise RuntimeError(f"device status {pipe.device_status():#x} after warm-up")
 
     peaks = measured_peaks()
     peak_int8, peak_note = int8_peak_tops(torch, peaks)
     torch.cuda.synchronize()
 
-    clocks = ClockSampler(dev)
+    clocks = ClockSampler(local)
     records = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
+    # Small footprints are timed step by step with a 256 MiB write between
+    # steps (outside the step's events) so that no step starts with a warm L2.
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if pipe.fits_l2 else None
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for i in range(args.steps):
-        step(records[i])
+        if flush is not None:
+            flush.zero_()
+        pipe.step(records[i])
     stop.record(stream)
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
-    total_ms = start.elapsed_time(stop)
-    pack_ms = statistics.mean(r[0].elapsed_time(r[1]) for r in records)
-    gemm_ms = statistics.mean(r[1].elapsed_time(r[2]) for r in records)
-    exp_ms = statistics.mean(r[2].elapsed_time(r[3]) for r in records)
-    if int(status[0].item()) != 0:
-        raise RuntimeError(f"device status {int(status[0].item()):#x} in the timed region")
+    if flush is None:
+        total_ms = start.elapsed_time(stop)
+    else:
+        total_ms = sum(r[0].elapsed_time(r[3]) for r in records)
+    stage_ms = {name: statistics.mean(r[i].elapsed_time(r[i + 1]) for r in records)
+                for i, name in enumerate(("pack", "plane_gemm", "export"))}
+    if pipe.device_status() != 0:
+        raise RuntimeError(f"device status {pipe.device_status():#x} in the timed region")
 
     t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_per_step = float(t.item()) / args.steps
-    value = world * 2.0 * M * N * K / (ms_per_step * 1e-3) / 1e9
+    value = world * cfg.ops / (ms_per_step * 1e-3) / 1e9
 
-    # ---- e2e through the public C ABI from pinned host memory -------------------
+    # ---- e2e through the public C ABI from pinned host buffers -------------------
     e2e = None
     if not args.no_e2e:
-        hA = A.cpu().pin_memory()
-        hB = B.cpu().pin_memory()
-        hC = torch.empty((M, N), dtype=torch.int64).pin_memory()
-        ctx = r8.Context(dev)
-        desc = r8.gemm_desc(r8.Semantics.BOUNDED_I64, r8.BoundKind.GLOBAL_MAX_ABS, M, N, K, bound=BOUND,
-                            max_prefix=PREFIX, flags=r8.PLAN_FORCE_FIXED_PREFIX)
-
-        def oneshot():
-            st = lib.rns8_gemm_i64_oneshot(ctx.handle, C.byref(desc), hA.data_ptr(), K, hB.data_ptr(), N,
-                                           hC.data_ptr(), N)
-            check(st, "rns8_gemm_i64_oneshot")
-
+        ee = EndToEnd(torch, r8, lib, cfg, local, pipe)
         for _ in range(max(3, args.warmup)):
-            oneshot()
+            ee.run()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            oneshot()  # synchronous: ends with a device sync and the result in host memory
+            ee.run()  # synchronous: every call ends with a device sync, the result in host memory
         el = torch.tensor([(time.perf_counter() - t0) * 1e3], dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(el, op=dist.ReduceOp.MAX)
         e2e_ms = float(el.item()) / args.steps
-        assert torch.equal(hC, out.cpu()), "e2e result differs from the device-resident result"
-        e2e = {"value": world * 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e9, "unit": "GOPS",
-               "h2d_bytes_per_step": 8 * (M * K + K * N), "d2h_bytes_per_step": 8 * M * N, "ms_per_step": e2e_ms,
-               "api": "rns8_gemm_i64_oneshot (pinned host buffers)"}
-        ctx.close()
+        assert torch.equal(ee.hC, pipe.out.cpu()), "e2e result differs from the device-resident result"
+        e2e = {"value": world * cfg.ops / (e2e_ms * 1e-3) / 1e9, "unit": "GOPS", "h2d_bytes_per_step": ee.h2d,
+               "d2h_bytes_per_step": ee.d2h, "ms_per_step": e2e_ms, "api": ee.api}
+        ee.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.cpu_rows)
+        cpu = cpu_baseline(cfg, cfg.cpu_rows)
 
-    gemm_ops = PREFIX * 2.0 * M * N * K
-    achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
-    pack_bytes = 2 * (8 * M * K) + 2 * PREFIX * M * K
-    exp_bytes = PREFIX * M * N + 8 * M * N
+    # Roofline of the dominant stage (one kernel launch per stage, except that
+    # the grouped finite GEMM launches once per 32 tasks).
+    work = pipe.stage_work()
+    dominant = max(stage_ms, key=stage_ms.get)
     hbm = float(peaks.get("hbm_gbs", 6650.0))
+    hbm_note = "MEASURED_PEAKS.json hbm_gbs (STREAM copy)" if not peaks.get("fallback") else "fallback 6650 GB/s"
+    kernel_names = {"pack": "pack_kernel", "plane_gemm": "tc_plane_gemm_kernel", "export": "export kernel"}
+    stage_frac = {}
+    for name, (bound, amount) in work.items():
+        sec = stage_ms[name] * 1e-3
+        stage_frac[name] = (amount / sec / 1e12 / peak_int8) if bound == "tensor" else (amount / sec / 1e9 / hbm)
+    bound, amount = work[dominant]
+    sec = stage_ms[dominant] * 1e-3
+    if bound == "tensor":
+        roof = {"kernel": kernel_names[dominant], "bound": "tensor", "achieved": amount / sec / 1e12,
+                "peak": peak_int8, "unit": "TOPS (int8)", "peak_source": peak_note,
+                "algorithmic_ops_per_step": amount}
+    else:
+        roof = {"kernel": kernel_names[dominant], "bound": "hbm", "achieved": amount / sec / 1e9, "peak": hbm,
+                "unit": "GB/s", "peak_source": hbm_note, "algorithmic_bytes_per_step": amount}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = profile_traffic(cfg, kernel_names[dominant])
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GOPS", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "m_per_rank": M, "n": N, "k": K, "prefix": PREFIX, "bound": "2^61",
-                       "parallelism": f"row-slab x{world}", "l2": "inputs larger than L2 (512 MiB each)"},
-            "roofline": {"kernel": "tc_plane_gemm_kernel", "bound": "tensor", "achieved": achieved,
-                         "peak": peak_int8, "unit": "TOPS (int8)", "frac": achieved / peak_int8,
-                         "peak_source": peak_note, "traffic": profile_traffic(),
-                         "algorithmic_ops_per_launch": gemm_ops},
-            "stages_ms": {"pack_a_b": pack_ms, "plane_gemm": gemm_ms, "export": exp_ms},
-            "stage_hbm_frac": {"pack": pack_bytes / (pack_ms * 1e-3) / 1e9 / hbm,
-                               "export": exp_bytes / (exp_ms * 1e-3) / 1e9 / hbm, "peak_gbs": hbm,
-                               "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
+            "vs_baseline": None, "dtype": "uint8" if cfg.kind == "finite" else "int64", "data": "synthetic",
+            "config": {"workload": cfg.workload, "name": cfg.name, "m_per_rank": cfg.m, "n": cfg.n, "k": cfg.k,
+                       "batch": cfg.batch, "prefix": cfg.prefix, "parallelism": f"row-slab x{world}",
+                       "l2": "L2 flushed between steps (256 MiB write outside the step's events)"
+                             if pipe.fits_l2 else "inputs larger than L2"},
+            "roofline": roof,
+            "stages_ms": stage_ms,
+            "stage_frac_of_peak": stage_frac,
             "e2e": e2e, "cpu_baseline": cpu, "clocks": clock_info,
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": pipe.launches_per_step * args.steps,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

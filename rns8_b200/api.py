@@ -204,9 +204,13 @@ def export_finite_u8(ctx: Context, plan: Plan, modulus: int, c: Matrix, out: np.
     return out
 
 
-def export_exact_wide_limbs(ctx: Context, plan: Plan, c: Matrix, limb_count: int, signed: bool = True) -> np.ndarray:
-    """Returns a (m, n, limb_count) uint64 array of little-endian limbs."""
-    out = np.zeros((plan.desc.m, plan.desc.n, limb_count), np.uint64)
+def export_exact_wide_limbs(ctx: Context, plan: Plan, c: Matrix, limb_count: int, signed: bool = True,
+                            out: np.ndarray | None = None) -> np.ndarray:
+    """Returns a (m, n, limb_count) uint64 array of little-endian limbs (written
+    into `out` when given: C-contiguous, that shape)."""
+    shape = (plan.desc.m, plan.desc.n, limb_count)
+    out = np.zeros(shape, np.uint64) if out is None else out
+    assert out.shape == shape and out.flags.c_contiguous
     fn = lib().rns8_export_exact_wide_signed_limbs if signed else lib().rns8_export_exact_wide_unsigned_limbs
     check(fn(ctx.handle, plan.handle, c.handle, _ptr(out), plan.desc.n, limb_count), "rns8_export_exact_wide_limbs")
     return out

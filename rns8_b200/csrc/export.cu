@@ -97,29 +97,13 @@ __global__ void __launch_bounds__(256) export_kernel(ExportArgs a) {
     for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += step) {
       uint32_t w[P];
 #pragma unroll
-      for (int p = 0; p < P; ++p)
-        w[p] = __ldcs(reinterpret_cast<const uint32_t*>(a.planes + static_cast<int64_t>(p) * cells) + g) ^ 0x80808080u;
+      for (int p = 0; p < P; ++p) w[p] = __ldcs(reinterpret_cast<const uint32_t*>(a.planes + static_cast<int64_t>(p) * cells) + g);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        uint32_t u[P];  // r + 128
+        int r[P];
 #pragma unroll
-        for (int p = 0; p < P; ++p) u[p] = __byte_perm(w[p], 0u, 0x4440u | static_cast<uint32_t>(e));
-        const int64_t cell = 4 * g + e;
-        int verdict = -1;
-        if constexpr (kMode == Mode::I64 || kMode == Mode::U64) {
-          if (a.frac.enabled) {
-            uint64_t v;
-            verdict = frac_reconstruct<P>(u, a.frac, &v);
-            if (verdict == 1) static_cast<uint64_t*>(a.dst)[dst_index(a, cell)] = v;
-          }
-        }
-        if (verdict < 0) {
-          int r[P];
-#pragma unroll
-          for (int p = 0; p < P; ++p) r[p] = static_cast<int>(u[p]) - 128;
-          verdict = export_cell<P, kMode>(a, cell, r) ? 1 : 0;
-        }
-        bad |= verdict == 0;
+        for (int p = 0; p < P; ++p) r[p] = static_cast<int>(static_cast<int8_t>(w[p] >> (8 * e)));
+        bad |= !export_cell<P, kMode>(a, 4 * g + e, r);
       }
     }
   } else {
@@ -133,9 +117,116 @@ __global__ void __launch_bounds__(256) export_kernel(ExportArgs a) {
   if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(a.status, kDevRangeError);
 }
 
+template <int kCells>
+__device__ __forceinline__ void load_plane_words(const int8_t* src, uint32_t (&w)[kCells / 4]) {
+  if constexpr (kCells == 4) {
+    w[0] = __ldcs(reinterpret_cast<const unsigned int*>(src));
+  } else if constexpr (kCells == 8) {
+    const uint2 v = __ldcs(reinterpret_cast<const uint2*>(src));
+    w[0] = v.x;
+    w[1] = v.y;
+  } else {
+    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src));
+    w[0] = v.x;
+    w[1] = v.y;
+    w[2] = v.z;
+    w[3] = v.w;
+  }
+}
+
+// Bounded int64 / uint64 export, kCells consecutive cells per thread: one
+// kCells-byte load per plane, the fractional CRT per cell, 16-byte streaming
+// stores when the destination is contiguous (ld == n, 16-byte aligned).
+template <int P, bool kSigned, int kCells, bool kContig>
+__global__ void __launch_bounds__(256) export_bounded_kernel(ExportArgs a) {
+  const int64_t cells = a.m * a.n;
+  const int64_t groups = cells / kCells;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  bool bad = false;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += step) {
+    uint32_t w[P][kCells / 4];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      load_plane_words<kCells>(a.planes + static_cast<int64_t>(p) * cells + g * kCells, w[p]);
+#pragma unroll
+      for (int j = 0; j < kCells / 4; ++j) w[p][j] ^= 0x80808080u;  // r + 128 in every byte
+    }
+    // Fast path: the fractional CRT. Cells it cannot decide are flagged and
+    // redone by the exact Garner path below, after the vector stores.
+    uint32_t undecided = a.frac.enabled ? 0u : (1u << kCells) - 1u;
+    const int64_t first = g * kCells;
+    if (a.frac.enabled) {
+#pragma unroll
+      for (int e = 0; e < kCells; e += 2) {
+        uint64_t v[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t u[P];
+#pragma unroll
+          for (int p = 0; p < P; ++p)
+            u[p] = __byte_perm(w[p][(e + h) / 4], 0u, 0x4440u | static_cast<uint32_t>((e + h) & 3));
+          const int verdict = frac_reconstruct<P>(u, a.frac, &v[h]);
+          bad |= verdict == 0;
+          undecided |= verdict < 0 ? (1u << (e + h)) : 0u;
+        }
+        if constexpr (kContig) {
+          __stcs(reinterpret_cast<ulonglong2*>(static_cast<uint64_t*>(a.dst) + first + e),
+                 make_ulonglong2(static_cast<unsigned long long>(v[0]), static_cast<unsigned long long>(v[1])));
+        } else {
+          static_cast<uint64_t*>(a.dst)[dst_index(a, first + e)] = v[0];
+          static_cast<uint64_t*>(a.dst)[dst_index(a, first + e + 1)] = v[1];
+        }
+      }
+    }
+    while (undecided != 0) {
+      const int e = __ffs(undecided) - 1;
+      undecided &= undecided - 1;
+      int r[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        uint32_t word = w[p][0];
+#pragma unroll
+        for (int j = 1; j < kCells / 4; ++j) word = (e >> 2) == j ? w[p][j] : word;
+        r[p] = static_cast<int>((word >> (8 * (e & 3))) & 0xFFu) - 128;
+      }
+      uint64_t v;
+      if (reconstruct_bounded<P, kSigned>(r, a.lim, &v))
+        static_cast<uint64_t*>(a.dst)[dst_index(a, first + e)] = v;
+      else
+        bad = true;
+    }
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(a.status, kDevRangeError);
+}
+
+template <int P, bool kSigned, int kCells>
+cudaError_t launch_bounded(const ExportArgs& a, cudaStream_t stream) {
+  const int64_t groups = a.m * a.n / kCells;
+  int64_t blocks = (groups + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks < 1) blocks = 1;
+  const bool contig = a.ld == a.n && reinterpret_cast<uintptr_t>(a.dst) % 16 == 0;
+  if (contig)
+    export_bounded_kernel<P, kSigned, kCells, true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+  else
+    export_bounded_kernel<P, kSigned, kCells, false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+#ifndef RNS8_EXPORT_CELLS
+#define RNS8_EXPORT_CELLS 8
+#endif
+
 template <int P, Mode kMode>
 cudaError_t launch_export(const ExportArgs& a, cudaStream_t stream) {
   const int64_t cells = a.m * a.n;
+  if constexpr (kMode == Mode::I64 || kMode == Mode::U64) {
+    constexpr bool kSigned = kMode == Mode::I64;
+    const uintptr_t base = reinterpret_cast<uintptr_t>(a.planes);
+    constexpr int kWide = RNS8_EXPORT_CELLS;
+    if (cells % kWide == 0 && base % kWide == 0) return launch_bounded<P, kSigned, kWide>(a, stream);
+    if (cells % 4 == 0 && base % 4 == 0) return launch_bounded<P, kSigned, 4>(a, stream);
+  }
   const bool vec = (cells % 4 == 0) && (reinterpret_cast<uintptr_t>(a.planes) % 4 == 0);
   const int64_t work = vec ? cells / 4 : cells;
   int64_t blocks = (work + 255) / 256;

@@ -210,11 +210,14 @@ __device__ __forceinline__ bool reconstruct_bounded(const int (&r)[P], const Bou
 // is used by the Ozaki-II integer emulation of floating-point GEMM.) Cells
 // whose fraction lies within the rounding error of the bound's edge are left
 // to the exact Garner path.
+constexpr int64_t kQuotientBias = 4096;  // > 128 * P + 1: keeps the biased quotient nonnegative
+
 template <int P>
 struct FracTable {
   uint32_t F[P];     // round(2^31 * inv_i / m_i)
-  uint64_t G[P];     // (E_i * inv_i) mod 2^64
-  uint64_t C0;       // 128 * sum G_i mod 2^64: residues enter as u_i = r_i + 128
+  uint32_t Glo[P];   // (E_i * inv_i) mod 2^64, low and high words
+  uint32_t Ghi[P];
+  uint64_t C0;       // 128 * sum G_i - kQuotientBias * M  (mod 2^64)
   int64_t sumF128;   // 128 * sum F_i
   uint64_t M64;      // M mod 2^64
 };
@@ -237,46 +240,53 @@ __host__ __device__ constexpr FracTable<P> make_frac_table() {
       emod = (emod * ladder_at(j)) % mi;
     }
     const uint32_t inv = inv_mod(emod, mi);
+    const uint64_t g = e64 * inv;
     t.F[i] = static_cast<uint32_t>(((static_cast<uint64_t>(inv) << 31) + mi / 2) / mi);
-    t.G[i] = e64 * inv;
-    c0 += 128ull * t.G[i];
+    t.Glo[i] = static_cast<uint32_t>(g);
+    t.Ghi[i] = static_cast<uint32_t>(g >> 32);
+    c0 += 128ull * g;
     sf += 128ll * t.F[i];
   }
-  t.C0 = c0;
+  t.C0 = c0 - static_cast<uint64_t>(kQuotientBias) * m64;
   t.sumF128 = sf;
   return t;
 }
 
-// Per-call thresholds in units of 2^-31 of M. Accepting |frac| <= t_in
-// implies the quotient is right and the value is in range; |frac| >= t_out
-// implies it is out of range; the band between goes to the exact path. A
-// wrong quotient needs |frac| >= 2^30 - err, which exceeds t_in because the
-// bound is below M/2 (signed) or M (unsigned).
+// Per-call constants in units of 2^-31 of M. The device sum starts at s_init =
+// 2^30 + kQuotientBias * 2^31 - (128 * sum F_i + center), so that s >> 31 is
+// the rounded quotient plus the bias and the low 31 bits minus 2^30 are the
+// signed fraction. Accepting |frac| <= t_in implies the quotient is right and
+// the value is in range; |frac| >= t_out implies it is out of range; the band
+// between goes to the exact path. A wrong quotient needs |frac| >= 2^30 - err,
+// which exceeds t_in because the bound is below M/2 (signed) or M (unsigned).
 struct FracLimits {
   int enabled;      // 0: use the exact path for every cell
-  int64_t offset;   // 128 * sum F_i + center of the accepted interval
-  int64_t t_in;     // |fraction| <= t_in: in range
-  int64_t t_out;    // |fraction| >= t_out: out of range
+  uint32_t t_in;
+  uint32_t t_out;
+  uint64_t s_init;
 };
 
 // 1 = value written to *out, 0 = out of range, -1 = undecided (use exact path).
+// u_i = r_i + 128.
 template <int P>
 __device__ __forceinline__ int frac_reconstruct(const uint32_t (&u)[P], const FracLimits& fl, uint64_t* out) {
   constexpr FracTable<P> T = make_frac_table<P>();
-  int64_t s = -fl.offset;
-  uint64_t v = 0ull - T.C0;
+  uint64_t s = fl.s_init;
+  uint64_t vl = 0;
+  uint32_t vh = 0;
 #pragma unroll
   for (int i = 0; i < P; ++i) {
-    s += static_cast<int64_t>(static_cast<uint64_t>(u[i]) * T.F[i]);
-    v += static_cast<uint64_t>(u[i]) * T.G[i];
+    s += static_cast<uint64_t>(u[i]) * T.F[i];
+    vl += static_cast<uint64_t>(u[i]) * T.Glo[i];
+    vh += u[i] * T.Ghi[i];
   }
-  const int64_t q = (s + (1ll << 30)) >> 31;
-  const int64_t frac = s - q * (1ll << 31);
-  const int64_t afrac = frac < 0 ? -frac : frac;
+  const uint32_t s_lo = static_cast<uint32_t>(s);
+  const uint32_t q = __funnelshift_r(s_lo, static_cast<uint32_t>(s >> 32), 31);
+  const int32_t frac = static_cast<int32_t>(s_lo & 0x7FFFFFFFu) - (1 << 30);
+  const uint32_t afrac = static_cast<uint32_t>(frac < 0 ? -frac : frac);
   if (afrac >= fl.t_out) return 0;
   if (afrac > fl.t_in) return -1;
-  v -= static_cast<uint64_t>(q) * T.M64;
-  *out = v;
+  *out = vl + (static_cast<uint64_t>(vh) << 32) - T.C0 - static_cast<uint64_t>(q) * T.M64;
   return 1;
 }
 
@@ -309,16 +319,17 @@ inline FracLimits host_frac_limits(uint32_t prefix, uint64_t bound, bool is_sign
   for (int l = 3; l >= 0; --l) M = (M << 32) | prod[l];
   const unsigned __int128 num = static_cast<unsigned __int128>(bound) << 31;
   const unsigned __int128 den = is_signed ? M : 2 * M;
-  const int64_t w = static_cast<int64_t>(num / den);
+  const int64_t w = static_cast<int64_t>(num / den);  // < 2^30: bound < M/2 (signed) or M (unsigned)
   const int64_t center = is_signed ? 0 : static_cast<int64_t>((num + M) / (2 * M));  // round(2^31 * bound / 2M)
   const int64_t err = 64 * static_cast<int64_t>(prefix) + 2;
-  fl.offset = sum_f128 + center;
-  fl.t_in = w - err - 1;
-  fl.t_out = w + err + 1;
-  fl.enabled = fl.t_in > 4 * err ? 1 : 0;
+  if (w - err - 1 <= 4 * err) return fl;
   // A signed bound of 2^63 admits -2^63 but not +2^63, an asymmetry the
   // fraction does not see: such calls take the exact path.
-  if (is_signed && bound > 0x7FFFFFFFFFFFFFFFull) fl.enabled = 0;
+  if (is_signed && bound > 0x7FFFFFFFFFFFFFFFull) return fl;
+  fl.enabled = 1;
+  fl.t_in = static_cast<uint32_t>(w - err - 1);
+  fl.t_out = static_cast<uint32_t>(w + err + 1);
+  fl.s_init = (1ull << 30) + (static_cast<uint64_t>(kQuotientBias) << 31) - static_cast<uint64_t>(sum_f128 + center);
   return fl;
 }
 

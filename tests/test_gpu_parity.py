@@ -212,6 +212,11 @@ def test_gemm_export_bounded_matches_oracle(lib, oracle, m, n, k, prefix, signed
     # A bound the values exceed: RANGE_ERROR through the status word.
     st, _, word = run_gemm_export(lib, a, b, prefix, 1, signed)
     assert st == OK and word == RANGE
+    # Strided destination: cells land at row * ld + col, the padding is untouched.
+    st, got, word = run_gemm_export(lib, a, b, prefix, bound, signed, ld=n + 6)
+    assert st == OK and word == 0
+    np.testing.assert_array_equal(got[:, :n], want)
+    assert (got[:, n:].astype(np.int64) == -7).all()
 
 
 # ---- export -------------------------------------------------------------------------
