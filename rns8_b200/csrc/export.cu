@@ -266,14 +266,40 @@ int64_t frac_sum_f128(uint32_t prefix) {
   }
 }
 
+// Centered -> canonical: r < 0 ? r + m : r, on four packed bytes. The sign
+// bit of each byte selects whether m is added; the per-byte add wraps modulo
+// 256 (a negative residue is stored as 256 + r, and 256 + r + m = r + m mod
+// 256), so no carry crosses into the next byte.
+__device__ __forceinline__ uint32_t canonical4(uint32_t w, uint32_t m4) {
+  const uint32_t neg = (w >> 7) & 0x01010101u;  // 1 in every byte holding a negative residue
+  return __vadd4(w, neg * 0xFFu & m4);          // add m to exactly those bytes
+}
+
+// Contiguous rows (ld == n): 16 cells per thread, one 16-byte load and store.
+__global__ void __launch_bounds__(256) export_u8_vec16_kernel(const uint4* __restrict__ res, int64_t groups,
+                                                              uint32_t modulus, uint4* __restrict__ dst) {
+  const uint32_t m4 = (modulus & 0xFFu) * 0x01010101u;  // m = 256 adds 0: the byte already is r mod 256
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < groups;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint4 v = __ldcs(res + i);
+    v.x = canonical4(v.x, m4);
+    v.y = canonical4(v.y, m4);
+    v.z = canonical4(v.z, m4);
+    v.w = canonical4(v.w, m4);
+    __stcs(dst + i, v);
+  }
+}
+
+// General layout: one thread per cell of a 2-D grid (x over columns, y over
+// rows), so no division per cell.
 __global__ void __launch_bounds__(256) export_u8_kernel(const int8_t* __restrict__ res, int64_t m, int64_t n,
                                                         uint32_t modulus, uint8_t* __restrict__ dst, int64_t ld) {
-  const int64_t cells = m * n;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < cells;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i / n, col = i - row * n;
-    const int r = res[i];
-    dst[row * ld + col] = static_cast<uint8_t>(r < 0 ? r + static_cast<int>(modulus) : r);
+  for (int64_t row = blockIdx.y; row < m; row += gridDim.y) {
+    for (int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; col < n;
+         col += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int r = res[row * n + col];
+      dst[row * ld + col] = static_cast<uint8_t>(r < 0 ? r + static_cast<int>(modulus) : r);
+    }
   }
 }
 
@@ -324,10 +350,22 @@ cudaError_t export_limbs(const int8_t* planes, int64_t m, int64_t n, uint32_t pr
 
 cudaError_t export_finite_u8(const int8_t* residues, int64_t m, int64_t n, uint32_t modulus, uint8_t* dst, int64_t ld,
                              cudaStream_t stream) {
-  int64_t blocks = (m * n + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
-  if (blocks < 1) blocks = 1;
-  export_u8_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(residues, m, n, modulus, dst, ld);
+  const int64_t cells = m * n;
+  if (ld == n && cells % 16 == 0 && reinterpret_cast<uintptr_t>(residues) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(dst) % 16 == 0) {
+    const int64_t groups = cells / 16;
+    int64_t blocks = (groups + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    if (blocks < 1) blocks = 1;
+    export_u8_vec16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        reinterpret_cast<const uint4*>(residues), groups, modulus, reinterpret_cast<uint4*>(dst));
+    return cudaGetLastError();
+  }
+  int64_t bx = (n + 255) / 256;
+  if (bx > 64) bx = 64;
+  const int64_t by = m < 65535 ? m : 65535;
+  export_u8_kernel<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(by)), 256, 0, stream>>>(residues, m, n,
+                                                                                                    modulus, dst, ld);
   return cudaGetLastError();
 }
 

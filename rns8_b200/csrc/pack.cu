@@ -155,38 +155,60 @@ cudaError_t dispatch_pack(const T* src, int64_t rows, int64_t cols, int64_t ld, 
 }
 
 // Finite u8: residues of bytes modulo an arbitrary m in [2, 256].
+enum class U8Kind : int {
+  General = 0,   // m < 128: magic-multiply modulo per byte
+  OneStep = 1,   // 128 <= m < 256: a byte needs at most one subtraction of m
+  Identity = 2,  // m = 256: the byte read as int8 is the centered residue
+};
+
+template <U8Kind kKind>
+__device__ __forceinline__ uint32_t residues4(uint32_t x, uint32_t m, uint32_t magic, uint32_t m4, uint32_t h4) {
+  if constexpr (kKind == U8Kind::Identity) {
+    return x;
+  } else if constexpr (kKind == U8Kind::OneStep) {
+    // Per byte: t = x >= m ? x - m : x, then t >= ceil(m/2) ? t - m : t
+    // (mod 256, i.e. the int8 of the centered residue).
+    const uint32_t t = __vsub4(x, __vcmpgeu4(x, m4) & m4);
+    return __vsub4(t, __vcmpgeu4(t, h4) & m4);
+  } else {
+    uint32_t r[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) r[b] = static_cast<uint32_t>(center_residue(umod_u32((x >> (8 * b)) & 0xFFu, m, magic), m));
+    return pack4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+// 16 bytes per thread; grid.x over the 16-byte groups of a row, grid.y over
+// rows (a contiguous matrix is passed as one row), so no division per group.
+template <U8Kind kKind>
 __global__ void __launch_bounds__(256) pack_u8_vec16_kernel(const uint8_t* __restrict__ src, int64_t rows,
                                                             int64_t cols, int64_t ld, uint32_t m, uint32_t magic,
                                                             int8_t* __restrict__ out) {
-  const int64_t groups_per_row = cols >> 4;
-  const int64_t total = rows * groups_per_row;
-  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
-       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = g / groups_per_row;
-    const int64_t col = (g - row * groups_per_row) << 4;
-    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + row * ld + col));
-    uint32_t words[4] = {v.x, v.y, v.z, v.w};
-    uint4 o;
-    uint32_t* ow = &o.x;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      uint32_t r[4];
-#pragma unroll
-      for (int b = 0; b < 4; ++b)
-        r[b] = static_cast<uint32_t>(center_residue(umod_u32((words[w] >> (8 * b)) & 0xFFu, m, magic), m));
-      ow[w] = pack4(r[0], r[1], r[2], r[3]);
+  const int64_t groups = cols >> 4;
+  const uint32_t m4 = (m & 0xFFu) * 0x01010101u;
+  const uint32_t h4 = ((m + 1) / 2) * 0x01010101u;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const uint4* s = reinterpret_cast<const uint4*>(src + row * ld);
+    uint4* o = reinterpret_cast<uint4*>(out + row * cols);
+    for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
+         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      uint4 v = __ldcs(s + g);
+      v.x = residues4<kKind>(v.x, m, magic, m4, h4);
+      v.y = residues4<kKind>(v.y, m, magic, m4, h4);
+      v.z = residues4<kKind>(v.z, m, magic, m4, h4);
+      v.w = residues4<kKind>(v.w, m, magic, m4, h4);
+      __stcs(o + g, v);
     }
-    *reinterpret_cast<uint4*>(out + row * cols + col) = o;
   }
 }
+
 __global__ void __launch_bounds__(256) pack_u8_scalar_kernel(const uint8_t* __restrict__ src, int64_t rows,
                                                              int64_t cols, int64_t ld, uint32_t m, uint32_t magic,
                                                              int8_t* __restrict__ out) {
-  const int64_t total = rows * cols;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i / cols, col = i - row * cols;
-    out[i] = static_cast<int8_t>(center_residue(umod_u32(src[row * ld + col], m, magic), m));
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    for (int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; col < cols;
+         col += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      out[row * cols + col] = static_cast<int8_t>(center_residue(umod_u32(src[row * ld + col], m, magic), m));
   }
 }
 
@@ -204,18 +226,28 @@ cudaError_t pack_finite_u8(const uint8_t* src, int64_t rows, int64_t cols, int64
                            int8_t* residues, cudaStream_t stream) {
   if (modulus < 2 || modulus > 256) return cudaErrorInvalidValue;
   const uint32_t magic = floor_magic(modulus);
+  if (ld == cols) {  // contiguous: one long row
+    cols *= rows;
+    ld = cols;
+    rows = 1;
+  }
   const bool vec = (cols % 16 == 0) && (ld % 16 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(residues) % 16 == 0);
-  const int64_t work = vec ? rows * (cols / 16) : rows * cols;
-  int64_t blocks = (work + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  if (blocks < 1) blocks = 1;
-  if (vec)
-    pack_u8_vec16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, rows, cols, ld, modulus, magic,
-                                                                            residues);
+  const int64_t per_row = vec ? cols / 16 : cols;
+  int64_t bx = (per_row + 255) / 256;
+  const int64_t by = rows < 65535 ? rows : 65535;
+  const int64_t max_x = (148 * 16 + by - 1) / by;  // about 16 blocks per SM in all
+  if (bx > max_x) bx = max_x;
+  if (bx < 1) bx = 1;
+  const dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(by));
+  if (!vec)
+    pack_u8_scalar_kernel<<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
+  else if (modulus == 256)
+    pack_u8_vec16_kernel<U8Kind::Identity><<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
+  else if (modulus >= 128)
+    pack_u8_vec16_kernel<U8Kind::OneStep><<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
   else
-    pack_u8_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, rows, cols, ld, modulus, magic,
-                                                                             residues);
+    pack_u8_vec16_kernel<U8Kind::General><<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
   return cudaGetLastError();
 }
 

@@ -71,8 +71,14 @@ def test_pack_i64_u64_match_oracle(lib, oracle, prefix, shape, ld):
         np.testing.assert_array_equal(host(d_out), want)
 
 
-@pytest.mark.parametrize("modulus", [2, 97, 251, 255, 256])
-@pytest.mark.parametrize("shape,ld", [((32, 64), 64), ((5, 9), 11)])
+U8_MODULI = [2, 97, 127, 128, 129, 251, 255, 256]   # per-byte modulo, one-subtraction, identity paths
+U8_SHAPES = [((32, 64), 64),    # contiguous: 16-byte groups over the flattened matrix
+             ((16, 48), 64),    # strided rows, 16-byte groups per row
+             ((5, 9), 11)]      # ragged: one byte per thread
+
+
+@pytest.mark.parametrize("modulus", U8_MODULI)
+@pytest.mark.parametrize("shape,ld", U8_SHAPES)
 def test_pack_finite_u8_matches_oracle(lib, oracle, modulus, shape, ld):
     rng = np.random.default_rng(modulus)
     src = rng.integers(0, 256, (shape[0], ld), dtype=np.uint8)
@@ -83,6 +89,24 @@ def test_pack_finite_u8_matches_oracle(lib, oracle, modulus, shape, ld):
                                                d_out.data_ptr(), stream()) == OK
     torch.cuda.synchronize()
     np.testing.assert_array_equal(host(d_out), want)
+
+
+@pytest.mark.parametrize("modulus", U8_MODULI)
+@pytest.mark.parametrize("shape,ld", U8_SHAPES)
+def test_export_finite_u8_canonical(lib, oracle, modulus, shape, ld):
+    """Centered residues -> canonical bytes (cpu_reference.cpp:132-153); padding untouched."""
+    rng = np.random.default_rng(modulus + ld)
+    src = rng.integers(0, 256, shape, dtype=np.uint8)
+    res = oracle.pack_finite_u8(src, modulus)
+    want = (src.astype(np.int64) % modulus).astype(np.uint8)
+    d_res = dev(res)
+    d_out = torch.full((shape[0], ld), 7, dtype=torch.uint8, device="cuda")
+    assert lib.rns8_cuda_export_finite_u8_device(0, d_res.data_ptr(), shape[0], shape[1], modulus,
+                                                 d_out.data_ptr(), ld, stream()) == OK
+    torch.cuda.synchronize()
+    got = host(d_out)
+    np.testing.assert_array_equal(got[:, : shape[1]], want)
+    assert (got[:, shape[1]:] == 7).all()
 
 
 # ---- plane GEMM -------------------------------------------------------------------
