@@ -459,7 +459,7 @@ class EndToEnd:
             self.nA, self.nB = self.hA.numpy(), self.hB.numpy()
             self.nC = self.hC.numpy().view("uint64")
             self.api = ("rns8_pack_i64 x 2, rns8_gemm_rns, rns8_export_exact_wide_signed_limbs "
-                        "(pinned host buffers; includes the host exact-range admission proof)")
+                        "(pinned host buffers; includes the exact-range admission proofs, computed on the device)")
         elem_in = 1 if cfg.kind == "finite" else 8
         self.h2d = cfg.batch * elem_in * (m * k + k * n)
         self.d2h = self.hC.numel() * self.hC.element_size()

@@ -122,6 +122,25 @@ RNS8_API rns8_status rns8_cuda_export_limbs_device(int device_id, const int8_t* 
 RNS8_API rns8_status rns8_cuda_export_finite_u8_device(int device_id, const int8_t* d_residues, int64_t m, int64_t n,
                                                        uint16_t modulus, uint8_t* d_dst, int64_t ld, void* stream);
 
+/* Exact-wide admission proof (reference src/core/exact_range.hpp:51-154 and
+ * api_pack.cpp:61-64) of A x B for native matrices already in device memory:
+ * A is m x k, B is k x n, both compact (ld = cols) int64 (is_signed = 1) or
+ * uint64 (0). Writes the admission bound (the smallest valid bound on every
+ * |C[r][c]|, maximised over the cells) to out_bound[4] and the largest |a|
+ * and |b| to out_a_max[4] / out_b_max[4], all 256-bit little-endian.
+ * out_row_stats[8*m] / out_col_stats[8*n], when not NULL, receive per output
+ * row / column the maximum and the sum of the cell bounds (4 + 4 limbs): the
+ * records an exact-wide GEMM keeps for its output. A GEMM is admitted when
+ * 2*bound < M_P (signed) or bound < M_P (unsigned). The reference computes
+ * this on the host inside pack and GEMM; here it runs on the device. Unlike
+ * the other calls in this header it allocates device scratch, synchronises
+ * `stream` and writes host memory. */
+RNS8_API rns8_status rns8_cuda_exact_gemm_bound_device(int device_id, const void* d_a, const void* d_b, int64_t m,
+                                                       int64_t n, int64_t k, uint32_t is_signed, uint64_t* out_bound,
+                                                       uint64_t* out_a_max, uint64_t* out_b_max,
+                                                       uint64_t* out_row_stats, uint64_t* out_col_stats,
+                                                       void* stream);
+
 /* Host-only: run the plan validation and prefix schedule of rns8_create_plan
  * for a descriptor without a context (no device needed). Writes the selected
  * and required prefix and the effective output bound on success. */

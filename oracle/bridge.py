@@ -48,6 +48,7 @@ _SIGS = {
                                               vp, i64, vp]),
     "oracle_gemm_finite_u8_oneshot": (C.c_int, [C.c_int, u16, i64, i64, i64, vp, i64, vp, i64, vp, i64]),
     "oracle_exact_gemm_admission": (C.c_int, [C.c_int, vp, i64, vp, i64, i64, i64, i64, u32, vp, vp, vp]),
+    "oracle_exact_gemm_cell_stats": (C.c_int, [C.c_int, vp, i64, vp, i64, i64, i64, i64, vp, vp]),
     "oracle_rng_new": (C.c_int, [u64]),
     "oracle_rng_free": (None, [C.c_int]),
     "oracle_rng_next": (u64, [C.c_int]),
@@ -228,6 +229,18 @@ def exact_gemm_admission(A: np.ndarray, B: np.ndarray, prefix: int) -> tuple[int
     st = lib().oracle_exact_gemm_admission(1 if A.dtype == np.int64 else 0, _p(A), _ld(A), _p(B), _ld(B), m, n, k,
                                            prefix, _p(bound), _p(amax), _p(bmax))
     return int(st), from_limbs4(bound)
+
+
+def exact_gemm_cell_stats(A: np.ndarray, B: np.ndarray) -> tuple[list[tuple[int, int]], list[tuple[int, int]]]:
+    """Per output row and column: (max, sum) of the exact-wide cell bounds."""
+    m, k = A.shape
+    n = B.shape[1]
+    rows = np.zeros((m, 8), np.uint64)
+    cols = np.zeros((n, 8), np.uint64)
+    lib().oracle_exact_gemm_cell_stats(1 if A.dtype == np.int64 else 0, _p(A), _ld(A), _p(B), _ld(B), m, n, k,
+                                       _p(rows), _p(cols))
+    pair = lambda v: (from_limbs4(v[:4]), from_limbs4(v[4:]))
+    return [pair(r) for r in rows], [pair(c) for c in cols]
 
 
 class Rng:

@@ -805,6 +805,41 @@ OX int oracle_exact_gemm_admission(int is_signed, const void* A, int64_t lda, co
   return fits(bound) ? ST_SUCCESS : ST_RANGE;
 }
 
+// The records an exact-wide GEMM keeps for its output (exact_range.hpp:108-143):
+// per output row and column, the maximum and the sum of the cell bounds.
+// row_stats[8*m], col_stats[8*n]: 4 limbs of the maximum, then 4 of the sum.
+OX int oracle_exact_gemm_cell_stats(int is_signed, const void* A, int64_t lda, const void* B, int64_t ldb, int64_t m,
+                                    int64_t n, int64_t k, uint64_t* row_stats, uint64_t* col_stats) {
+  std::vector<axis_range> ar, ac, br, bc;
+  wide256 amax, bmax;
+  if (is_signed) {
+    native_exact_ranges<int64_t>(static_cast<const int64_t*>(A), m, k, lda, ar, ac, amax);
+    native_exact_ranges<int64_t>(static_cast<const int64_t*>(B), k, n, ldb, br, bc, bmax);
+  } else {
+    native_exact_ranges<uint64_t>(static_cast<const uint64_t*>(A), m, k, lda, ar, ac, amax);
+    native_exact_ranges<uint64_t>(static_cast<const uint64_t*>(B), k, n, ldb, br, bc, bmax);
+  }
+  std::vector<wide256> rmax(static_cast<size_t>(m), w_zero()), rsum(static_cast<size_t>(m), w_zero());
+  std::vector<wide256> cmax(static_cast<size_t>(n), w_zero()), csum(static_cast<size_t>(n), w_zero());
+  for (int64_t r = 0; r < m; ++r)
+    for (int64_t c = 0; c < n; ++c) {
+      const wide256 b = axis_product_bound(ar[r], bc[c], k);
+      rmax[r] = w_max(rmax[r], b);
+      rsum[r] = w_add(rsum[r], b);
+      cmax[c] = w_max(cmax[c], b);
+      csum[c] = w_add(csum[c], b);
+    }
+  for (int64_t r = 0; r < m; ++r) {
+    write_w(rmax[r], row_stats + 8 * r);
+    write_w(rsum[r], row_stats + 8 * r + 4);
+  }
+  for (int64_t c = 0; c < n; ++c) {
+    write_w(cmax[c], col_stats + 8 * c);
+    write_w(csum[c], col_stats + 8 * c + 4);
+  }
+  return ST_SUCCESS;
+}
+
 // Seeded inputs: std::mt19937_64 + std::uniform_int_distribution, as the
 // reference's tests and benchmark generate them (rns8_bench_core_helpers.inc:
 // 1150-1166, test_bounded_reference_sweeps.cpp:209-243).

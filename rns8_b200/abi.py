@@ -244,6 +244,7 @@ SIGNATURES = {
     "rns8_cuda_export_limbs_device": (c_status, [C.c_int, vp, i64, i64, u32, u32, u32, vp, i64, vp, vp]),
     "rns8_cuda_export_finite_u8_device": (c_status, [C.c_int, vp, i64, i64, u16, vp, i64, vp]),
     "rns8_cuda_plan_probe": (c_status, [vp, P(u32), P(u32), P(u64)]),
+    "rns8_cuda_exact_gemm_bound_device": (c_status, [C.c_int, vp, vp, i64, i64, i64, u32, vp, vp, vp, vp, vp, vp]),
 }
 
 _LIB: C.CDLL | None = None

@@ -7,10 +7,10 @@
 // RNS8_RANGE_ERROR unless the largest cell bound fits the prefix (signed:
 // 2*bound < P; unsigned: bound < P). The arithmetic is exact: 128-bit
 // accumulators for the summaries, 256-bit for products, with cpp_int's
-// truncation toward zero for the axis centers. Work is split over host
-// threads by rows.
+// truncation toward zero for the axis centers. The summaries and the cell
+// bounds run on the device (exact_range.cu); the host keeps the per-axis
+// records and the final comparisons.
 #include <algorithm>
-#include <thread>
 #include <vector>
 
 #include "api_internal.hpp"
@@ -18,119 +18,41 @@
 namespace rns8host {
 namespace {
 
-unsigned worker_count(int64_t units) {
-  unsigned hw = std::thread::hardware_concurrency();
-  if (hw == 0) hw = 4;
-  if (hw > 32) hw = 32;
-  const int64_t by_work = units / 4096 + 1;
-  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(hw, by_work)));
+AxisRange to_axis(const rns8cuda::AxisSummary& s) {
+  AxisRange a;
+  a.max_magnitude = i256::from_u128(s.max_mag);
+  a.absolute_sum = i256::from_u128(s.abs_sum);
+  a.sum = i256::from_i128(s.sum);
+  a.minimum = i256::from_i128(s.minimum);
+  a.maximum = i256::from_i128(s.maximum);
+  a.deviation_sum = i256::from_u128(s.dev_sum);
+  a.sum_known = s.any != 0;
+  return a;
 }
 
-template <typename F>
-void parallel_rows(int64_t rows, F&& body) {
-  const unsigned workers = worker_count(rows * 64);
-  if (workers <= 1) {
-    body(0, rows, 0u);
-    return;
-  }
-  std::vector<std::thread> pool;
-  const int64_t chunk = (rows + workers - 1) / workers;
-  for (unsigned w = 0; w < workers; ++w) {
-    const int64_t r0 = w * chunk, r1 = std::min(rows, r0 + chunk);
-    if (r0 >= r1) break;
-    pool.emplace_back([&body, r0, r1, w] { body(r0, r1, w); });
-  }
-  for (auto& t : pool) t.join();
+void put(uint64_t (&dst)[4], const i256& v) {
+  for (int l = 0; l < 4; ++l) dst[l] = v.w[l];
 }
-
-// 128-bit accumulation of one axis while scanning.
-struct Acc {
-  unsigned __int128 max_mag = 0, abs_sum = 0, dev_sum = 0;
-  __int128 sum = 0, minimum = 0, maximum = 0;
-  bool any = false;
-  void add(__int128 v) {
-    const unsigned __int128 mag = v < 0 ? static_cast<unsigned __int128>(-v) : static_cast<unsigned __int128>(v);
-    if (mag > max_mag) max_mag = mag;
-    abs_sum += mag;
-    sum += v;
-    if (!any) {
-      minimum = maximum = v;
-      any = true;
-    } else {
-      if (v < minimum) minimum = v;
-      if (v > maximum) maximum = v;
-    }
-  }
-  void merge(const Acc& o) {
-    if (!o.any) return;
-    if (o.max_mag > max_mag) max_mag = o.max_mag;
-    abs_sum += o.abs_sum;
-    sum += o.sum;
-    dev_sum += o.dev_sum;
-    if (!any) {
-      minimum = o.minimum;
-      maximum = o.maximum;
-      any = true;
-    } else {
-      minimum = std::min(minimum, o.minimum);
-      maximum = std::max(maximum, o.maximum);
-    }
-  }
-  // (min + max) / 2 rounded toward zero.
-  __int128 center() const { return (minimum + maximum) / 2; }
-  AxisRange to_axis() const {
-    AxisRange a;
-    a.max_magnitude = i256::from_u128(max_mag);
-    a.absolute_sum = i256::from_u128(abs_sum);
-    a.sum = i256::from_i128(sum);
-    a.minimum = i256::from_i128(minimum);
-    a.maximum = i256::from_i128(maximum);
-    a.deviation_sum = i256::from_u128(dev_sum);
-    a.sum_known = any;
-    return a;
-  }
-};
-
-inline unsigned __int128 absdiff(__int128 a, __int128 b) {
-  return a >= b ? static_cast<unsigned __int128>(a - b) : static_cast<unsigned __int128>(b - a);
-}
-
-i256 axis_center(const AxisRange& a) { return half_trunc(a.minimum + a.maximum); }
-i256 axis_dev_max(const AxisRange& a, const i256& c) { return max(abs(a.minimum - c), abs(a.maximum - c)); }
-void tighten(i256& bound, const i256& cand) {
-  if (cand < bound) bound = cand;
+i256 get(const uint64_t (&src)[4]) {
+  i256 v;
+  for (int l = 0; l < 4; ++l) v.w[l] = src[l];
+  return v;
 }
 
 // Per-axis quantities reused for every cell (exact_range.hpp:79-98).
-struct AxisPre {
-  const AxisRange* axis;
-  i256 center, dev_max;
-};
-AxisPre precompute(const AxisRange& a) {
-  AxisPre p;
-  p.axis = &a;
+rns8cuda::AxisBoundInput bound_input(const AxisRange& a) {
+  rns8cuda::AxisBoundInput in{};
+  put(in.max_mag, a.max_magnitude);
+  put(in.abs_sum, a.absolute_sum);
+  put(in.sum, a.sum);
+  put(in.dev_sum, a.deviation_sum);
+  in.sum_known = a.sum_known ? 1 : 0;
   if (a.sum_known) {
-    p.center = axis_center(a);
-    p.dev_max = axis_dev_max(a, p.center);
+    const i256 center = half_trunc(a.minimum + a.maximum);
+    put(in.center, center);
+    put(in.dev_max, max(abs(a.minimum - center), abs(a.maximum - center)));
   }
-  return p;
-}
-
-i256 axis_product_bound(const AxisPre& pa, const AxisPre& pb, const i256& k) {
-  const AxisRange& a = *pa.axis;
-  const AxisRange& b = *pb.axis;
-  i256 bound = k * a.max_magnitude * b.max_magnitude;
-  tighten(bound, a.absolute_sum * b.max_magnitude);
-  tighten(bound, a.max_magnitude * b.absolute_sum);
-  if (a.sum_known && b.sum_known) {
-    i256 rem = k * pa.dev_max * pb.dev_max;
-    tighten(rem, a.deviation_sum * pb.dev_max);
-    tighten(rem, pa.dev_max * b.deviation_sum);
-    // dot(a,b) = ca*sum(b) + cb*sum(a) - K*ca*cb + dot(a-ca, b-cb)
-    const i256 center_term = pa.center * b.sum + pb.center * a.sum - k * pa.center * pb.center;
-    tighten(bound, abs(center_term) + rem);
-  }
-  return bound;
+  return in;
 }
 
 AxisRange uniform_axis(const i256& maximum, int64_t length) {
@@ -141,6 +63,26 @@ AxisRange uniform_axis(const i256& maximum, int64_t length) {
   return a;
 }
 
+uint64_t round256(uint64_t v) { return (v + 255) / 256 * 256; }
+
+// Carves consecutive 256-byte aligned pieces out of the context's admission
+// buffer; the caller holds admission_mutex.
+struct AdmissionArena {
+  rns8_context& ctx;
+  uint8_t* base = nullptr;
+  uint64_t used = 0;
+  rns8_status reserve(uint64_t bytes) {
+    const rns8_status st = ctx.admission.ensure(ctx.device_id, bytes);
+    base = static_cast<uint8_t*>(ctx.admission.ptr);
+    return st;
+  }
+  void* take(uint64_t bytes) {
+    void* p = base + used;
+    used += round256(bytes);
+    return p;
+  }
+};
+
 }  // namespace
 
 bool exact_range_fits(rns8_semantics s, const i256& bound, const i256& product) {
@@ -148,118 +90,107 @@ bool exact_range_fits(rns8_semantics s, const i256& bound, const i256& product) 
   return s == RNS8_EXACT_WIDE_SIGNED ? (bound * i256::from_u64(2)) < product : bound < product;
 }
 
-template <typename T>
-void native_exact_ranges(const T* src, int64_t rows, int64_t cols, int64_t ld, ExactRanges& out, i256& maximum) {
-  std::vector<Acc> row_acc(static_cast<size_t>(rows));
-  const unsigned workers = worker_count(rows * 64);
-  std::vector<std::vector<Acc>> col_part(workers, std::vector<Acc>(static_cast<size_t>(cols)));
-  parallel_rows(rows, [&](int64_t r0, int64_t r1, unsigned w) {
-    auto& cp = col_part[w];
-    for (int64_t r = r0; r < r1; ++r) {
-      Acc& ra = row_acc[r];
-      const T* line = src + r * ld;
-      for (int64_t c = 0; c < cols; ++c) {
-        const __int128 v = static_cast<__int128>(line[c]);
-        ra.add(v);
-        cp[c].add(v);
-      }
-    }
-  });
-  std::vector<Acc> col_acc(static_cast<size_t>(cols));
-  for (auto& cp : col_part)
-    for (int64_t c = 0; c < cols; ++c) col_acc[c].merge(cp[c]);
-  // Second scan: L1 distance of every value from its row and column centers.
-  for (auto& cp : col_part)
-    for (auto& a : cp) a.dev_sum = 0;
-  std::vector<__int128> col_center(static_cast<size_t>(cols));
-  for (int64_t c = 0; c < cols; ++c) col_center[c] = col_acc[c].center();
-  parallel_rows(rows, [&](int64_t r0, int64_t r1, unsigned w) {
-    auto& cp = col_part[w];
-    for (int64_t r = r0; r < r1; ++r) {
-      Acc& ra = row_acc[r];
-      const __int128 rc = ra.center();
-      const T* line = src + r * ld;
-      for (int64_t c = 0; c < cols; ++c) {
-        const __int128 v = static_cast<__int128>(line[c]);
-        ra.dev_sum += absdiff(v, rc);
-        cp[c].dev_sum += absdiff(v, col_center[c]);
-      }
-    }
-  });
-  for (int64_t c = 0; c < cols; ++c) {
-    unsigned __int128 d = 0;
-    for (auto& cp : col_part) d += cp[c].dev_sum;
-    col_acc[c].dev_sum = d;
-  }
+rns8_status device_exact_ranges(rns8_context& ctx, const void* d_src, bool is_signed, int64_t rows, int64_t cols,
+                                ExactRanges& out, i256& maximum) {
+  if (cudaSetDevice(ctx.device_id) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  std::lock_guard<std::mutex> lock(ctx.admission_mutex);
+  using rns8cuda::AxisSummary;
+  const uint64_t row_bytes = static_cast<uint64_t>(rows) * sizeof(AxisSummary);
+  const uint64_t col_bytes = static_cast<uint64_t>(cols) * sizeof(AxisSummary);
+  const uint64_t scratch = rns8cuda::axis_summaries_scratch_bytes(rows, cols);
+  AdmissionArena arena{ctx};
+  rns8_status st = arena.reserve(round256(row_bytes) + round256(col_bytes) + round256(scratch));
+  if (st != RNS8_SUCCESS) return st;
+  auto* d_rows = static_cast<AxisSummary*>(arena.take(row_bytes));
+  auto* d_cols = static_cast<AxisSummary*>(arena.take(col_bytes));
+  void* d_scratch = arena.take(scratch);
+  if (rns8cuda::axis_summaries(d_src, is_signed, rows, cols, d_rows, d_cols, d_scratch, scratch, ctx.stream) !=
+      cudaSuccess)
+    return RNS8_BACKEND_FAILURE;
+  std::vector<AxisSummary> h_rows(static_cast<size_t>(rows)), h_cols(static_cast<size_t>(cols));
+  if (cudaMemcpyAsync(h_rows.data(), d_rows, row_bytes, cudaMemcpyDeviceToHost, ctx.stream) != cudaSuccess ||
+      cudaMemcpyAsync(h_cols.data(), d_cols, col_bytes, cudaMemcpyDeviceToHost, ctx.stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx.stream) != cudaSuccess)
+    return RNS8_BACKEND_FAILURE;
   out.rows.resize(static_cast<size_t>(rows));
   out.cols.resize(static_cast<size_t>(cols));
   unsigned __int128 best = 0;
   for (int64_t r = 0; r < rows; ++r) {
-    out.rows[r] = row_acc[r].to_axis();
-    best = std::max(best, row_acc[r].max_mag);
+    out.rows[r] = to_axis(h_rows[r]);
+    best = std::max(best, h_rows[r].max_mag);
   }
-  for (int64_t c = 0; c < cols; ++c) out.cols[c] = col_acc[c].to_axis();
+  for (int64_t c = 0; c < cols; ++c) out.cols[c] = to_axis(h_cols[c]);
   maximum = i256::from_u128(best);
+  return RNS8_SUCCESS;
 }
 
-template void native_exact_ranges<int64_t>(const int64_t*, int64_t, int64_t, int64_t, ExactRanges&, i256&);
-template void native_exact_ranges<uint64_t>(const uint64_t*, int64_t, int64_t, int64_t, ExactRanges&, i256&);
-
-// exact_gemm_bound + exact_gemm_range (exact_range.hpp:109-154).
-rns8_status exact_gemm_range(const rns8_plan& plan, const rns8_matrix& A, const rns8_matrix& B, i256& bound,
-                             ExactRanges* out_ranges) {
-  if (!exact_wide(plan.desc.semantics)) return RNS8_SUCCESS;
-  if (A.exact_range_prefix < plan.prefix || B.exact_range_prefix < plan.prefix) return RNS8_RANGE_ERROR;
-  const int64_t m = plan.desc.m, n = plan.desc.n;
-  const i256 k = i256::from_i64(plan.desc.k);
-  const bool a_rows = A.exact_axes.rows.size() == static_cast<size_t>(m);
-  const bool b_cols = B.exact_axes.cols.size() == static_cast<size_t>(n);
-  bound = k * A.exact_max_magnitude * B.exact_max_magnitude;
+// exact_gemm_bound (exact_range.hpp:109-144).
+rns8_status exact_gemm_bound(rns8_context& ctx, int64_t m, int64_t n, int64_t k, const i256& a_max,
+                             const std::vector<AxisRange>* a_rows, const i256& b_max,
+                             const std::vector<AxisRange>* b_cols, i256& bound, ExactRanges* out_ranges) {
+  const i256 kk = i256::from_i64(k);
+  bound = kk * a_max * b_max;
   if (out_ranges) {
     out_ranges->rows.clear();
     out_ranges->cols.clear();
   }
-  if (a_rows || b_cols) {
-    const AxisRange fa = uniform_axis(A.exact_max_magnitude, plan.desc.k);
-    const AxisRange fb = uniform_axis(B.exact_max_magnitude, plan.desc.k);
-    std::vector<AxisPre> pa(static_cast<size_t>(m)), pb(static_cast<size_t>(n));
-    for (int64_t r = 0; r < m; ++r) pa[r] = precompute(a_rows ? A.exact_axes.rows[r] : fa);
-    for (int64_t c = 0; c < n; ++c) pb[c] = precompute(b_cols ? B.exact_axes.cols[c] : fb);
-    const unsigned workers = worker_count(m * 64);
-    std::vector<i256> part_max(workers);
-    std::vector<std::vector<AxisRange>> col_part(out_ranges ? workers : 0, std::vector<AxisRange>(static_cast<size_t>(n)));
-    if (out_ranges) out_ranges->rows.resize(static_cast<size_t>(m));
-    parallel_rows(m, [&](int64_t r0, int64_t r1, unsigned w) {
-      i256 best;
-      for (int64_t r = r0; r < r1; ++r) {
-        AxisRange rr;
-        for (int64_t c = 0; c < n; ++c) {
-          const i256 b = axis_product_bound(pa[r], pb[c], k);
-          best = max(best, b);
-          if (out_ranges) {
-            rr.max_magnitude = max(rr.max_magnitude, b);
-            rr.absolute_sum = rr.absolute_sum + b;
-            AxisRange& cr = col_part[w][c];
-            cr.max_magnitude = max(cr.max_magnitude, b);
-            cr.absolute_sum = cr.absolute_sum + b;
-          }
-        }
-        if (out_ranges) out_ranges->rows[r] = rr;
-      }
-      part_max[w] = best;
-    });
-    i256 maximum;
-    for (const auto& v : part_max) maximum = max(maximum, v);
-    if (out_ranges) {
-      out_ranges->cols.resize(static_cast<size_t>(n));
-      for (auto& cp : col_part)
-        for (int64_t c = 0; c < n; ++c) {
-          out_ranges->cols[c].max_magnitude = max(out_ranges->cols[c].max_magnitude, cp[c].max_magnitude);
-          out_ranges->cols[c].absolute_sum = out_ranges->cols[c].absolute_sum + cp[c].absolute_sum;
-        }
+  if (!a_rows && !b_cols) return RNS8_SUCCESS;
+  using rns8cuda::AxisBoundInput;
+  using rns8cuda::BoundStats;
+  std::vector<AxisBoundInput> h_in(static_cast<size_t>(m + n));
+  const AxisRange fa = uniform_axis(a_max, k);
+  const AxisRange fb = uniform_axis(b_max, k);
+  for (int64_t r = 0; r < m; ++r) h_in[r] = bound_input(a_rows ? (*a_rows)[r] : fa);
+  for (int64_t c = 0; c < n; ++c) h_in[m + c] = bound_input(b_cols ? (*b_cols)[c] : fb);
+  if (cudaSetDevice(ctx.device_id) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  std::lock_guard<std::mutex> lock(ctx.admission_mutex);
+  const uint64_t in_bytes = static_cast<uint64_t>(m + n) * sizeof(AxisBoundInput);
+  const uint64_t stat_bytes = static_cast<uint64_t>(m + n) * sizeof(BoundStats);
+  const uint64_t scratch = rns8cuda::cell_bounds_scratch_bytes(m, n);
+  AdmissionArena arena{ctx};
+  rns8_status st = arena.reserve(round256(in_bytes) + round256(stat_bytes) + round256(scratch));
+  if (st != RNS8_SUCCESS) return st;
+  auto* d_in = static_cast<AxisBoundInput*>(arena.take(in_bytes));
+  auto* d_stats = static_cast<BoundStats*>(arena.take(stat_bytes));
+  void* d_scratch = arena.take(scratch);
+  if (cudaMemcpyAsync(d_in, h_in.data(), in_bytes, cudaMemcpyHostToDevice, ctx.stream) != cudaSuccess ||
+      rns8cuda::cell_bounds(d_in, m, d_in + m, n, k, d_stats, d_stats + m, d_scratch, scratch, ctx.stream) !=
+          cudaSuccess)
+    return RNS8_BACKEND_FAILURE;
+  std::vector<BoundStats> h_stats(static_cast<size_t>(m + n));
+  if (cudaMemcpyAsync(h_stats.data(), d_stats, stat_bytes, cudaMemcpyDeviceToHost, ctx.stream) != cudaSuccess ||
+      cudaStreamSynchronize(ctx.stream) != cudaSuccess)
+    return RNS8_BACKEND_FAILURE;
+  i256 maximum;
+  for (int64_t r = 0; r < m; ++r) maximum = max(maximum, get(h_stats[r].max));
+  if (out_ranges) {
+    out_ranges->rows.resize(static_cast<size_t>(m));
+    out_ranges->cols.resize(static_cast<size_t>(n));
+    for (int64_t r = 0; r < m; ++r) {
+      out_ranges->rows[r].max_magnitude = get(h_stats[r].max);
+      out_ranges->rows[r].absolute_sum = get(h_stats[r].sum);
     }
-    tighten(bound, maximum);
+    for (int64_t c = 0; c < n; ++c) {
+      out_ranges->cols[c].max_magnitude = get(h_stats[m + c].max);
+      out_ranges->cols[c].absolute_sum = get(h_stats[m + c].sum);
+    }
   }
+  if (maximum < bound) bound = maximum;
+  return RNS8_SUCCESS;
+}
+
+// exact_gemm_range (exact_range.hpp:146-154): the bound must fit the plan's prefix.
+rns8_status exact_gemm_range(rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& A, const rns8_matrix& B,
+                             i256& bound, ExactRanges* out_ranges) {
+  if (!exact_wide(plan.desc.semantics)) return RNS8_SUCCESS;
+  if (A.exact_range_prefix < plan.prefix || B.exact_range_prefix < plan.prefix) return RNS8_RANGE_ERROR;
+  const int64_t m = plan.desc.m, n = plan.desc.n;
+  const bool a_rows = A.exact_axes.rows.size() == static_cast<size_t>(m);
+  const bool b_cols = B.exact_axes.cols.size() == static_cast<size_t>(n);
+  const rns8_status st = exact_gemm_bound(ctx, m, n, plan.desc.k, A.exact_max_magnitude,
+                                          a_rows ? &A.exact_axes.rows : nullptr, B.exact_max_magnitude,
+                                          b_cols ? &B.exact_axes.cols : nullptr, bound, out_ranges);
+  if (st != RNS8_SUCCESS) return st;
   return exact_range_fits(plan.desc.semantics, bound, plan.modulus_product) ? RNS8_SUCCESS : RNS8_RANGE_ERROR;
 }
 
@@ -276,3 +207,42 @@ void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, Exac
 }
 
 }  // namespace rns8host
+
+using namespace rns8host;
+
+extern "C" rns8_status rns8_cuda_exact_gemm_bound_device(int device_id, const void* d_a, const void* d_b, int64_t m,
+                                                         int64_t n, int64_t k, uint32_t is_signed, uint64_t* out_bound,
+                                                         uint64_t* out_a_max, uint64_t* out_b_max,
+                                                         uint64_t* out_row_stats, uint64_t* out_col_stats,
+                                                         void* stream) {
+  return guard([&]() -> rns8_status {
+    if (!d_a || !d_b || !out_bound || m <= 0 || n <= 0 || k <= 0 || is_signed > 1 ||
+        !valid_matrix_access(m, k, k) || !valid_matrix_access(k, n, n))
+      return RNS8_INVALID_ARGUMENT;
+    if (device_id < 0) return RNS8_INVALID_ARGUMENT;
+    rns8_context scope;  // device, stream and admission scratch of this call
+    scope.device_id = device_id;
+    scope.stream = static_cast<cudaStream_t>(stream);
+    ExactRanges ra, rb, rc;
+    i256 a_max, b_max, bound;
+    rns8_status st = device_exact_ranges(scope, d_a, is_signed != 0, m, k, ra, a_max);
+    if (st == RNS8_SUCCESS) st = device_exact_ranges(scope, d_b, is_signed != 0, k, n, rb, b_max);
+    if (st == RNS8_SUCCESS) st = exact_gemm_bound(scope, m, n, k, a_max, &ra.rows, b_max, &rb.cols, bound, &rc);
+    if (st != RNS8_SUCCESS) return st;
+    for (int l = 0; l < 4; ++l) {
+      out_bound[l] = bound.w[l];
+      if (out_a_max) out_a_max[l] = a_max.w[l];
+      if (out_b_max) out_b_max[l] = b_max.w[l];
+    }
+    auto write_stats = [](uint64_t* dst, const std::vector<AxisRange>& axes) {
+      for (size_t i = 0; i < axes.size(); ++i)
+        for (int l = 0; l < 4; ++l) {
+          dst[8 * i + l] = axes[i].max_magnitude.w[l];
+          dst[8 * i + 4 + l] = axes[i].absolute_sum.w[l];
+        }
+    };
+    if (out_row_stats) write_stats(out_row_stats, rc.rows);
+    if (out_col_stats) write_stats(out_col_stats, rc.cols);
+    return RNS8_SUCCESS;
+  });
+}

@@ -166,25 +166,29 @@ rns8_status pack_native(rns8_context* ctx, rns8_matrix* matrix, const T* src, in
   if (ctx->backend != matrix->backend || matrix->device_id != ctx->device_id || matrix->prefix == 0)
     return RNS8_INVALID_ARGUMENT;
   const bool same_source = source_version != 0 && matrix->source_version == source_version && matrix->device_current;
-  i256 exact_bound;
-  ExactRanges ranges;
-  if (exact_wide(s)) {
-    if (same_source) {
-      exact_bound = matrix->exact_max_magnitude;
-    } else {
-      native_exact_ranges<T>(src, matrix->desc.rows, matrix->desc.cols, ld, ranges, exact_bound);
-    }
-    if (!exact_range_fits(s, exact_bound, modulus_product(matrix->prefix))) return RNS8_RANGE_ERROR;
+  if (same_source) {
+    if (exact_wide(s) && !exact_range_fits(s, matrix->exact_max_magnitude, modulus_product(matrix->prefix)))
+      return RNS8_RANGE_ERROR;
+    return RNS8_SUCCESS;
   }
-  if (same_source) return RNS8_SUCCESS;
   DeviceScope dev(ctx->device_id);
   if (!dev.ok) return RNS8_BACKEND_FAILURE;
   const int64_t rows = matrix->desc.rows, cols = matrix->desc.cols;
   rns8_status st = matrix->upload.ensure(ctx->device_id, static_cast<uint64_t>(rows) * cols * sizeof(T));
   if (st != RNS8_SUCCESS) return st;
-  matrix->device_current = false;
   st = copy_in_2d(*ctx, matrix->upload.ptr, src, rows, cols, ld, sizeof(T));
   if (st != RNS8_SUCCESS) return st;
+  // Exact-wide admission (exact_range.hpp:51-77): the row and column
+  // summaries of the uploaded values, before the residues are touched, so a
+  // RANGE_ERROR leaves the matrix as it was.
+  i256 exact_bound;
+  ExactRanges ranges;
+  if (exact_wide(s)) {
+    st = device_exact_ranges(*ctx, matrix->upload.ptr, kSigned, rows, cols, ranges, exact_bound);
+    if (st != RNS8_SUCCESS) return st;
+    if (!exact_range_fits(s, exact_bound, modulus_product(matrix->prefix))) return RNS8_RANGE_ERROR;
+  }
+  matrix->device_current = false;
   const cudaError_t e =
       kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(matrix->upload.ptr), rows, cols, cols,
                                    matrix->prefix, matrix->residues, ctx->stream)
@@ -338,7 +342,7 @@ rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const
                 : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(dB), k, n, n, P, rB, ctx->stream);
   if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
   if ((st = clear_status(*ctx)) != RNS8_SUCCESS) return st;
-  // GEMM and Garner export; fused into the GEMM epilogue when the shape allows.
+  // Plane GEMM into arena planes, then the bounded export.
   task = {rA, rB, nullptr};
   e = rns8cuda::gemm_export_bounded(prob, kSigned, plan.desc.bound, dC, n, ctx->sm_count, dS, scratch, ctx->dev_status,
                                     ctx->stream);
@@ -433,7 +437,7 @@ rns8_status grouped_gemm(rns8_context* ctx, const rns8_plan* plan, const rns8_gr
       if (t.c == tasks[j].a || t.c == tasks[j].b || (i != j && t.c == tasks[j].c)) return RNS8_INVALID_ARGUMENT;
     }
     if (!bounds.empty()) {
-      const rns8_status r = exact_gemm_range(*plan, *t.a, *t.b, bounds[i], &ranges[i]);
+      const rns8_status r = exact_gemm_range(*ctx, *plan, *t.a, *t.b, bounds[i], &ranges[i]);
       if (r != RNS8_SUCCESS) return r;
     }
   }
@@ -511,7 +515,7 @@ extern "C" rns8_status rns8_gemm_rns(rns8_context* ctx, const rns8_plan* plan, c
     i256 bound;
     ExactRanges ranges;
     if (exact_wide(plan->desc.semantics)) {
-      st = exact_gemm_range(*plan, *A, *B, bound, &ranges);
+      st = exact_gemm_range(*ctx, *plan, *A, *B, bound, &ranges);
       if (st != RNS8_SUCCESS) return st;
     }
     DeviceScope dev(ctx->device_id);

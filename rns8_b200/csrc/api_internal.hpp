@@ -58,6 +58,9 @@ struct rns8_context {
   // Device arena reused by the one-shot entry points (serialised by the mutex).
   std::mutex oneshot_mutex;
   rns8host::DevBuf oneshot_arena;
+  // Device scratch of the exact-wide admission proofs (serialised by the mutex).
+  std::mutex admission_mutex;
+  rns8host::DevBuf admission;
 };
 
 struct rns8_plan {
@@ -144,12 +147,20 @@ bool backend_request_ok(rns8_backend_kind requested);
 // Plan construction shared by rns8_create_plan and rns8_cuda_plan_probe.
 rns8_status build_plan(const rns8_gemm_desc& desc, rns8_plan& plan);
 
-// Exact-wide proofs (reference src/core/exact_range.hpp).
-template <typename T>
-void native_exact_ranges(const T* src, int64_t rows, int64_t cols, int64_t ld, ExactRanges& out, i256& maximum);
+// Exact-wide proofs (reference src/core/exact_range.hpp), computed on the
+// context's device. device_exact_ranges summarises a compact native matrix
+// already in device memory; maximum = the largest |v|.
+rns8_status device_exact_ranges(rns8_context& ctx, const void* d_src, bool is_signed, int64_t rows, int64_t cols,
+                                ExactRanges& out, i256& maximum);
 bool exact_range_fits(rns8_semantics s, const i256& bound, const i256& product);
-rns8_status exact_gemm_range(const rns8_plan& plan, const rns8_matrix& A, const rns8_matrix& B, i256& bound,
-                             ExactRanges* out_ranges);
+// The admission bound of an m x n x k product from A's row records (or its
+// largest |a| alone when a_rows is null) and B's column records; out_ranges
+// receives the per-row and per-column maxima and sums of the cell bounds.
+rns8_status exact_gemm_bound(rns8_context& ctx, int64_t m, int64_t n, int64_t k, const i256& a_max,
+                             const std::vector<AxisRange>* a_rows, const i256& b_max,
+                             const std::vector<AxisRange>* b_cols, i256& bound, ExactRanges* out_ranges);
+rns8_status exact_gemm_range(rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& A, const rns8_matrix& B,
+                             i256& bound, ExactRanges* out_ranges);
 void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, ExactRanges* ranges);
 
 uint64_t next_matrix_id();

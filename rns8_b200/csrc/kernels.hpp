@@ -72,4 +72,41 @@ cudaError_t export_limbs(const int8_t* planes, int64_t m, int64_t n, uint32_t pr
 cudaError_t export_finite_u8(const int8_t* residues, int64_t m, int64_t n, uint32_t modulus, uint8_t* dst, int64_t ld,
                              cudaStream_t stream);
 
+// ---- exact-wide admission (reference src/core/exact_range.hpp:51-154) ------------
+// Summary of one row or column of native int64/uint64 values: max |v|, sum |v|,
+// sum v, min, max and sum |v - center| with center = (min + max) / 2
+// truncated toward zero. 128-bit fields hold sums of up to 2^63 values.
+struct AxisSummary {
+  unsigned __int128 max_mag, abs_sum, dev_sum;
+  __int128 sum, minimum, maximum;
+  uint64_t any;
+  uint64_t pad;
+};
+// Scratch for axis_summaries on a rows x cols matrix.
+uint64_t axis_summaries_scratch_bytes(int64_t rows, int64_t cols);
+// Row and column summaries of a compact (ld == cols) int64 (is_signed) or
+// uint64 matrix in device memory into d_rows[rows] and d_cols[cols].
+cudaError_t axis_summaries(const void* src, bool is_signed, int64_t rows, int64_t cols, AxisSummary* d_rows,
+                           AxisSummary* d_cols, void* scratch, uint64_t scratch_bytes, cudaStream_t stream);
+
+// Per-axis inputs of the cell bound (exact_range.hpp:79-98), 256-bit
+// little-endian two's complement limbs.
+struct AxisBoundInput {
+  uint64_t max_mag[4], abs_sum[4], sum[4], center[4], dev_max[4], dev_sum[4];
+  uint64_t sum_known;
+};
+// Maximum and sum of the cell bounds along one output row or column.
+struct BoundStats {
+  uint64_t max[4];
+  uint64_t sum[4];
+};
+uint64_t cell_bounds_scratch_bytes(int64_t m, int64_t n);
+// For every output cell (r, c) of an m x n exact-wide product with inner
+// dimension k, the smallest of the admission bounds of row r of A and
+// column c of B; d_row_stats[m] and d_col_stats[n] receive their maxima and
+// sums along rows and columns.
+cudaError_t cell_bounds(const AxisBoundInput* d_rows, int64_t m, const AxisBoundInput* d_cols, int64_t n, int64_t k,
+                        BoundStats* d_row_stats, BoundStats* d_col_stats, void* scratch, uint64_t scratch_bytes,
+                        cudaStream_t stream);
+
 }  // namespace rns8cuda

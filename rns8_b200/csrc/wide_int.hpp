@@ -7,24 +7,32 @@
 
 #include <cstdint>
 
+// Usable from device code too (the exact-wide admission kernels) when the
+// including file is compiled as CUDA.
+#ifdef __CUDACC__
+#define RNS8_HD __host__ __device__ __forceinline__
+#else
+#define RNS8_HD inline
+#endif
+
 namespace rns8host {
 
 struct i256 {
   uint64_t w[4] = {0, 0, 0, 0};
 
-  static i256 from_u64(uint64_t v) {
+  RNS8_HD static i256 from_u64(uint64_t v) {
     i256 r;
     r.w[0] = v;
     return r;
   }
-  static i256 from_i64(int64_t v) {
+  RNS8_HD static i256 from_i64(int64_t v) {
     i256 r;
     const uint64_t s = v < 0 ? ~0ull : 0ull;
     r.w[0] = static_cast<uint64_t>(v);
     r.w[1] = r.w[2] = r.w[3] = s;
     return r;
   }
-  static i256 from_i128(__int128 v) {
+  RNS8_HD static i256 from_i128(__int128 v) {
     i256 r;
     const uint64_t s = v < 0 ? ~0ull : 0ull;
     r.w[0] = static_cast<uint64_t>(v);
@@ -32,17 +40,17 @@ struct i256 {
     r.w[2] = r.w[3] = s;
     return r;
   }
-  static i256 from_u128(unsigned __int128 v) {
+  RNS8_HD static i256 from_u128(unsigned __int128 v) {
     i256 r;
     r.w[0] = static_cast<uint64_t>(v);
     r.w[1] = static_cast<uint64_t>(v >> 64);
     return r;
   }
-  bool neg() const { return (w[3] >> 63) != 0; }
-  bool zero() const { return (w[0] | w[1] | w[2] | w[3]) == 0; }
+  RNS8_HD bool neg() const { return (w[3] >> 63) != 0; }
+  RNS8_HD bool zero() const { return (w[0] | w[1] | w[2] | w[3]) == 0; }
 };
 
-inline i256 operator+(const i256& a, const i256& b) {
+RNS8_HD i256 operator+(const i256& a, const i256& b) {
   i256 r;
   unsigned __int128 c = 0;
   for (int i = 0; i < 4; ++i) {
@@ -52,28 +60,28 @@ inline i256 operator+(const i256& a, const i256& b) {
   }
   return r;
 }
-inline i256 operator-(const i256& a) {
+RNS8_HD i256 operator-(const i256& a) {
   i256 r;
   for (int i = 0; i < 4; ++i) r.w[i] = ~a.w[i];
   return r + i256::from_u64(1);
 }
-inline i256 operator-(const i256& a, const i256& b) { return a + (-b); }
-inline int cmp(const i256& a, const i256& b) {
+RNS8_HD i256 operator-(const i256& a, const i256& b) { return a + (-b); }
+RNS8_HD int cmp(const i256& a, const i256& b) {
   if (a.neg() != b.neg()) return a.neg() ? -1 : 1;
   for (int i = 3; i >= 0; --i)
     if (a.w[i] != b.w[i]) return a.w[i] < b.w[i] ? -1 : 1;
   return 0;
 }
-inline bool operator<(const i256& a, const i256& b) { return cmp(a, b) < 0; }
-inline bool operator>(const i256& a, const i256& b) { return cmp(a, b) > 0; }
-inline bool operator<=(const i256& a, const i256& b) { return cmp(a, b) <= 0; }
-inline bool operator>=(const i256& a, const i256& b) { return cmp(a, b) >= 0; }
-inline bool operator==(const i256& a, const i256& b) { return cmp(a, b) == 0; }
-inline i256 abs(const i256& a) { return a.neg() ? -a : a; }
-inline i256 max(const i256& a, const i256& b) { return a >= b ? a : b; }
-inline i256 min(const i256& a, const i256& b) { return a <= b ? a : b; }
+RNS8_HD bool operator<(const i256& a, const i256& b) { return cmp(a, b) < 0; }
+RNS8_HD bool operator>(const i256& a, const i256& b) { return cmp(a, b) > 0; }
+RNS8_HD bool operator<=(const i256& a, const i256& b) { return cmp(a, b) <= 0; }
+RNS8_HD bool operator>=(const i256& a, const i256& b) { return cmp(a, b) >= 0; }
+RNS8_HD bool operator==(const i256& a, const i256& b) { return cmp(a, b) == 0; }
+RNS8_HD i256 abs(const i256& a) { return a.neg() ? -a : a; }
+RNS8_HD i256 max(const i256& a, const i256& b) { return a >= b ? a : b; }
+RNS8_HD i256 min(const i256& a, const i256& b) { return a <= b ? a : b; }
 // Truncating signed product.
-inline i256 operator*(const i256& a0, const i256& b0) {
+RNS8_HD i256 operator*(const i256& a0, const i256& b0) {
   const bool n = a0.neg() != b0.neg();
   const i256 a = abs(a0), b = abs(b0);
   i256 r;
@@ -88,7 +96,7 @@ inline i256 operator*(const i256& a0, const i256& b0) {
   }
   return n ? -r : r;
 }
-inline i256 shl(const i256& a, unsigned s) {
+RNS8_HD i256 shl(const i256& a, unsigned s) {
   i256 r;
   const unsigned limb = s / 64, bit = s % 64;
   for (int i = 3; i >= 0; --i) {
@@ -100,16 +108,20 @@ inline i256 shl(const i256& a, unsigned s) {
   return r;
 }
 // Signed division by two rounding toward zero (cpp_int semantics).
-inline i256 half_trunc(const i256& a) {
+RNS8_HD i256 half_trunc(const i256& a) {
   const bool n = a.neg();
   i256 m = abs(a);
   for (int i = 0; i < 4; ++i) m.w[i] = (m.w[i] >> 1) | (i < 3 ? (m.w[i + 1] << 63) : 0);
   return n ? -m : m;
 }
-inline uint32_t bit_length(const i256& a) {
+RNS8_HD uint32_t bit_length(const i256& a) {
   if (a.neg() || a.zero()) return 0;
   for (int i = 3; i >= 0; --i)
+#ifdef __CUDA_ARCH__
+    if (a.w[i]) return static_cast<uint32_t>(64 * i + 64 - __clzll(static_cast<long long>(a.w[i])));
+#else
     if (a.w[i]) return static_cast<uint32_t>(64 * i + 64 - __builtin_clzll(a.w[i]));
+#endif
   return 0;
 }
 
