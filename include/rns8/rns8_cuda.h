@@ -122,6 +122,24 @@ RNS8_API rns8_status rns8_cuda_export_limbs_device(int device_id, const int8_t* 
 RNS8_API rns8_status rns8_cuda_export_finite_u8_device(int device_id, const int8_t* d_residues, int64_t m, int64_t n,
                                                        uint16_t modulus, uint8_t* d_dst, int64_t ld, void* stream);
 
+/* WRAP_U64_MOD_2_64 byte-limb path (reference src/backend_wrap64/wrap64_hip.hpp:
+ * 12 pack, :22 GEMM, :31 export). A wrap64 matrix is eight unsigned byte
+ * planes, limb-major: byte l of cell (r, c) of an R x C matrix is
+ * d_limbs[l*R*C + r*C + c].
+ * pack:   uint64 d_src (row-major, ld >= cols) -> d_limbs (8*rows*cols bytes).
+ * gemm:   d_c (m x n uint64, compact row-major) = A x B mod 2^64 from byte
+ *         planes; the tensor-core path (K and N multiples of 16) ORs 0x100
+ *         into *d_status if a bounded wait ran out (d_status may be NULL only
+ *         for RNS8_CUDA_GEMM_SIMT).
+ * export: d_limbs -> uint64 d_dst[row*ld + col]. */
+RNS8_API rns8_status rns8_cuda_pack_wrap_u64_device(int device_id, const uint64_t* d_src, int64_t rows, int64_t cols,
+                                                    int64_t ld, uint8_t* d_limbs, void* stream);
+RNS8_API rns8_status rns8_cuda_gemm_wrap_u64_device(int device_id, const uint8_t* d_a_limbs, const uint8_t* d_b_limbs,
+                                                    uint64_t* d_c, int64_t m, int64_t n, int64_t k,
+                                                    uint32_t gemm_path, uint32_t* d_status, void* stream);
+RNS8_API rns8_status rns8_cuda_export_wrap_u64_device(int device_id, const uint8_t* d_limbs, int64_t rows,
+                                                      int64_t cols, uint64_t* d_dst, int64_t ld, void* stream);
+
 /* Exact-wide admission proof (reference src/core/exact_range.hpp:51-154 and
  * api_pack.cpp:61-64) of A x B for native matrices already in device memory:
  * A is m x k, B is k x n, both compact (ld = cols) int64 (is_signed = 1) or

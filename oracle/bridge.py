@@ -49,6 +49,8 @@ _SIGS = {
     "oracle_gemm_finite_u8_oneshot": (C.c_int, [C.c_int, u16, i64, i64, i64, vp, i64, vp, i64, vp, i64]),
     "oracle_exact_gemm_admission": (C.c_int, [C.c_int, vp, i64, vp, i64, i64, i64, i64, u32, vp, vp, vp]),
     "oracle_exact_gemm_cell_stats": (C.c_int, [C.c_int, vp, i64, vp, i64, i64, i64, i64, vp, vp]),
+    "oracle_wrap64_gemm": (None, [vp, i64, vp, i64, vp, i64, i64, i64, i64]),
+    "oracle_wrap64_gemm_diagonals": (None, [vp, i64, vp, i64, vp, i64, i64, i64, i64]),
     "oracle_rng_new": (C.c_int, [u64]),
     "oracle_rng_free": (None, [C.c_int]),
     "oracle_rng_next": (u64, [C.c_int]),
@@ -241,6 +243,16 @@ def exact_gemm_cell_stats(A: np.ndarray, B: np.ndarray) -> tuple[list[tuple[int,
                                        _p(rows), _p(cols))
     pair = lambda v: (from_limbs4(v[:4]), from_limbs4(v[4:]))
     return [pair(r) for r in rows], [pair(c) for c in cols]
+
+
+def wrap64_gemm(A: np.ndarray, B: np.ndarray, diagonals: bool = False) -> np.ndarray:
+    """C = A x B mod 2^64 over uint64 (A, B may be row-padded views)."""
+    m, k = A.shape
+    n = B.shape[1]
+    out = np.zeros((m, n), np.uint64)
+    fn = lib().oracle_wrap64_gemm_diagonals if diagonals else lib().oracle_wrap64_gemm
+    fn(_p(A), _ld(A), _p(B), _ld(B), _p(out), n, m, n, k)
+    return out
 
 
 class Rng:

@@ -840,6 +840,54 @@ OX int oracle_exact_gemm_cell_stats(int is_signed, const void* A, int64_t lda, c
   return ST_SUCCESS;
 }
 
+// ---- WRAP_U64_MOD_2_64: src/backend_wrap64/wrap64_reference.cpp -------------
+// cpu_gemm_wrap_u64 (:254-290): native uint64 multiply-accumulate, which wraps
+// modulo 2^64, row by row (OpenMP over rows above the work threshold).
+OX void oracle_wrap64_gemm(const uint64_t* A, int64_t lda, const uint64_t* B, int64_t ldb, uint64_t* C, int64_t ldc,
+                           int64_t m, int64_t n, int64_t k) {
+  auto row = [&](int64_t r) {
+    std::vector<uint64_t> acc(static_cast<size_t>(n), 0);
+    for (int64_t kk = 0; kk < k; ++kk) {
+      const uint64_t a = A[r * lda + kk];
+      const uint64_t* b = B + kk * ldb;
+      for (int64_t c = 0; c < n; ++c) acc[c] += a * b[c];
+    }
+    for (int64_t c = 0; c < n; ++c) C[r * ldc + c] = acc[c];
+  };
+  if (parallel_should_use(sat_mul3(m, n, k))) {
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < m; ++r) row(r);
+    return;
+  }
+  for (int64_t r = 0; r < m; ++r) row(r);
+}
+
+// wrap64_low_diagonal_byte_pair_gemm_cell (:166-190) with
+// wrap64_low64_from_diagonals (:105-117): the 36 unsigned byte products of the
+// low eight Comba diagonals, summed per diagonal (128-bit here; the reference
+// uses cpp_int), then carried byte by byte into the low 64 bits.
+OX void oracle_wrap64_gemm_diagonals(const uint64_t* A, int64_t lda, const uint64_t* B, int64_t ldb, uint64_t* C,
+                                     int64_t ldc, int64_t m, int64_t n, int64_t k) {
+  for (int64_t r = 0; r < m; ++r)
+    for (int64_t c = 0; c < n; ++c) {
+      unsigned __int128 diag[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int64_t kk = 0; kk < k; ++kk) {
+        const uint64_t a = A[r * lda + kk], b = B[kk * ldb + c];
+        for (uint32_t i = 0; i < 8; ++i)
+          for (uint32_t j = 0; i + j < 8; ++j)
+            diag[i + j] += static_cast<uint32_t>((a >> (8 * i)) & 0xFFu) * static_cast<uint32_t>((b >> (8 * j)) & 0xFFu);
+      }
+      uint64_t out = 0;
+      unsigned __int128 carry = 0;
+      for (uint32_t d = 0; d < 8; ++d) {
+        const unsigned __int128 column = diag[d] + carry;
+        out |= static_cast<uint64_t>(column & 0xFFu) << (8 * d);
+        carry = column >> 8;
+      }
+      C[r * ldc + c] = out;
+    }
+}
+
 // Seeded inputs: std::mt19937_64 + std::uniform_int_distribution, as the
 // reference's tests and benchmark generate them (rns8_bench_core_helpers.inc:
 // 1150-1166, test_bounded_reference_sweeps.cpp:209-243).

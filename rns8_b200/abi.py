@@ -225,6 +225,9 @@ SIGNATURES = {
     "rns8_export_exact_wide_unsigned_limbs": (c_status, [vp, vp, vp, vp, i64, u32]),
     "rns8_gemm_i64_oneshot": (c_status, [vp, vp, vp, i64, vp, i64, vp, i64]),
     "rns8_gemm_u64_oneshot": (c_status, [vp, vp, vp, i64, vp, i64, vp, i64]),
+    "rns8_gemm_wrap_u64": (c_status, [vp, vp, vp, vp, vp, vp]),
+    "rns8_export_wrap_u64": (c_status, [vp, vp, vp, vp, i64]),
+    "rns8_gemm_wrap_u64_oneshot": (c_status, [vp, vp, vp, i64, vp, i64, vp, i64]),
     "rns8_gemm_finite_ring_u8_oneshot": (c_status, [vp, vp, u16, vp, i64, vp, i64, vp, i64]),
     "rns8_gemm_finite_field_u8_oneshot": (c_status, [vp, vp, u16, vp, i64, vp, i64, vp, i64]),
     # device-pointer seam (include/rns8/rns8_cuda.h)
@@ -245,6 +248,9 @@ SIGNATURES = {
     "rns8_cuda_export_finite_u8_device": (c_status, [C.c_int, vp, i64, i64, u16, vp, i64, vp]),
     "rns8_cuda_plan_probe": (c_status, [vp, P(u32), P(u32), P(u64)]),
     "rns8_cuda_exact_gemm_bound_device": (c_status, [C.c_int, vp, vp, i64, i64, i64, u32, vp, vp, vp, vp, vp, vp]),
+    "rns8_cuda_pack_wrap_u64_device": (c_status, [C.c_int, vp, i64, i64, i64, vp, vp]),
+    "rns8_cuda_gemm_wrap_u64_device": (c_status, [C.c_int, vp, vp, vp, i64, i64, i64, u32, vp, vp]),
+    "rns8_cuda_export_wrap_u64_device": (c_status, [C.c_int, vp, i64, i64, vp, i64, vp]),
 }
 
 _LIB: C.CDLL | None = None

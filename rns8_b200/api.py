@@ -163,6 +163,12 @@ def gemm_rns(ctx: Context, plan: Plan, a: Matrix, b: Matrix, c: Matrix, ws: Work
     check(lib().rns8_gemm_rns(ctx.handle, plan.handle, a.handle, b.handle, c.handle, ws.handle), "rns8_gemm_rns")
 
 
+def gemm_wrap_u64(ctx: Context, plan: Plan, a: Matrix, b: Matrix, c: Matrix, ws: Workspace) -> None:
+    """C = A x B mod 2^64 on byte-limb (WRAP_U64_MOD_2_64) matrices."""
+    check(lib().rns8_gemm_wrap_u64(ctx.handle, plan.handle, a.handle, b.handle, c.handle, ws.handle),
+          "rns8_gemm_wrap_u64")
+
+
 def gemm_finite_u8(ctx: Context, plan: Plan, modulus: int, a: Matrix, b: Matrix, c: Matrix, ws: Workspace) -> None:
     check(lib().rns8_gemm_finite_u8(ctx.handle, plan.handle, modulus, a.handle, b.handle, c.handle, ws.handle),
           "rns8_gemm_finite_u8")
@@ -194,6 +200,12 @@ def export_i64(ctx: Context, plan: Plan, c: Matrix, out: np.ndarray | None = Non
 def export_u64(ctx: Context, plan: Plan, c: Matrix, out: np.ndarray | None = None) -> np.ndarray:
     out = np.zeros((plan.desc.m, plan.desc.n), np.uint64) if out is None else out
     check(lib().rns8_export_u64(ctx.handle, plan.handle, c.handle, _ptr(out), _ld(out)), "rns8_export_u64")
+    return out
+
+
+def export_wrap_u64(ctx: Context, plan: Plan, c: Matrix, out: np.ndarray | None = None) -> np.ndarray:
+    out = np.zeros((plan.desc.m, plan.desc.n), np.uint64) if out is None else out
+    check(lib().rns8_export_wrap_u64(ctx.handle, plan.handle, c.handle, _ptr(out), _ld(out)), "rns8_export_wrap_u64")
     return out
 
 
@@ -229,6 +241,14 @@ def gemm_u64_oneshot(ctx: Context, desc: abi.GemmDesc, A: np.ndarray, B: np.ndar
     out = np.zeros((desc.m, desc.n), np.uint64) if out is None else out
     check(lib().rns8_gemm_u64_oneshot(ctx.handle, C.byref(desc), _ptr(A), _ld(A), _ptr(B), _ld(B), _ptr(out),
                                       _ld(out)), "rns8_gemm_u64_oneshot")
+    return out
+
+
+def gemm_wrap_u64_oneshot(ctx: Context, desc: abi.GemmDesc, A: np.ndarray, B: np.ndarray,
+                          out: np.ndarray | None = None) -> np.ndarray:
+    out = np.zeros((desc.m, desc.n), np.uint64) if out is None else out
+    check(lib().rns8_gemm_wrap_u64_oneshot(ctx.handle, C.byref(desc), _ptr(A), _ld(A), _ptr(B), _ld(B), _ptr(out),
+                                           _ld(out)), "rns8_gemm_wrap_u64_oneshot")
     return out
 
 

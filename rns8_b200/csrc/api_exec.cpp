@@ -153,6 +153,71 @@ rns8cuda::PlaneGemmProblem rns_problem(const rns8_plan& plan, uint32_t planes, c
   return prob;
 }
 
+// ---- WRAP_U64_MOD_2_64 (byte-limb storage) ------------------------------------
+// wrap_matrix_storage_matches (api_gemm.cpp:190-193): eight byte planes of a
+// rows x cols row-major wrap64 matrix, no CRT prefix.
+bool wrap_storage_ok(const rns8_matrix& m, int64_t rows, int64_t cols) {
+  return m.desc.semantics == RNS8_WRAP_U64_MOD_2_64 && m.desc.bound_kind == RNS8_BOUND_NONE && m.desc.rows == rows &&
+         m.desc.cols == cols && m.desc.logical_layout == RNS8_LAYOUT_ROW_MAJOR && m.prefix == 0 &&
+         m.desc.max_prefix == 0 && m.residues != nullptr &&
+         m.residue_bytes == static_cast<uint64_t>(rows) * static_cast<uint64_t>(cols) * 8;
+}
+
+// rns8_pack_u64 on a wrap64 matrix (api_pack.cpp:178-208): upload, then the
+// byte planes; a repeated non-zero source version skips the work.
+rns8_status pack_wrap(rns8_context* ctx, rns8_matrix* matrix, const uint64_t* src, int64_t ld,
+                      uint64_t source_version) {
+  if (ctx->backend != matrix->backend || matrix->device_id != ctx->device_id ||
+      !wrap_storage_ok(*matrix, matrix->desc.rows, matrix->desc.cols))
+    return RNS8_INVALID_ARGUMENT;
+  if (source_version != 0 && matrix->source_version == source_version && matrix->device_current)
+    return RNS8_SUCCESS;
+  DeviceScope dev(ctx->device_id);
+  if (!dev.ok) return RNS8_BACKEND_FAILURE;
+  const int64_t rows = matrix->desc.rows, cols = matrix->desc.cols;
+  rns8_status st = matrix->upload.ensure(ctx->device_id, static_cast<uint64_t>(rows) * cols * sizeof(uint64_t));
+  if (st != RNS8_SUCCESS) return st;
+  if ((st = copy_in_2d(*ctx, matrix->upload.ptr, src, rows, cols, ld, sizeof(uint64_t))) != RNS8_SUCCESS) return st;
+  matrix->device_current = false;
+  if (rns8cuda::wrap_pack_u64(static_cast<const uint64_t*>(matrix->upload.ptr), rows, cols, cols,
+                              reinterpret_cast<uint8_t*>(matrix->residues), ctx->stream) != cudaSuccess)
+    return RNS8_BACKEND_FAILURE;
+  if ((st = sync(*ctx)) != RNS8_SUCCESS) return st;
+  matrix->device_current = true;
+  matrix->source_version = source_version;
+  return RNS8_SUCCESS;
+}
+
+// validate_wrap_gemm_operands (api_gemm.cpp:158-198).
+rns8_status validate_wrap_operands(const rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& A,
+                                   const rns8_matrix& B, const rns8_matrix& C) {
+  if (plan.desc.semantics != RNS8_WRAP_U64_MOD_2_64 || plan.prefix != 0) return RNS8_INVALID_ARGUMENT;
+  if (A.backend != plan.backend || B.backend != plan.backend || C.backend != plan.backend) return RNS8_INVALID_ARGUMENT;
+  if (A.device_id != ctx.device_id || B.device_id != ctx.device_id || C.device_id != ctx.device_id)
+    return RNS8_INVALID_ARGUMENT;
+  const auto& d = plan.desc;
+  if (!wrap_storage_ok(A, d.m, d.k) || !wrap_storage_ok(B, d.k, d.n) || !wrap_storage_ok(C, d.m, d.n))
+    return RNS8_INVALID_ARGUMENT;
+  if (!A.device_current || !B.device_current) return RNS8_INVALID_ARGUMENT;
+  return RNS8_SUCCESS;
+}
+
+// C = A x B mod 2^64 into the uint64 buffer c (m x n), then c's byte planes
+// into `planes` when given. Reads the status word (a wait that ran out is a
+// backend failure).
+rns8_status run_wrap_gemm(rns8_context& ctx, const uint8_t* a, const uint8_t* b, uint64_t* c, int64_t m, int64_t n,
+                          int64_t k, uint8_t* planes) {
+  rns8_status st = clear_status(ctx);
+  if (st != RNS8_SUCCESS) return st;
+  if (rns8cuda::wrap_gemm(a, b, c, m, n, k, rns8cuda::GemmPath::Auto, ctx.sm_count, ctx.dev_status, ctx.stream) !=
+      cudaSuccess)
+    return RNS8_BACKEND_FAILURE;
+  if (planes && rns8cuda::wrap_pack_u64(c, m, n, n, planes, ctx.stream) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  uint32_t word = 0;
+  if ((st = read_status(ctx, &word)) != RNS8_SUCCESS) return st;
+  return status_from_device(word);
+}
+
 template <typename T>
 rns8_status pack_native(rns8_context* ctx, rns8_matrix* matrix, const T* src, int64_t ld, uint64_t source_version) {
   constexpr bool kSigned = std::numeric_limits<T>::is_signed;
@@ -162,7 +227,9 @@ rns8_status pack_native(rns8_context* ctx, rns8_matrix* matrix, const T* src, in
   if (kSigned ? (s != RNS8_BOUNDED_I64 && s != RNS8_EXACT_WIDE_SIGNED)
               : (s != RNS8_BOUNDED_U64 && s != RNS8_EXACT_WIDE_UNSIGNED && s != RNS8_WRAP_U64_MOD_2_64))
     return RNS8_INVALID_ARGUMENT;
-  if (s == RNS8_WRAP_U64_MOD_2_64) return RNS8_UNSUPPORTED_BACKEND;
+  if constexpr (!kSigned) {
+    if (s == RNS8_WRAP_U64_MOD_2_64) return pack_wrap(ctx, matrix, src, ld, source_version);
+  }
   if (ctx->backend != matrix->backend || matrix->device_id != ctx->device_id || matrix->prefix == 0)
     return RNS8_INVALID_ARGUMENT;
   const bool same_source = source_version != 0 && matrix->source_version == source_version && matrix->device_current;
@@ -657,4 +724,91 @@ extern "C" rns8_status rns8_gemm_finite_field_u8_oneshot(rns8_context* ctx, cons
                                                          uint16_t modulus, const uint8_t* A, int64_t lda,
                                                          const uint8_t* B, int64_t ldb, uint8_t* C, int64_t ldc) {
   return guard([&] { return finite_oneshot(ctx, desc, RNS8_FINITE_FIELD_U8, modulus, A, lda, B, ldb, C, ldc); });
+}
+
+extern "C" rns8_status rns8_gemm_wrap_u64(rns8_context* ctx, const rns8_plan* plan, const rns8_matrix* A,
+                                         const rns8_matrix* B, rns8_matrix* C, rns8_workspace* workspace) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !A || !B || !C || !workspace) return RNS8_INVALID_ARGUMENT;
+    rns8_status st = validate_workspace(*ctx, *plan, *workspace);
+    if (st != RNS8_SUCCESS) return st;
+    if ((st = validate_wrap_operands(*ctx, *plan, *A, *B, *C)) != RNS8_SUCCESS) return st;
+    DeviceScope dev(ctx->device_id);
+    if (!dev.ok) return RNS8_BACKEND_FAILURE;
+    const int64_t m = plan->desc.m, n = plan->desc.n, k = plan->desc.k;
+    if ((st = workspace->scratch.ensure(ctx->device_id, static_cast<uint64_t>(m) * n * sizeof(uint64_t))) !=
+        RNS8_SUCCESS)
+      return st;
+    C->device_current = false;
+    st = run_wrap_gemm(*ctx, reinterpret_cast<const uint8_t*>(A->residues), reinterpret_cast<const uint8_t*>(B->residues),
+                       static_cast<uint64_t*>(workspace->scratch.ptr), m, n, k, reinterpret_cast<uint8_t*>(C->residues));
+    if (st != RNS8_SUCCESS) return st;
+    C->device_current = true;
+    C->source_version = combine_source_versions(A->source_version, B->source_version);
+    return RNS8_SUCCESS;
+  });
+}
+
+// rns8_export_wrap_u64 (api_export.cpp:534-585): the low 64 bits of every cell.
+extern "C" rns8_status rns8_export_wrap_u64(rns8_context* ctx, const rns8_plan* plan, const rns8_matrix* C,
+                                           uint64_t* dst, int64_t ld) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !plan || !C || !dst || !valid_matrix_access(plan->desc.m, plan->desc.n, ld))
+      return RNS8_INVALID_ARGUMENT;
+    if (!plan_context_ok(*ctx, *plan) || plan->desc.semantics != RNS8_WRAP_U64_MOD_2_64 || plan->prefix != 0)
+      return RNS8_INVALID_ARGUMENT;
+    if (C->device_id != ctx->device_id || C->backend != plan->backend ||
+        !wrap_storage_ok(*C, plan->desc.m, plan->desc.n) || !C->device_current)
+      return RNS8_INVALID_ARGUMENT;
+    DeviceScope dev(ctx->device_id);
+    if (!dev.ok) return RNS8_BACKEND_FAILURE;
+    const int64_t m = plan->desc.m, n = plan->desc.n;
+    rns8_matrix& mc = const_cast<rns8_matrix&>(*C);  // export staging is a documented mutable cache
+    rns8_status st = mc.staging.ensure(ctx->device_id, static_cast<uint64_t>(m) * n * sizeof(uint64_t));
+    if (st != RNS8_SUCCESS) return st;
+    if (rns8cuda::wrap_export_u64(reinterpret_cast<const uint8_t*>(C->residues), m, n,
+                                  static_cast<uint64_t*>(mc.staging.ptr), n, ctx->stream) != cudaSuccess)
+      return RNS8_BACKEND_FAILURE;
+    if ((st = copy_out_2d(*ctx, dst, ld, mc.staging.ptr, m, n, sizeof(uint64_t))) != RNS8_SUCCESS) return st;
+    return sync(*ctx);
+  });
+}
+
+// rns8_gemm_wrap_u64_oneshot (api_oneshot.cpp:588-618): pack, GEMM and export
+// through the context's one-shot arena.
+extern "C" rns8_status rns8_gemm_wrap_u64_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const uint64_t* A,
+                                                 int64_t lda, const uint64_t* B, int64_t ldb, uint64_t* C,
+                                                 int64_t ldc) {
+  return guard([&]() -> rns8_status {
+    if (!ctx || !desc || !A || !B || !C) return RNS8_INVALID_ARGUMENT;
+    rns8_status st = validate_typed_oneshot(*desc, RNS8_WRAP_U64_MOD_2_64, lda, ldb, ldc);
+    if (st != RNS8_SUCCESS) return st;
+    rns8_plan plan;
+    plan.device_id = ctx->device_id;
+    if ((st = build_plan(*desc, plan)) != RNS8_SUCCESS) return st;
+    DeviceScope dev(ctx->device_id);
+    if (!dev.ok) return RNS8_BACKEND_FAILURE;
+    const int64_t m = plan.desc.m, n = plan.desc.n, k = plan.desc.k;
+    const uint64_t a_bytes = static_cast<uint64_t>(m) * k * 8, b_bytes = static_cast<uint64_t>(k) * n * 8;
+    const uint64_t c_bytes = static_cast<uint64_t>(m) * n * 8;
+    const uint64_t total = 2 * round256(a_bytes) + 2 * round256(b_bytes) + round256(c_bytes);
+    std::unique_lock<std::mutex> lock(ctx->oneshot_mutex, std::try_to_lock);
+    DevBuf local;
+    DevBuf& arena = lock.owns_lock() ? ctx->oneshot_arena : local;
+    if ((st = arena.ensure(ctx->device_id, total)) != RNS8_SUCCESS) return st;
+    Carve cv{static_cast<uint8_t*>(arena.ptr)};
+    auto* dA = static_cast<uint64_t*>(cv.take(a_bytes));
+    auto* dB = static_cast<uint64_t*>(cv.take(b_bytes));
+    auto* lA = static_cast<uint8_t*>(cv.take(a_bytes));
+    auto* lB = static_cast<uint8_t*>(cv.take(b_bytes));
+    auto* dC = static_cast<uint64_t*>(cv.take(c_bytes));
+    if ((st = copy_in_2d(*ctx, dA, A, m, k, lda, 8)) != RNS8_SUCCESS) return st;
+    if ((st = copy_in_2d(*ctx, dB, B, k, n, ldb, 8)) != RNS8_SUCCESS) return st;
+    if (rns8cuda::wrap_pack_u64(dA, m, k, k, lA, ctx->stream) != cudaSuccess ||
+        rns8cuda::wrap_pack_u64(dB, k, n, n, lB, ctx->stream) != cudaSuccess)
+      return RNS8_BACKEND_FAILURE;
+    if ((st = run_wrap_gemm(*ctx, lA, lB, dC, m, n, k, nullptr)) != RNS8_SUCCESS) return st;
+    if ((st = copy_out_2d(*ctx, C, ldc, dC, m, n, 8)) != RNS8_SUCCESS) return st;
+    return sync(*ctx);
+  });
 }

@@ -282,7 +282,6 @@ rns8_status build_plan(const rns8_gemm_desc& desc, rns8_plan& plan) {
   const rns8_status v = validate_gemm_desc(desc, prefix);
   if (v != RNS8_SUCCESS) return v;
   if (!backend_request_ok(desc.requested_backend)) return RNS8_UNSUPPORTED_BACKEND;
-  if (desc.semantics == RNS8_WRAP_U64_MOD_2_64) return RNS8_UNSUPPORTED_BACKEND;  // not implemented here
   plan.desc = desc;
   plan.desc.struct_size = sizeof(rns8_gemm_desc);
   plan.desc.max_prefix = prefix;
@@ -300,8 +299,8 @@ rns8_status build_plan(const rns8_gemm_desc& desc, rns8_plan& plan) {
   plan.tile_count = plan.tile_rows * plan.tile_cols;
   const i256 required_range = schedule_required_range(plan.desc);
   plan.range_bit_length = bit_length(required_range);
-  if (uses_finite_storage(plan.desc.semantics)) {
-    plan.prefix = 0;
+  if (uses_finite_storage(plan.desc.semantics) || plan.desc.semantics == RNS8_WRAP_U64_MOD_2_64) {
+    plan.prefix = 0;  // finite: one residue plane; wrap64: eight byte planes, no CRT prefix
     plan.fingerprint = plan_fingerprint(plan);
     return RNS8_SUCCESS;
   }
@@ -466,6 +465,8 @@ static std::string selected_kernel_name(const rns8_plan& plan) {
   prob.task_count = 1;
   prob.tasks = &task;
   const bool tc = prob.k % 16 == 0 && prob.n % 16 == 0;
+  if (plan.desc.semantics == RNS8_WRAP_U64_MOD_2_64)
+    return tc ? "sm100a_tcgen05_u8_byte_gemm36_128x256x128_wrap64" : "sm100a_simt_wrap64_u64_16x16";
   return tc ? "sm100a_tcgen05_i8_plane_gemm_128x256x128_modm_epilogue" : "sm100a_simt_plane_gemm_64x64_modm";
 }
 
@@ -505,6 +506,26 @@ extern "C" rns8_status rns8_get_plan_backend_info(const rns8_plan* plan, rns8_pl
     set_text(out->accumulator_modulus_policy, sizeof(out->accumulator_modulus_policy),
              "reduce_modulo_plane_modulus_every_65536_products");
     set_text(out->accumulator_safety_status, sizeof(out->accumulator_safety_status), "proven_int32_safe");
+    if (plan->desc.semantics == RNS8_WRAP_U64_MOD_2_64) {
+      // 36 unsigned byte-pair products on the low 8 diagonals; a 16384-product
+      // K block keeps diagonals 0..3 exact in 32 bits, diagonals 4..7 only
+      // matter modulo 2^32.
+      set_text(out->epilogue_mode, sizeof(out->epilogue_mode), "u32_diagonal_shift_add_mod_2_64");
+      set_text(out->workspace_mode, sizeof(out->workspace_mode), "uint64_result_accumulator");
+      set_text(out->isa_evidence, sizeof(out->isa_evidence), "tcgen05.mma.kind::i8 (u8 x u8) + cp.async.bulk.tensor");
+      out->accumulator_k_block_size = 16384;
+      out->accumulator_k_block_cap = 16384;
+      out->accumulator_modulus = 0;
+      out->accumulator_max_lhs_abs = 255;
+      out->accumulator_max_rhs_abs = 255;
+      out->accumulator_max_product = 65025;
+      set_text(out->accumulator_input_domain, sizeof(out->accumulator_input_domain), "unsigned_byte_limb");
+      set_text(out->accumulator_signedness, sizeof(out->accumulator_signedness), "unsigned");
+      set_text(out->accumulator_type, sizeof(out->accumulator_type), "uint32");
+      set_text(out->accumulator_modulus_policy, sizeof(out->accumulator_modulus_policy),
+               "low_64_bits_of_36_byte_pair_diagonals");
+      set_text(out->accumulator_safety_status, sizeof(out->accumulator_safety_status), "proven_uint32_safe");
+    }
     return RNS8_SUCCESS;
   });
 }
@@ -539,6 +560,21 @@ extern "C" rns8_status rns8_get_plan_packing_info(const rns8_plan* plan, rns8_pl
     prob.tasks = &task;
     out->accumulator_workspace_bytes = rns8cuda::plane_gemm_scratch_bytes(prob, 148);
     out->total_transient_workspace_bytes = out->accumulator_workspace_bytes;
+    if (plan->desc.semantics == RNS8_WRAP_U64_MOD_2_64) {
+      out->input_domain = RNS8_OUTPUT_DOMAIN_WRAP64_BYTE_LIMB;
+      out->output_domain = RNS8_OUTPUT_DOMAIN_WRAP64_BYTE_LIMB;
+      out->next_op_flags = RNS8_NEXT_OP_FINAL_EXPORT;
+      out->accumulator_workspace_bytes = static_cast<uint64_t>(plan->desc.m) * plan->desc.n * 8;
+      out->total_transient_workspace_bytes = out->accumulator_workspace_bytes;
+      set_text(out->input_domain_name, sizeof(out->input_domain_name), "wrap64_byte_limb");
+      set_text(out->output_domain_name, sizeof(out->output_domain_name), "wrap64_byte_limb");
+      set_text(out->next_op_hint, sizeof(out->next_op_hint), "export_wrap_u64 or chain wrap gemm");
+      set_text(out->a_layout_version, sizeof(out->a_layout_version), "limb_major_compact_row_major_u8_v1");
+      set_text(out->b_layout_version, sizeof(out->b_layout_version), "limb_major_compact_row_major_u8_v1");
+      set_text(out->output_layout_version, sizeof(out->output_layout_version), "limb_major_compact_row_major_u8_v1");
+      set_text(out->detail, sizeof(out->detail), "eight unsigned byte planes in HBM; 36 byte-pair tensor-core products");
+      return RNS8_SUCCESS;
+    }
     set_text(out->input_domain_name, sizeof(out->input_domain_name), "rns_residue");
     set_text(out->output_domain_name, sizeof(out->output_domain_name), finite ? "finite_u8" : "rns_residue");
     set_text(out->next_op_hint, sizeof(out->next_op_hint), finite ? "export_finite_u8" : "export or chain rns gemm");

@@ -143,7 +143,7 @@ extern "C" rns8_status rns8_get_backend_capability_info(rns8_backend_kind backen
     out->supports_bounded_rns = ours ? 1u : 0u;
     out->supports_exact_wide_rns = ours ? 1u : 0u;
     out->supports_finite_u8 = ours ? 1u : 0u;
-    out->supports_wrap64 = 0;
+    out->supports_wrap64 = ours ? 1u : 0u;
     out->requires_feature_detection = ours ? 1u : 0u;
     out->compiled_kernel_available = ours ? 1u : 0u;
     out->exact_differential_validated = ours ? 1u : 0u;
@@ -169,8 +169,9 @@ extern "C" rns8_status rns8_create_matrix(rns8_context* ctx, const rns8_matrix_d
     const uint32_t prefix = desc->max_prefix == 0 ? default_prefix_for_semantics(desc->semantics) : desc->max_prefix;
     const rns8_status v = validate_matrix_desc(*desc, prefix);
     if (v != RNS8_SUCCESS) return v;
-    if (desc->semantics == RNS8_WRAP_U64_MOD_2_64) return RNS8_UNSUPPORTED_BACKEND;
-    const uint64_t planes = uses_finite_storage(desc->semantics) ? 1 : prefix;
+    const bool wrap = desc->semantics == RNS8_WRAP_U64_MOD_2_64;
+    // Residue planes; finite storage has one; wrap64 keeps eight byte planes.
+    const uint64_t planes = wrap ? 8 : (uses_finite_storage(desc->semantics) ? 1 : prefix);
     const uint64_t cells = static_cast<uint64_t>(desc->rows) * static_cast<uint64_t>(desc->cols);
     if (desc->cols != 0 && static_cast<uint64_t>(desc->rows) > UINT64_MAX / static_cast<uint64_t>(desc->cols))
       return RNS8_RANGE_ERROR;
@@ -237,12 +238,20 @@ extern "C" rns8_status rns8_get_matrix_storage_info(const rns8_matrix* m, rns8_m
     out->matrix_instance_id = m->id;
     out->source_version = m->source_version;
     out->host_residues_current = 0;
+    out->hip_device_id = m->device_id;
+    set_text(out->storage_scope, sizeof(out->storage_scope), "device_resident_hbm");
+    if (m->desc.semantics == RNS8_WRAP_U64_MOD_2_64) {
+      out->device_byte_limbs_current = m->device_current ? 1u : 0u;
+      out->uses_byte_limb_storage = 1;
+      out->device_byte_limb_bytes = m->residue_bytes;
+      set_text(out->layout_version, sizeof(out->layout_version), "limb_major_compact_row_major_u8_v1");
+      set_text(out->detail, sizeof(out->detail), "eight unsigned byte planes on device " + std::to_string(m->device_id));
+      return RNS8_SUCCESS;
+    }
     out->device_residues_current = m->device_current ? 1u : 0u;
     out->uses_residue_storage = 1;
-    out->hip_device_id = m->device_id;
     out->device_residue_bytes = m->residue_bytes;
     set_text(out->layout_version, sizeof(out->layout_version), "modulus_major_compact_row_major_i8_v1");
-    set_text(out->storage_scope, sizeof(out->storage_scope), "device_resident_hbm");
     set_text(out->detail, sizeof(out->detail), "centered int8 residue planes on device " + std::to_string(m->device_id));
     return RNS8_SUCCESS;
   });
@@ -267,7 +276,9 @@ extern "C" rns8_status rns8_get_resident_lifetime_info(const rns8_matrix* matrix
     out->bound_kind = matrix->desc.bound_kind;
     out->matrix_role = role;
     const bool finite = uses_finite_storage(matrix->desc.semantics);
-    out->current_output_domain = finite ? RNS8_OUTPUT_DOMAIN_FINITE_U8 : RNS8_OUTPUT_DOMAIN_RNS_RESIDUE;
+    const bool wrap = matrix->desc.semantics == RNS8_WRAP_U64_MOD_2_64;
+    out->current_output_domain = wrap ? RNS8_OUTPUT_DOMAIN_WRAP64_BYTE_LIMB
+                                      : (finite ? RNS8_OUTPUT_DOMAIN_FINITE_U8 : RNS8_OUTPUT_DOMAIN_RNS_RESIDUE);
     out->rows = matrix->desc.rows;
     out->cols = matrix->desc.cols;
     out->logical_ld = matrix->desc.logical_ld;
@@ -292,9 +303,10 @@ extern "C" rns8_status rns8_get_resident_lifetime_info(const rns8_matrix* matrix
       out->workspace_backend_matches = 1;
       out->workspace_schedule_matches = out->workspace_identity_matches;
     }
-    out->can_feed_rns_gemm = (!finite && matrix->device_current) ? 1u : 0u;
+    out->can_feed_rns_gemm = (!finite && !wrap && matrix->device_current) ? 1u : 0u;
     out->can_feed_final_export = matrix->device_current ? 1u : 0u;
-    set_text(out->current_domain, sizeof(out->current_domain), finite ? "finite_u8" : "rns_residue");
+    set_text(out->current_domain, sizeof(out->current_domain),
+             wrap ? "wrap64_byte_limb" : (finite ? "finite_u8" : "rns_residue"));
     const char* names[] = {"unknown", "a", "b", "c"};
     set_text(out->matrix_role_name, sizeof(out->matrix_role_name), names[static_cast<uint32_t>(role)]);
     set_text(out->source_version_policy, sizeof(out->source_version_policy), "nonzero_version_elides_repack");

@@ -193,3 +193,30 @@ extern "C" rns8_status rns8_cuda_export_finite_u8_device(int device_id, const in
   if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::export_finite_u8(d_residues, m, n, modulus, d_dst, ld, as_stream(stream)));
 }
+
+extern "C" rns8_status rns8_cuda_pack_wrap_u64_device(int device_id, const uint64_t* d_src, int64_t rows, int64_t cols,
+                                                    int64_t ld, uint8_t* d_limbs, void* stream) {
+  if (!d_src || !d_limbs || !rns8host::valid_matrix_access(rows, cols, ld)) return RNS8_INVALID_ARGUMENT;
+  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  return launch_result(rns8cuda::wrap_pack_u64(d_src, rows, cols, ld, d_limbs, as_stream(stream)));
+}
+
+extern "C" rns8_status rns8_cuda_gemm_wrap_u64_device(int device_id, const uint8_t* d_a_limbs, const uint8_t* d_b_limbs,
+                                                    uint64_t* d_c, int64_t m, int64_t n, int64_t k,
+                                                    uint32_t gemm_path, uint32_t* d_status, void* stream) {
+  bool ok = false;
+  const rns8cuda::GemmPath path = path_of(gemm_path, &ok);
+  if (!ok || !d_a_limbs || !d_b_limbs || !d_c || m <= 0 || n <= 0 || k <= 0) return RNS8_INVALID_ARGUMENT;
+  if (!rns8host::valid_matrix_access(m, k, k) || !rns8host::valid_matrix_access(k, n, n)) return RNS8_INVALID_ARGUMENT;
+  if (!d_status && path != rns8cuda::GemmPath::Simt) return RNS8_INVALID_ARGUMENT;
+  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  return launch_result(rns8cuda::wrap_gemm(d_a_limbs, d_b_limbs, d_c, m, n, k, path, sm_count_of(device_id), d_status,
+                                           as_stream(stream)));
+}
+
+extern "C" rns8_status rns8_cuda_export_wrap_u64_device(int device_id, const uint8_t* d_limbs, int64_t rows,
+                                                      int64_t cols, uint64_t* d_dst, int64_t ld, void* stream) {
+  if (!d_limbs || !d_dst || !rns8host::valid_matrix_access(rows, cols, ld)) return RNS8_INVALID_ARGUMENT;
+  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  return launch_result(rns8cuda::wrap_export_u64(d_limbs, rows, cols, d_dst, ld, as_stream(stream)));
+}

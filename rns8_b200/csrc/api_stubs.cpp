@@ -101,18 +101,6 @@ rns8_status rns8_gemm_rns_prepacked_b(rns8_context*, const rns8_plan*, const rns
                                       rns8_matrix*, rns8_workspace*) {
   RNS8_UNSUPPORTED;
 }
-rns8_status rns8_gemm_wrap_u64(rns8_context*, const rns8_plan*, const rns8_matrix*, const rns8_matrix*, rns8_matrix*,
-                               rns8_workspace*) {
-  RNS8_UNSUPPORTED;
-}
-rns8_status rns8_export_wrap_u64(rns8_context*, const rns8_plan*, const rns8_matrix*, uint64_t*, int64_t) {
-  RNS8_UNSUPPORTED;
-}
-rns8_status rns8_gemm_wrap_u64_oneshot(rns8_context*, const rns8_gemm_desc*, const uint64_t*, int64_t,
-                                       const uint64_t*, int64_t, uint64_t*, int64_t) {
-  RNS8_UNSUPPORTED;
-}
-
 rns8_status rns8_ozaki_decompose_i64(rns8_context*, const int64_t*, int64_t, int64_t, int64_t, int8_t**, int64_t*,
                                      int*) {
   RNS8_UNSUPPORTED;

@@ -193,4 +193,10 @@ __host__ __device__ constexpr uint32_t make_idesc_i8(uint32_t m, uint32_t n, boo
          | ((m >> 4) << 24);             // M / 16
 }
 
+// Same layout for unsigned 8-bit A and B (formats 0): u8 x u8 -> s32, the
+// accumulator wrapping modulo 2^32 (saturation bit 3 left clear).
+__host__ __device__ constexpr uint32_t make_idesc_u8(uint32_t m, uint32_t n, bool b_mn_major) {
+  return (2u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
 }  // namespace rns8cuda

@@ -23,4 +23,10 @@ TcSchedule tc_schedule(const PlaneGemmProblem& prob, int sm_count);
 cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
                           uint32_t* dev_status, cudaStream_t stream);
 
+// wrap64 on the tensor cores: c (m x n uint64, row-major) = A x B mod 2^64 from
+// 8 byte planes each (k % 16 == 0, n % 16 == 0, 16-byte aligned planes).
+bool tma_encode_available();
+cudaError_t tc_wrap64_gemm(const uint8_t* a_limbs, const uint8_t* b_limbs, uint64_t* c, int64_t m, int64_t n,
+                           int64_t k, int sm_count, uint32_t* dev_status, cudaStream_t stream);
+
 }  // namespace rns8cuda

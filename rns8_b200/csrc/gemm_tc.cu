@@ -1,5 +1,6 @@
 // Tensor-core plane GEMM for sm_100a: C_p = (A_p x B_p) mod m_p over every
-// plane p of every task, in one persistent launch.
+// plane p of every task, in one persistent launch; and the wrap64 byte-plane
+// GEMM (C = A x B mod 2^64) on the same pipeline.
 //
 // Roles (192 threads, one CTA per SM):
 //   warp 0      one thread issues TMA loads of A (128 x 128, K-major) and B
@@ -284,6 +285,228 @@ __global__ void __launch_bounds__(256) split_finalize_kernel(const int32_t* __re
   }
 }
 
+// ---- wrap64: C = A x B mod 2^64 from unsigned byte planes ---------------------
+// With A = sum_i 2^(8i) A_i and B = sum_j 2^(8j) B_j (byte planes), the low 64
+// bits of A x B are sum_{d<8} 2^(8d) S_d with S_d = sum_{i+j=d} A_i x B_j: the
+// 36 byte-pair products of the low eight Comba diagonals (reference
+// src/backend_wrap64/wrap64_reference.cpp:105-117). A work unit is one output
+// tile over one K range; it runs the diagonals in order, each as one u8 x u8
+// MMA chain over (K block, byte pair) into a 32-bit TMEM accumulator, and the
+// epilogue adds S_d * 2^(8d) into the 64-bit output with wrapping atomic adds
+// (the output is zeroed first). Only S_d mod 2^(64-8d) matters: for d >= 4 that
+// is S_d mod 2^32, which the accumulator keeps whatever K is; for d <= 3 a unit
+// spans at most 16384 products, so S_d <= 4 * 16384 * 255^2 < 2^32 is exact.
+// Longer K is split into several units whose sums the atomics add up.
+constexpr int kWrapMaxKbPerUnit = 16384 / BK;  // 128
+
+struct __align__(64) WrapParams {
+  CUtensorMap tmA;  // (k, m, 8) byte planes of A
+  CUtensorMap tmB;  // (n, k, 8) byte planes of B
+  unsigned long long* C;
+  int64_t m, n;
+  uint32_t m_tiles, n_tiles, total_kb, splits, kb_per_split;
+  uint64_t units;
+  uint32_t* status;
+};
+
+struct WrapUnit {
+  uint32_t mt, nt, kb0, kb1;
+};
+
+__device__ __forceinline__ WrapUnit decode_wrap_unit(const WrapParams& prm, uint64_t u) {
+  const uint64_t tiles = static_cast<uint64_t>(prm.m_tiles) * prm.n_tiles;
+  const uint64_t tile = u % tiles;
+  const uint32_t s = static_cast<uint32_t>(u / tiles);
+  WrapUnit w;
+  const uint32_t span = GROUP_M * prm.n_tiles;
+  const uint32_t group = static_cast<uint32_t>(tile / span);
+  const uint32_t first_m = group * GROUP_M;
+  const uint32_t gsize = min(prm.m_tiles - first_m, static_cast<uint32_t>(GROUP_M));
+  const uint32_t in_group = static_cast<uint32_t>(tile % span);
+  w.mt = first_m + in_group % gsize;
+  w.nt = in_group / gsize;
+  w.kb0 = s * prm.kb_per_split;
+  w.kb1 = min(prm.total_kb, w.kb0 + prm.kb_per_split);
+  return w;
+}
+
+__device__ __forceinline__ void report_wrap_timeout(uint32_t* status, volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicOr(status, kDevWaitTimeout);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) tc_wrap64_kernel(const __grid_constant__ WrapParams prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&prm.tmA);
+    tma_prefetch_desc(&prm.tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: (diagonal, K block, byte pair) ----------------
+      uint32_t stage = 0, phase = 0;
+      uint32_t pending = 0, pending_parity = 0;
+      bool ok = true;
+      for (uint64_t u = blockIdx.x; ok && u < prm.units; u += gridDim.x) {
+        const WrapUnit w = decode_wrap_unit(prm, u);
+        for (int d = 0; ok && d < 8; ++d) {
+          for (uint32_t kb = w.kb0; ok && kb < w.kb1; ++kb) {
+            for (int i = 0; i <= d; ++i) {
+              if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
+                if (!*abort_flag) report_wrap_timeout(prm.status, abort_flag);
+                ok = false;
+                break;
+              }
+              pending &= ~(1u << stage);
+              mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+              uint8_t* sa = smem + stage * STAGE_BYTES;
+              uint8_t* sb = sa + A_BYTES;
+              const int32_t kc = static_cast<int32_t>(kb * BK);
+              tma_load_3d(sa, &prm.tmA, &full[stage], kc, static_cast<int32_t>(w.mt * BM), i);
+              tma_load_3d(sb, &prm.tmB, &full[stage], static_cast<int32_t>(w.nt * BN), kc, d - i);
+              tma_load_3d(sb + B_HALF_BYTES, &prm.tmB, &full[stage], static_cast<int32_t>(w.nt * BN + 128), kc, d - i);
+              pending |= 1u << stage;
+              pending_parity = (pending_parity & ~(1u << stage)) | (phase << stage);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+          }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s)
+        if (pending & (1u << s)) (void)mbar_wait_bounded(&full[s], (pending_parity >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer: one accumulator per diagonal ----------------
+      constexpr uint32_t idesc = make_idesc_u8(BM, BN, /*b_mn_major=*/true);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (uint64_t u = blockIdx.x; ok && u < prm.units; u += gridDim.x) {
+        const WrapUnit w = decode_wrap_unit(prm, u);
+        for (int d = 0; ok && d < 8; ++d) {
+          if (*abort_flag || !mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u)) {
+            if (!*abort_flag) report_wrap_timeout(prm.status, abort_flag);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+          bool first = true;
+          for (uint32_t kb = w.kb0; ok && kb < w.kb1; ++kb) {
+            for (int i = 0; i <= d; ++i) {
+              if (*abort_flag || !mbar_wait_bounded(&full[stage], phase)) {
+                if (!*abort_flag) report_wrap_timeout(prm.status, abort_flag);
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+              const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+              for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                const uint64_t adesc = make_smem_desc_sw128(sa + kk * UMMA_K, 16, 1024);
+                const uint64_t bdesc = make_smem_desc_sw128(sb + kk * UMMA_K * 128, B_HALF_BYTES, 1024);
+                tc_mma_i8(d_tmem, adesc, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
+              }
+              first = false;
+              tc_commit(&empty[stage]);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+          }
+          if (!ok) break;
+          tc_commit(&acc_full[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+        }
+      }
+      tc_commit(drain);
+      (void)mbar_wait_bounded(drain, 0);
+    }
+  } else {
+    // ---------------- epilogue: C += S_d * 2^(8d) ----------------
+    const uint32_t quarter = static_cast<uint32_t>(warp & 3);
+    uint32_t acc = 0, acc_phase = 0;
+    bool ok = true;
+    for (uint64_t u = blockIdx.x; ok && u < prm.units; u += gridDim.x) {
+      const WrapUnit w = decode_wrap_unit(prm, u);
+      const int64_t row = static_cast<int64_t>(w.mt) * BM + quarter * 32 + lane;
+      const bool row_ok = row < prm.m;
+      unsigned long long* crow = prm.C + row * prm.n;
+      for (int d = 0; d < 8; ++d) {
+        if (*abort_flag || !mbar_wait_bounded(&acc_full[acc], acc_phase)) {
+          if (!*abort_flag) report_wrap_timeout(prm.status, abort_flag);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS + c * 32, v);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(w.nt) * BN + c * 32;
+          if (!row_ok || col >= prm.n) continue;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col + j < prm.n) atomicAdd(crow + col + j, static_cast<unsigned long long>(v[j]) << (8 * d));
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
 // ---- host side ---------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -399,6 +622,48 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+// ---- wrap64 host side -----------------------------------------------------------
+bool tma_encode_available() { return encode_fn() != nullptr; }
+
+cudaError_t tc_wrap64_gemm(const uint8_t* a_limbs, const uint8_t* b_limbs, uint64_t* c, int64_t m, int64_t n,
+                           int64_t k, int sm_count, uint32_t* dev_status, cudaStream_t stream) {
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(tc_wrap64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(SMEM_BYTES));
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  WrapParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  if (!encode_planes(&prm.tmA, a_limbs, static_cast<uint64_t>(k), static_cast<uint64_t>(m), 8) ||
+      !encode_planes(&prm.tmB, b_limbs, static_cast<uint64_t>(n), static_cast<uint64_t>(k), 8))
+    return cudaErrorInvalidValue;
+  prm.m_tiles = static_cast<uint32_t>((m + BM - 1) / BM);
+  prm.n_tiles = static_cast<uint32_t>((n + BN - 1) / BN);
+  prm.total_kb = static_cast<uint32_t>((k + BK - 1) / BK);
+  const uint64_t tiles = static_cast<uint64_t>(prm.m_tiles) * prm.n_tiles;
+  uint32_t splits = (prm.total_kb + kWrapMaxKbPerUnit - 1) / kWrapMaxKbPerUnit;
+  if (tiles * splits < static_cast<uint64_t>(sm_count) && prm.total_kb >= 8) {
+    const uint64_t want = (static_cast<uint64_t>(sm_count) + tiles - 1) / tiles;
+    const uint32_t cap = prm.total_kb / 4;
+    const uint32_t target = static_cast<uint32_t>(want < cap ? want : cap);
+    if (target > splits) splits = target;
+  }
+  prm.kb_per_split = (prm.total_kb + splits - 1) / splits;
+  prm.splits = (prm.total_kb + prm.kb_per_split - 1) / prm.kb_per_split;
+  prm.units = tiles * prm.splits;
+  prm.C = reinterpret_cast<unsigned long long*>(c);
+  prm.m = m;
+  prm.n = n;
+  prm.status = dev_status;
+  cudaError_t e = cudaMemsetAsync(c, 0, static_cast<size_t>(m) * n * sizeof(uint64_t), stream);
+  if (e != cudaSuccess) return e;
+  const uint64_t grid = prm.units < static_cast<uint64_t>(sm_count) ? prm.units : static_cast<uint64_t>(sm_count);
+  tc_wrap64_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM_BYTES, stream>>>(prm);
+  return cudaGetLastError();
 }
 
 // ---- dispatch --------------------------------------------------------------

@@ -72,6 +72,21 @@ cudaError_t export_limbs(const int8_t* planes, int64_t m, int64_t n, uint32_t pr
 cudaError_t export_finite_u8(const int8_t* residues, int64_t m, int64_t n, uint32_t modulus, uint8_t* dst, int64_t ld,
                              cudaStream_t stream);
 
+// ---- WRAP_U64_MOD_2_64 (reference src/backend_wrap64/) -----------------------------
+// uint64 (row-major, ld >= cols) -> 8 limb-major byte planes [8][rows][cols].
+cudaError_t wrap_pack_u64(const uint64_t* src, int64_t rows, int64_t cols, int64_t ld, uint8_t* planes,
+                          cudaStream_t stream);
+// 8 byte planes -> uint64 dst[row * ld + col].
+cudaError_t wrap_export_u64(const uint8_t* planes, int64_t rows, int64_t cols, uint64_t* dst, int64_t ld,
+                            cudaStream_t stream);
+bool wrap_tensor_core_supported(const uint8_t* a, const uint8_t* b, const uint64_t* c, int64_t m, int64_t n,
+                                int64_t k);
+// c (m x n uint64, compact row-major) = A x B mod 2^64 from byte planes. The
+// tensor-core path ORs kDevWaitTimeout into *dev_status if a wait runs out.
+cudaError_t wrap_gemm(const uint8_t* a_limbs, const uint8_t* b_limbs, uint64_t* c, int64_t m, int64_t n, int64_t k,
+                      GemmPath path, int sm_count, uint32_t* dev_status, cudaStream_t stream,
+                      GemmPath* used = nullptr);
+
 // ---- exact-wide admission (reference src/core/exact_range.hpp:51-154) ------------
 // Summary of one row or column of native int64/uint64 values: max |v|, sum |v|,
 // sum v, min, max and sum |v - center| with center = (min + max) / 2

@@ -115,6 +115,20 @@ def reference_kats() -> dict:
                              "cases": [["i64", 2**49, 0, 0, 7], ["i64", 2**61, 0, 0, 8], ["i64", 2**61, 9, 1, 9],
                                        ["u64", 2**62, 0, 0, 8], ["i64", 2**63, 0, 0, 9], ["u64", 2**64 - 1, 0, 0, 9]]},
     }
+    # wrap64 public-path inputs of the reference's differential test (padded
+    # lda = 6, ldb = 4); the expected cells are sum a*b mod 2^64, the value
+    # wrap64_reference.cpp:254-290 computes.
+    u64max = 2**64 - 1
+    wa = [0, 1, u64max, 0x8080808080808080, 0x0102030405060708, 0xAAAA,
+          255, 256, u64max - 1, 0x7F7F7F7F7F7F7F7F, 17, 0xBBBB]
+    wb = [3, u64max, 0x1112131415161718, 0xCCCC, 29, 0x8080808080808080, 31, 0xDDDD,
+          0x0101010101010101, 0xFEFDFCFBFAF9F8F7, 37, 0xEEEE, 41, 43, 47, 0xFFFF, 53, 59, 61, 0x1234]
+    m, n, k, lda, ldb = 2, 3, 5, 6, 4
+    kats["wrap64_public_2x3x5"] = {
+        "source": "tests/differential/test_hip_direct_wrap64_public_cases.inc:6-45",
+        "m": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "A": [str(v) for v in wa], "B": [str(v) for v in wb],
+        "expected": [[str(sum(wa[r * lda + q] * wb[q * ldb + c] for q in range(k)) % 2**64) for c in range(n)]
+                     for r in range(m)]}
     # Expected values for the 2x3x4 ring GEMM KAT.
     A = np.array(kats["ring_gemm_2x3x4"]["A"]).reshape(2, 4)
     B = np.array(kats["ring_gemm_2x3x4"]["B"]).reshape(4, 3)

@@ -87,7 +87,8 @@ def test_unsupported_surfaces_leave_outputs_untouched(rns8):
     out = C.c_void_p(1234)
     assert lib.rns8_create_result_cache(None, None, None, C.byref(out)) == rns8.Status.UNSUPPORTED_BACKEND
     assert out.value is None
-    assert lib.rns8_gemm_wrap_u64_oneshot(None, None, None, 0, None, 0, None, 0) == rns8.Status.UNSUPPORTED_BACKEND
+    # wrap64 is implemented: null arguments are malformed, as in the reference (api_oneshot.cpp:597-599).
+    assert lib.rns8_gemm_wrap_u64_oneshot(None, None, None, 0, None, 0, None, 0) == rns8.Status.INVALID_ARGUMENT
     assert lib.rns8_freivalds_verify(None, None, None, None, 0, 0, None) == rns8.Status.UNSUPPORTED_BACKEND
     assert lib.rns8_destroy_plan(None) == 0 and lib.rns8_destroy_matrix(None) == 0
 

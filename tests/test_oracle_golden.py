@@ -280,3 +280,30 @@ def test_exact_wide_limbs_round_trip(oracle):
             assert v == exact[i][j]
     st, _ = oracle.export_limbs(planes, P, 1, signed=True)
     assert st == RANGE  # products of full-range int64 need more than 64 bits
+
+
+# ---- WRAP_U64_MOD_2_64 -------------------------------------------------------------
+def test_wrap64_public_kat(oracle):
+    """Inputs of the reference's public wrap64 differential test (padded lda/ldb)."""
+    kat = KATS["wrap64_public_2x3x5"]
+    m, n, k = kat["m"], kat["n"], kat["k"]
+    A = np.array([int(v) for v in kat["A"]], np.uint64).reshape(m, kat["lda"])[:, :k]
+    B = np.array([int(v) for v in kat["B"]], np.uint64).reshape(k, kat["ldb"])[:, :n]
+    want = np.array([[int(v) for v in row] for row in kat["expected"]], np.uint64)
+    np.testing.assert_array_equal(oracle.wrap64_gemm(A, B), want)
+    np.testing.assert_array_equal(oracle.wrap64_gemm(A, B, diagonals=True), want)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (7, 5, 33), (16, 24, 300)])
+def test_wrap64_oracles_agree(oracle, m, n, k):
+    """Native uint64 accumulation (wrap64_reference.cpp:254-290) and the 36-pair
+    Comba-diagonal restatement (:166-190) agree, and match numpy's wrapping
+    uint64 matmul, on random and extreme values."""
+    rng = np.random.default_rng(m * 100 + k)
+    A = rng.integers(0, 2**64 - 1, (m, k), dtype=np.uint64, endpoint=True)
+    B = rng.integers(0, 2**64 - 1, (k, n), dtype=np.uint64, endpoint=True)
+    A[0, :] = 2**64 - 1
+    B[:, 0] = 0x8080808080808080
+    want = A @ B  # numpy integer matmul wraps modulo 2^64
+    np.testing.assert_array_equal(oracle.wrap64_gemm(A, B), want)
+    np.testing.assert_array_equal(oracle.wrap64_gemm(A, B, diagonals=True), want)
