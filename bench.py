@@ -8,11 +8,13 @@ int8 planes, nine int8 plane GEMMs (one persistent tcgen05 launch), export to
 int64 (fractional CRT, exact Garner for undecided cells).
 
 The other BASELINE configs run with --config C1|C2|C4|C5 (same metric, same
-JSON line; they are measurements for the record, the driver runs C3):
+JSON line; they are measurements for the record, the driver runs C3), and
+--config W runs the WRAP_U64_MOD_2_64 path at the C3 shape:
   C1  int64 512^3, U[-2^20, 2^20], bound 2^49, prefix 7 (default plan)
   C2  finite field 251, 64 independent 2048^3 pairs, grouped GEMM
   C4  uint64 256 x 256 x 262144, U[0, 2^22), bound 2^62, prefix 8 (split-K)
   C5  exact-wide signed int64 4096^3, full int64 range, 3 limbs, prefix 20 forced
+  W   uint64 8192^3 modulo 2^64, full uint64 range
 
   value  device-resident: inputs already in HBM, output left in HBM, timed
          with CUDA events on the launching stream (max over ranks).
@@ -25,7 +27,7 @@ slab of A and C of the config's size and a full B (weak scaling, no collective
 on the data path); value = all ranks' work / max-over-ranks time.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config C1..C5] [--size S (C3 only: M = N = K = S)]
+                  [--config C1..C5|W] [--size S (C3 only: M = N = K = S)]
 """
 
 from __future__ import annotations
@@ -57,7 +59,7 @@ class Config:
     k: int
     lo: int
     hi: int
-    prefix: int          # residue planes per matrix (1 for finite)
+    prefix: int          # residue planes per matrix (1 for finite, 8 byte planes for wrap)
     forced: bool         # RNS8_PLAN_FORCE_FIXED_PREFIX
     workload: str
     bound: int = 0
@@ -88,6 +90,10 @@ CONFIGS = {
     "C5": Config("C5", "exact", 4096, 4096, 4096, -(2**63), 2**63 - 1, 20, True,
                  "RNS8_EXACT_WIDE_SIGNED 4096^3, U[INT64_MIN,INT64_MAX], 3 limbs, prefix 20 forced "
                  "(BASELINE config 5)", limbs=3, cpu_rows=16),
+    # Not a BASELINE config: the WRAP_U64_MOD_2_64 path at the C3 shape.
+    "W": Config("W", "wrap", 8192, 8192, 8192, 0, 2**64 - 1, 8, False,
+                "RNS8_WRAP_U64_MOD_2_64 8192^3, U[0,2^64) (36 byte-pair products on the tensor cores)",
+                cpu_rows=64),
 }
 
 
@@ -233,7 +239,7 @@ def host_inputs(cfg: Config, rows: int, seed: int):
     if cfg.kind == "finite":
         A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.uint8, endpoint=True)
         B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.uint8, endpoint=True)
-    elif cfg.kind == "u64":
+    elif cfg.kind in ("u64", "wrap"):
         A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.uint64, endpoint=True)
         B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.uint64, endpoint=True)
     else:
@@ -256,6 +262,15 @@ def cpu_baseline(cfg: Config, rows: int) -> dict:
     threads = lib.oracle_max_threads()
     A, B = host_inputs(cfg, rows, 123)
     P = cfg.prefix
+    if cfg.kind == "wrap":  # wrap64_reference.cpp:254-290 on the slab; packing is a byte copy
+        t0 = time.perf_counter()
+        out = bridge.wrap64_gemm(A, B)
+        t_slab = time.perf_counter() - t0
+        full = cfg.m / rows * t_slab
+        return {"value": cfg.ops / full / 1e9, "unit": "GOPS", "cores": threads, "kind": "port",
+                "sample": f"oracle wrap64 GEMM (native uint64 multiply-add) on a {rows}-row slab of A in "
+                          f"{t_slab:.2f} s; step = {cfg.m}/{rows} x t_slab = {full:.1f} s; {threads} threads",
+                "seconds": t_slab, "step_seconds": full}
     t0 = time.perf_counter()
     if cfg.kind == "finite":
         b = bridge.pack_finite_u8(B, cfg.modulus)
@@ -329,6 +344,16 @@ class DevicePipeline:
             self.pb = vp(*[self.rb[t].data_ptr() for t in range(bt)])
             self.pc = vp(*[self.rc[t].data_ptr() for t in range(bt)])
             self.sbytes = lib.rns8_cuda_gemm_finite_u8_scratch_bytes(dev, m, n, k, bt)
+        elif cfg.kind == "wrap":
+            self.A = torch.randint(0, 256, (m, k, 8), dtype=torch.uint8, device="cuda", generator=g).view(
+                torch.int64).reshape(m, k)
+            self.B = torch.randint(0, 256, (k, n, 8), dtype=torch.uint8, device="cuda", generator=gb).view(
+                torch.int64).reshape(k, n)
+            self.ra = torch.empty((8, m, k), dtype=torch.uint8, device="cuda")
+            self.rb = torch.empty((8, k, n), dtype=torch.uint8, device="cuda")
+            self.rc = torch.empty((1,), dtype=torch.uint8, device="cuda")
+            self.out = torch.empty((m, n), dtype=torch.int64, device="cuda")
+            self.sbytes = 0
         else:
             if cfg.kind == "exact":  # full int64 range: uniform random bytes
                 self.A = torch.randint(0, 256, (m, k, 8), dtype=torch.uint8, device="cuda", generator=g).view(
@@ -347,7 +372,7 @@ class DevicePipeline:
         self.scratch = torch.empty(max(1, self.sbytes), dtype=torch.uint8, device="cuda")
         self.status = torch.zeros(4, dtype=torch.int32, device="cuda")
         gemm_launches = (1 + (1 if self.sbytes > 0 else 0)) * ((bt + 31) // 32 if cfg.kind == "finite" else 1)
-        self.launches_per_step = 2 + gemm_launches + 1
+        self.launches_per_step = 2 + gemm_launches + (0 if cfg.kind == "wrap" else 1)
         footprint = sum(t.numel() * t.element_size() for t in (self.A, self.B, self.ra, self.rb, self.rc, self.out))
         self.fits_l2 = footprint < (512 << 20)  # L2 is 126 MB: below this, flush it between steps
 
@@ -365,12 +390,23 @@ class DevicePipeline:
             self._check(lib.rns8_cuda_pack_finite_u8_device(d, self.B.data_ptr(), bt * k, n, n, cfg.modulus,
                                                             self.rb.data_ptr(), s), "pack B")
             return
+        if cfg.kind == "wrap":
+            self._check(lib.rns8_cuda_pack_wrap_u64_device(d, self.A.data_ptr(), m, k, k, self.ra.data_ptr(), s),
+                        "pack A")
+            self._check(lib.rns8_cuda_pack_wrap_u64_device(d, self.B.data_ptr(), k, n, n, self.rb.data_ptr(), s),
+                        "pack B")
+            return
         fn = lib.rns8_cuda_pack_u64_device if cfg.kind == "u64" else lib.rns8_cuda_pack_i64_device
         self._check(fn(d, self.A.data_ptr(), m, k, k, cfg.prefix, self.ra.data_ptr(), s), "pack A")
         self._check(fn(d, self.B.data_ptr(), k, n, n, cfg.prefix, self.rb.data_ptr(), s), "pack B")
 
     def gemm(self):
         cfg, lib, d, s = self.cfg, self.lib, self.dev, self.sptr
+        if cfg.kind == "wrap":  # C = A x B mod 2^64, left in HBM as uint64
+            self._check(lib.rns8_cuda_gemm_wrap_u64_device(d, self.ra.data_ptr(), self.rb.data_ptr(),
+                                                           self.out.data_ptr(), cfg.m, cfg.n, cfg.k, 0,
+                                                           self.status.data_ptr(), s), "wrap gemm")
+            return
         if cfg.kind == "finite":
             self._check(lib.rns8_cuda_gemm_finite_u8_grouped_device(
                 d, self.pa, self.pb, self.pc, cfg.batch, cfg.m, cfg.n, cfg.k, cfg.modulus, 0,
@@ -383,6 +419,8 @@ class DevicePipeline:
     def export(self):
         cfg, lib, d, s = self.cfg, self.lib, self.dev, self.sptr
         m, n = cfg.m, cfg.n
+        if cfg.kind == "wrap":
+            return  # the GEMM already wrote uint64 C
         if cfg.kind == "finite":
             st = lib.rns8_cuda_export_finite_u8_device(d, self.rc.data_ptr(), cfg.batch * m, n, cfg.modulus,
                                                        self.out.data_ptr(), n, s)
@@ -413,6 +451,9 @@ class DevicePipeline:
         m, n, k, P, bt = cfg.m, cfg.n, cfg.k, cfg.prefix, cfg.batch
         elem_in = 1 if cfg.kind == "finite" else 8
         out_bytes = {"finite": 1, "exact": 8 * cfg.limbs}.get(cfg.kind, 8)
+        if cfg.kind == "wrap":  # 36 u8 x u8 products per cell and k; no export stage
+            return {"pack": ("hbm", 16 * (m * k + k * n)), "plane_gemm": ("tensor", 36 * 2.0 * m * n * k),
+                    "export": ("hbm", 0)}
         return {
             "pack": ("hbm", bt * (elem_in + P) * (m * k + k * n)),
             "plane_gemm": ("tensor", bt * P * 2.0 * m * n * k),
@@ -431,7 +472,11 @@ class EndToEnd:
         self.hB = pipe.B.cpu().pin_memory()
         self.hC = torch.empty(tuple(pipe.out.shape), dtype=pipe.out.dtype).pin_memory()
         S = r8.Semantics
-        if cfg.kind in ("i64", "u64"):
+        if cfg.kind == "wrap":
+            self.desc = r8.gemm_desc(S.WRAP_U64_MOD_2_64, r8.BoundKind.NONE, m, n, k)
+            self.oneshot = lib.rns8_gemm_wrap_u64_oneshot
+            self.api = "rns8_gemm_wrap_u64_oneshot (pinned host buffers)"
+        elif cfg.kind in ("i64", "u64"):
             signed = cfg.kind == "i64"
             self.desc = r8.gemm_desc(S.BOUNDED_I64 if signed else S.BOUNDED_U64,
                                      r8.BoundKind.GLOBAL_MAX_ABS if signed else r8.BoundKind.GLOBAL_MAX_UNSIGNED,
@@ -466,7 +511,7 @@ class EndToEnd:
 
     def run(self):
         cfg, r8, lib = self.cfg, self.r8, self.lib
-        if cfg.kind in ("i64", "u64"):
+        if cfg.kind in ("i64", "u64", "wrap"):
             st = self.oneshot(self.ctx.handle, C.byref(self.desc), self.hA.data_ptr(), cfg.k, self.hB.data_ptr(),
                               cfg.n, self.hC.data_ptr(), cfg.n)
             DevicePipeline._check(st, self.api)
@@ -592,10 +637,11 @@ def main():
     dominant = max(stage_ms, key=stage_ms.get)
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     hbm_note = "MEASURED_PEAKS.json hbm_gbs (STREAM copy)" if not peaks.get("fallback") else "fallback 6650 GB/s"
-    kernel_names = {"pack": "pack_kernel", "plane_gemm": "tc_plane_gemm_kernel", "export": "export kernel"}
+    kernel_names = {"pack": "pack_kernel", "plane_gemm": "tc_wrap64_kernel" if cfg.kind == "wrap" else
+                    "tc_plane_gemm_kernel", "export": "export kernel"}
     stage_frac = {}
     for name, (bound, amount) in work.items():
-        sec = stage_ms[name] * 1e-3
+        sec = max(stage_ms[name], 1e-6) * 1e-3
         stage_frac[name] = (amount / sec / 1e12 / peak_int8) if bound == "tensor" else (amount / sec / 1e9 / hbm)
     bound, amount = work[dominant]
     sec = stage_ms[dominant] * 1e-3
@@ -612,7 +658,8 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "GOPS", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "uint8" if cfg.kind == "finite" else "int64", "data": "synthetic",
+            "vs_baseline": None, "dtype": {"finite": "uint8", "wrap": "uint64"}.get(cfg.kind, "int64"),
+            "data": "synthetic",
             "config": {"workload": cfg.workload, "name": cfg.name, "m_per_rank": cfg.m, "n": cfg.n, "k": cfg.k,
                        "batch": cfg.batch, "prefix": cfg.prefix, "parallelism": f"row-slab x{world}",
                        "l2": "L2 flushed between steps (256 MiB write outside the step's events)"
