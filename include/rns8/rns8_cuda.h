@@ -165,6 +165,14 @@ RNS8_API rns8_status rns8_cuda_exact_gemm_bound_device(int device_id, const void
 RNS8_API rns8_status rns8_cuda_plan_probe(const rns8_gemm_desc* desc, uint32_t* selected_prefix,
                                           uint32_t* required_prefix, uint64_t* effective_bound);
 
+/* Host-only: the tile schedule rns8_create_plan would build for a descriptor
+ * (per-tile bound plans: required and selected prefix, group and flags per
+ * tile), with the rns8_get_plan_tile_schedule contract (written = tile count;
+ * RNS8_WORKSPACE_TOO_SMALL when capacity is short). info may be NULL. */
+RNS8_API rns8_status rns8_cuda_plan_tile_schedule_probe(const rns8_gemm_desc* desc,
+                                                        rns8_plan_tile_schedule_entry* entries, uint64_t capacity,
+                                                        uint64_t* written, rns8_plan_schedule_info* info);
+
 #ifdef __cplusplus
 }
 #endif

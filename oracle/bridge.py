@@ -50,6 +50,9 @@ _SIGS = {
     "oracle_exact_gemm_admission": (C.c_int, [C.c_int, vp, i64, vp, i64, i64, i64, i64, u32, vp, vp, vp]),
     "oracle_exact_gemm_cell_stats": (C.c_int, [C.c_int, vp, i64, vp, i64, i64, i64, i64, vp, vp]),
     "oracle_wrap64_gemm": (None, [vp, i64, vp, i64, vp, i64, i64, i64, i64]),
+    "oracle_plan_tile_schedule": (C.c_int, [u32, i64, i64, u32, u32, u32, u32, vp, vp, vp, vp, vp]),
+    "oracle_gemm_rns_scheduled": (None, [vp, vp, vp, i64, i64, i64, u32, u32, vp]),
+    "oracle_export_scheduled": (C.c_int, [vp, i64, i64, u32, u32, vp, vp, C.c_int, vp, i64]),
     "oracle_wrap64_gemm_diagonals": (None, [vp, i64, vp, i64, vp, i64, i64, i64, i64]),
     "oracle_rng_new": (C.c_int, [u64]),
     "oracle_rng_free": (None, [C.c_int]),
@@ -253,6 +256,41 @@ def wrap64_gemm(A: np.ndarray, B: np.ndarray, diagonals: bool = False) -> np.nda
     fn = lib().oracle_wrap64_gemm_diagonals if diagonals else lib().oracle_wrap64_gemm
     fn(_p(A), _ld(A), _p(B), _ld(B), _p(out), n, m, n, k)
     return out
+
+
+def plan_tile_schedule(semantics: int, m: int, n: int, tile_m: int, tile_n: int, max_prefix: int, flags: int,
+                       tile_bounds, zero_a_rows=None, zero_b_cols=None):
+    """(status, per-tile rows (required, selected, group, range_bits, flags), summary dict)."""
+    tiles = -(-m // tile_m) * -(-n // tile_n)
+    tb = np.ascontiguousarray(np.asarray(tile_bounds, np.uint64))
+    za = np.ascontiguousarray(np.asarray(zero_a_rows if zero_a_rows is not None else np.zeros(m), np.uint8))
+    zb = np.ascontiguousarray(np.asarray(zero_b_cols if zero_b_cols is not None else np.zeros(n), np.uint8))
+    out = np.zeros((tiles, 5), np.uint32)
+    summ = np.zeros(10, np.uint32)
+    st = lib().oracle_plan_tile_schedule(semantics, m, n, tile_m, tile_n, max_prefix, flags, _p(tb), _p(za), _p(zb),
+                                         _p(out), _p(summ))
+    keys = ["min_required", "max_required", "min_selected", "max_selected", "group_count", "range_bits",
+            "adaptive_prefix", "adaptive_skip", "flags", "collapsed"]
+    return int(st), out, dict(zip(keys, (int(v) for v in summ)))
+
+
+def gemm_rns_scheduled(a: np.ndarray, b: np.ndarray, c: np.ndarray, tile_m: int, tile_n: int, sel) -> np.ndarray:
+    """C planes updated in place under a tile schedule (sel: prefix | 0x80 for proven zero)."""
+    _, m, k = a.shape
+    n = b.shape[2]
+    s = np.ascontiguousarray(np.asarray(sel, np.uint8))
+    lib().oracle_gemm_rns_scheduled(_p(a), _p(b), _p(c), m, n, k, tile_m, tile_n, _p(s))
+    return c
+
+
+def export_scheduled(planes: np.ndarray, tile_m: int, tile_n: int, sel, tile_bounds, signed: bool):
+    _, m, n = planes.shape
+    s = np.ascontiguousarray(np.asarray(sel, np.uint8))
+    tb = np.ascontiguousarray(np.asarray(tile_bounds, np.uint64))
+    out = np.zeros((m, n), np.int64 if signed else np.uint64)
+    st = lib().oracle_export_scheduled(_p(np.ascontiguousarray(planes)), m, n, tile_m, tile_n, _p(s), _p(tb),
+                                       1 if signed else 0, _p(out), n)
+    return int(st), out
 
 
 class Rng:

@@ -17,6 +17,7 @@
 // this library, and only as the checker or the timed CPU baseline. The
 // product library (rns8_b200) never links or calls it.
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <cmath>
@@ -837,6 +838,119 @@ OX int oracle_exact_gemm_cell_stats(int is_signed, const void* A, int64_t lda, c
     write_w(cmax[c], col_stats + 8 * c);
     write_w(csum[c], col_stats + 8 * c + 4);
   }
+  return ST_SUCCESS;
+}
+
+// ---- per-tile bound schedules ---------------------------------------------------
+// configure_plan_schedule for per-tile bounds (api_plan_schedule.inc:178-261).
+// out5[5*t..]: required, selected, group index, range bits, flags of tile t.
+// summary[10]: min/max required, min/max selected, group count, max range
+// bits, adaptive prefix, adaptive skip, schedule flags, collapsed (1 when the
+// schedule is trivial and the reference clears it).
+OX int oracle_plan_tile_schedule(uint32_t semantics, int64_t m, int64_t n, uint32_t tile_m, uint32_t tile_n,
+                                 uint32_t max_prefix, uint32_t flags, const uint64_t* tile_bounds,
+                                 const uint8_t* zero_a_rows, const uint8_t* zero_b_cols, uint32_t* out5,
+                                 uint32_t* summary) {
+  const uint32_t prefix = max_prefix ? max_prefix : default_prefix_for_semantics(semantics);
+  const int64_t tile_rows = (m + tile_m - 1) / tile_m, tile_cols = (n + tile_n - 1) / tile_n;
+  const bool fixed = (flags & FLAG_FORCE) != 0;
+  const bool zero_tiles = (flags & 2u) != 0, zero_rc = (flags & 4u) != 0;
+  uint32_t min_req = UINT32_MAX, max_req = 0, min_sel = UINT32_MAX, max_sel = 0, max_bits = 0, sched_flags = 0;
+  std::vector<uint32_t> groups;
+  const int64_t tiles = tile_rows * tile_cols;
+  for (int64_t t = 0; t < tiles; ++t) {
+    const uint64_t bound = tile_bounds[t];
+    if (semantics == SEM_I64 && bound > (uint64_t{1} << 63)) return ST_INVALID;
+    const wide256 range = semantics == SEM_I64 ? w_mul(w_u64(2), w_u64(bound)) : w_u64(bound);
+    const uint32_t bits = w_bit_length(range);
+    const uint32_t req = required_prefix_for_range(range);
+    if (req == 0 || req > prefix) return ST_RANGE;
+    const uint32_t sel = fixed ? prefix : req;
+    min_req = std::min(min_req, req);
+    max_req = std::max(max_req, req);
+    min_sel = std::min(min_sel, sel);
+    max_sel = std::max(max_sel, sel);
+    max_bits = std::max(max_bits, bits);
+    bool seen = false;
+    for (uint32_t g : groups) seen = seen || g == sel;
+    if (!seen) groups.push_back(sel);
+    uint32_t f = (zero_tiles && bound == 0) ? 1u : 0u;
+    if (zero_rc) {
+      const int64_t r0 = (t / tile_cols) * tile_m, c0 = (t % tile_cols) * tile_n;
+      const int64_t r1 = std::min<int64_t>(m, r0 + tile_m), c1 = std::min<int64_t>(n, c0 + tile_n);
+      bool hit = false;
+      for (int64_t r = r0; r < r1; ++r) hit = hit || zero_a_rows[r] != 0;
+      for (int64_t c = c0; c < c1; ++c) hit = hit || zero_b_cols[c] != 0;
+      if (hit) f |= 2u;
+    }
+    sched_flags |= f;
+    out5[5 * t + 0] = req;
+    out5[5 * t + 1] = sel;
+    out5[5 * t + 3] = bits;
+    out5[5 * t + 4] = f;
+  }
+  std::sort(groups.begin(), groups.end());
+  for (int64_t t = 0; t < tiles; ++t)
+    out5[5 * t + 2] = static_cast<uint32_t>(std::lower_bound(groups.begin(), groups.end(), out5[5 * t + 1]) -
+                                            groups.begin());
+  const uint32_t adaptive = groups.size() > 1 ? 1u : 0u, skip = max_sel < prefix ? 1u : 0u;
+  const uint32_t collapsed = (groups.size() == 1 && min_req == prefix && max_req == prefix && min_sel == prefix &&
+                              max_sel == prefix && adaptive == 0 && skip == 0 && sched_flags == 0) ? 1u : 0u;
+  const uint32_t vals[10] = {min_req, max_req, min_sel, max_sel, static_cast<uint32_t>(groups.size()), max_bits,
+                             adaptive, skip, sched_flags, collapsed};
+  for (int i = 0; i < 10; ++i) summary[i] = vals[i];
+  return ST_SUCCESS;
+}
+
+// cpu_gemm_rns under a tile schedule (cpu_reference.cpp:221-260): per tile,
+// planes below its selected prefix; proven-zero tiles get zeros there.
+// sel[t] = selected prefix | 0x80 for a proven-zero tile. C is updated in place.
+OX void oracle_gemm_rns_scheduled(const int8_t* A, const int8_t* B, int8_t* C, int64_t m, int64_t n, int64_t k,
+                                  uint32_t tile_m, uint32_t tile_n, const uint8_t* sel) {
+  const int64_t tile_rows = (m + tile_m - 1) / tile_m, tile_cols = (n + tile_n - 1) / tile_n;
+  for (int64_t t = 0; t < tile_rows * tile_cols; ++t) {
+    const int64_t r0 = (t / tile_cols) * tile_m, c0 = (t % tile_cols) * tile_n;
+    const int64_t rows = std::min<int64_t>(tile_m, m - r0), cols = std::min<int64_t>(tile_n, n - c0);
+    for (uint32_t p = 0; p < (sel[t] & 0x7Fu); ++p) {
+      int8_t* ct = C + p * m * n + r0 * n + c0;
+      if (sel[t] & 0x80u) {
+        for (int64_t r = 0; r < rows; ++r) std::memset(ct + r * n, 0, static_cast<size_t>(cols));
+        continue;
+      }
+      ring_gemm_modulus(A + p * m * k + r0 * k, B + p * k * n + c0, ct, rows, cols, k, k, n, n, kLadder[p]);
+    }
+  }
+}
+
+// rns8_export_i64 / u64 under a per-tile plan (api_export.cpp:365-414): each
+// cell with its tile's selected prefix and bound, staged, committed only when
+// every cell passed (dst untouched otherwise).
+OX int oracle_export_scheduled(const int8_t* planes, int64_t m, int64_t n, uint32_t tile_m, uint32_t tile_n,
+                               const uint8_t* sel, const uint64_t* tile_bounds, int is_signed, void* dst, int64_t ld) {
+  const int64_t tile_cols = (n + tile_n - 1) / tile_n;
+  std::vector<uint64_t> staged(static_cast<size_t>(m * n), 0);
+  for (int64_t row = 0; row < m; ++row)
+    for (int64_t col = 0; col < n; ++col) {
+      const int64_t t = (row / tile_m) * tile_cols + col / tile_n;
+      if (sel[t] & 0x80u) continue;  // proven zero
+      const uint32_t prefix = sel[t] & 0x7Fu;
+      int8_t residues[32];
+      for (uint32_t p = 0; p < prefix; ++p) residues[p] = planes[p * m * n + row * n + col];
+      int st;
+      if (is_signed) {
+        int64_t v = 0;
+        st = reconstruct_signed(residues, prefix, tile_bounds[t], &v);
+        staged[row * n + col] = static_cast<uint64_t>(v);
+      } else {
+        uint64_t v = 0;
+        st = reconstruct_unsigned(residues, prefix, tile_bounds[t], &v);
+        staged[row * n + col] = v;
+      }
+      if (st != ST_SUCCESS) return st;
+    }
+  uint64_t* out = static_cast<uint64_t*>(dst);
+  for (int64_t row = 0; row < m; ++row)
+    for (int64_t col = 0; col < n; ++col) out[row * ld + col] = staged[row * n + col];
   return ST_SUCCESS;
 }
 

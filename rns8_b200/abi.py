@@ -119,6 +119,14 @@ class GemmDesc(_Struct):
                 ("zero_b_cols_count", C.c_uint64)]
 
 
+class PlanTileScheduleEntry(_Struct):
+    _fields_ = [("struct_size", C.c_uint64), ("abi_version", C.c_uint32), ("flags", C.c_uint32),
+                ("tile_row", C.c_uint64), ("tile_col", C.c_uint64), ("row_offset", C.c_int64),
+                ("col_offset", C.c_int64), ("row_extent", C.c_int64), ("col_extent", C.c_int64),
+                ("required_prefix", C.c_uint32), ("selected_prefix", C.c_uint32), ("group_index", C.c_uint32),
+                ("range_bit_length", C.c_uint32)]
+
+
 class MatrixDesc(_Struct):
     _fields_ = [("struct_size", C.c_uint64), ("abi_version", C.c_uint32), ("rows", C.c_int64), ("cols", C.c_int64),
                 ("logical_ld", C.c_int64), ("semantics", c_enum), ("logical_layout", c_enum),
@@ -247,6 +255,7 @@ SIGNATURES = {
     "rns8_cuda_export_limbs_device": (c_status, [C.c_int, vp, i64, i64, u32, u32, u32, vp, i64, vp, vp]),
     "rns8_cuda_export_finite_u8_device": (c_status, [C.c_int, vp, i64, i64, u16, vp, i64, vp]),
     "rns8_cuda_plan_probe": (c_status, [vp, P(u32), P(u32), P(u64)]),
+    "rns8_cuda_plan_tile_schedule_probe": (c_status, [vp, vp, u64, P(u64), vp]),
     "rns8_cuda_exact_gemm_bound_device": (c_status, [C.c_int, vp, vp, i64, i64, i64, u32, vp, vp, vp, vp, vp, vp]),
     "rns8_cuda_pack_wrap_u64_device": (c_status, [C.c_int, vp, i64, i64, i64, vp, vp]),
     "rns8_cuda_gemm_wrap_u64_device": (c_status, [C.c_int, vp, vp, vp, i64, i64, i64, u32, vp, vp]),

@@ -43,6 +43,43 @@ def gemm_desc(semantics, bound_kind, m, n, k, bound=0, max_prefix=0, flags=0, fi
                         tile_n=tile_n)
 
 
+def set_tile_bounds(desc: abi.GemmDesc, tile_bounds, zero_a_rows=None, zero_b_cols=None) -> abi.GemmDesc:
+    """Attach per-tile bounds (and zero row/column masks) to a descriptor; the
+    arrays are kept alive on the descriptor object."""
+    tb = (C.c_uint64 * len(tile_bounds))(*[int(v) for v in tile_bounds])
+    desc._keep = [tb]
+    desc.tile_bounds = C.cast(tb, C.POINTER(C.c_uint64))
+    desc.tile_bounds_count = len(tile_bounds)
+    if zero_a_rows is not None:
+        za = (C.c_uint8 * len(zero_a_rows))(*[int(v) for v in zero_a_rows])
+        zb = (C.c_uint8 * len(zero_b_cols))(*[int(v) for v in zero_b_cols])
+        desc._keep += [za, zb]
+        desc.zero_a_rows = C.cast(za, C.POINTER(C.c_uint8))
+        desc.zero_a_rows_count = len(zero_a_rows)
+        desc.zero_b_cols = C.cast(zb, C.POINTER(C.c_uint8))
+        desc.zero_b_cols_count = len(zero_b_cols)
+    return desc
+
+
+def _entries(fn, count_fn) -> list:
+    written = C.c_uint64()
+    check(count_fn(None, 0, C.byref(written)), "tile schedule count")
+    arr = (abi.PlanTileScheduleEntry * max(written.value, 1))()
+    for e in arr:
+        e.struct_size, e.abi_version = C.sizeof(abi.PlanTileScheduleEntry), abi.ABI_VERSION
+    check(fn(arr, written.value, C.byref(written)), "tile schedule")
+    return list(arr)[: written.value]
+
+
+def plan_tile_schedule_probe(desc: abi.GemmDesc) -> tuple[list, abi.PlanScheduleInfo]:
+    """Host-only: the tile schedule and schedule info rns8_create_plan would build."""
+    info = abi.PlanScheduleInfo()
+    f = lib().rns8_cuda_plan_tile_schedule_probe
+    entries = _entries(lambda a, c, w: f(C.byref(desc), a, c, w, C.byref(info)),
+                       lambda a, c, w: f(C.byref(desc), a, c, w, None))
+    return entries, info
+
+
 class _Handle:
     _destroy = ""
 
@@ -94,6 +131,10 @@ class Plan(_Handle):
         info = abi.PlanScheduleInfo()
         check(lib().rns8_get_plan_schedule_info(self.handle, C.byref(info)), "rns8_get_plan_schedule_info")
         return info
+
+    def tile_schedule(self) -> list:
+        f = lib().rns8_get_plan_tile_schedule
+        return _entries(lambda a, c, w: f(self.handle, a, c, w), lambda a, c, w: f(self.handle, a, c, w))
 
     def backend_info(self) -> abi.PlanBackendInfo:
         info = abi.PlanBackendInfo()

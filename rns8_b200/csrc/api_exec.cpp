@@ -94,9 +94,9 @@ rns8_status validate_rns_operands(const rns8_context& ctx, const rns8_plan& plan
     return RNS8_INVALID_ARGUMENT;
   const rns8_bound_kind bk = storage_bound_kind(plan);
   const auto& d = plan.desc;
-  if (!descriptor_matches(A, d.semantics, bk, d.m, d.k, plan.prefix) ||
-      !descriptor_matches(B, d.semantics, bk, d.k, d.n, plan.prefix) ||
-      !descriptor_matches(C, d.semantics, bk, d.m, d.n, plan.prefix))
+  const uint32_t sp = plan.storage_prefix();
+  if (!descriptor_matches(A, d.semantics, bk, d.m, d.k, sp) || !descriptor_matches(B, d.semantics, bk, d.k, d.n, sp) ||
+      !descriptor_matches(C, d.semantics, bk, d.m, d.n, sp))
     return RNS8_INVALID_ARGUMENT;
   if (!A.device_current || !B.device_current) return RNS8_INVALID_ARGUMENT;
   if (exact_wide(d.semantics) && (&A == &C || &B == &C)) return RNS8_INVALID_ARGUMENT;
@@ -137,6 +137,45 @@ rns8_status run_plane_gemm(rns8_context& ctx, const rns8cuda::PlaneGemmProblem& 
   uint32_t word = 0;
   s = read_status(ctx, &word);
   if (s != RNS8_SUCCESS) return s;
+  return word == 0 ? RNS8_SUCCESS : RNS8_BACKEND_FAILURE;
+}
+
+// Per-tile schedule in kernel form: the selected prefix of every schedule
+// tile, | 0x80 for proven-zero outputs. A per-tile plan whose schedule
+// collapsed runs every tile at the plan prefix.
+struct KernelSchedule {
+  std::vector<uint8_t> sel;
+  rns8cuda::PlaneSchedule view{};
+};
+KernelSchedule kernel_schedule(const rns8_plan& plan) {
+  KernelSchedule ks;
+  ks.sel.assign(static_cast<size_t>(plan.tile_count), static_cast<uint8_t>(plan.prefix));
+  for (size_t t = 0; t < plan.tile_schedule.size() && t < ks.sel.size(); ++t) {
+    const auto& e = plan.tile_schedule[t];
+    ks.sel[t] = static_cast<uint8_t>(e.selected_prefix | ((e.flags & RNS8_TILE_SCHEDULE_ZERO_OUTPUT) ? 0x80u : 0u));
+  }
+  ks.view.tile_m = plan.desc.tile_m;
+  ks.view.tile_n = plan.desc.tile_n;
+  ks.view.tile_rows = plan.tile_rows;
+  ks.view.tile_cols = plan.tile_cols;
+  ks.view.tile_sel = ks.sel.data();
+  return ks;
+}
+
+// rns8_gemm_rns under a tile schedule (reference cpu_reference.cpp:221-260).
+rns8_status run_plane_gemm_scheduled(rns8_context& ctx, const rns8_plan& plan,
+                                     const rns8cuda::PlaneGemmProblem& prob, rns8_workspace* ws) {
+  const KernelSchedule ks = kernel_schedule(plan);
+  const uint64_t need = rns8cuda::plane_gemm_scheduled_scratch_bytes(prob, ks.view, ctx.sm_count);
+  if (!ws) return RNS8_INVALID_ARGUMENT;
+  rns8_status s = ws->scratch.ensure(ctx.device_id, need);
+  if (s != RNS8_SUCCESS) return s;
+  if ((s = clear_status(ctx)) != RNS8_SUCCESS) return s;
+  s = cuda_status(rns8cuda::plane_gemm_scheduled(prob, ks.view, ctx.sm_count, ws->scratch.ptr, need, ctx.dev_status,
+                                                 ctx.stream));
+  if (s != RNS8_SUCCESS) return s;
+  uint32_t word = 0;
+  if ((s = read_status(ctx, &word)) != RNS8_SUCCESS) return s;
   return word == 0 ? RNS8_SUCCESS : RNS8_BACKEND_FAILURE;
 }
 
@@ -280,7 +319,7 @@ rns8_status validate_rns_export(const rns8_context& ctx, const rns8_plan& plan, 
                                 rns8_semantics semantics) {
   if (!plan_context_ok(ctx, plan) || plan.desc.semantics != semantics) return RNS8_INVALID_ARGUMENT;
   if (C.device_id != ctx.device_id || C.backend != plan.backend) return RNS8_INVALID_ARGUMENT;
-  if (!descriptor_matches(C, semantics, storage_bound_kind(plan), plan.desc.m, plan.desc.n, plan.prefix))
+  if (!descriptor_matches(C, semantics, storage_bound_kind(plan), plan.desc.m, plan.desc.n, plan.storage_prefix()))
     return RNS8_INVALID_ARGUMENT;
   if (!C.device_current) return RNS8_INVALID_ARGUMENT;
   if (exact_wide(semantics) && C.exact_range_prefix != 0 &&
@@ -305,6 +344,14 @@ rns8_status export_rns(rns8_context& ctx, const rns8_plan& plan, const rns8_matr
   st = clear_status(ctx);
   if (st != RNS8_SUCCESS) return st;
   cudaError_t e = cudaSuccess;
+  if (!plan.tile_bounds.empty() && (kind == ExportKind::I64 || kind == ExportKind::U64)) {
+    // Per-tile plans: each tile's selected prefix and bound (api_export.cpp:365-391).
+    const KernelSchedule ks = kernel_schedule(plan);
+    const uint64_t jb = rns8cuda::export_scheduled_scratch_bytes(ks.view);
+    if ((st = C.export_jobs.ensure(ctx.device_id, jb)) != RNS8_SUCCESS) return st;
+    e = rns8cuda::export_scheduled(C.residues, m, n, kind == ExportKind::I64, ks.view, plan.tile_bounds.data(),
+                                   C.staging.ptr, ctx.dev_status, C.export_jobs.ptr, jb, ctx.stream);
+  } else {
   switch (kind) {
     case ExportKind::I64:
       e = rns8cuda::export_i64(C.residues, m, n, plan.prefix, plan.desc.bound, static_cast<int64_t*>(C.staging.ptr), n,
@@ -319,6 +366,7 @@ rns8_status export_rns(rns8_context& ctx, const rns8_plan& plan, const rns8_matr
       e = rns8cuda::export_limbs(C.residues, m, n, plan.prefix, kind == ExportKind::LimbsS, limbs,
                                  static_cast<uint64_t*>(C.staging.ptr), n, ctx.dev_status, ctx.stream);
       break;
+  }
   }
   if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
   uint32_t word = 0;
@@ -364,6 +412,71 @@ rns8_status validate_typed_oneshot(const rns8_gemm_desc& d, rns8_semantics expec
   return RNS8_SUCCESS;
 }
 
+// One-shot under a per-tile bound plan: pack the storage prefix, the
+// scheduled plane GEMM, the per-tile export, all in the context's arena.
+template <typename T>
+rns8_status bounded_oneshot_per_tile(rns8_context* ctx, const rns8_plan& plan, const T* A, int64_t lda, const T* B,
+                                     int64_t ldb, T* C, int64_t ldc) {
+  constexpr bool kSigned = std::numeric_limits<T>::is_signed;
+  const int64_t m = plan.desc.m, n = plan.desc.n, k = plan.desc.k;
+  const uint32_t P = plan.storage_prefix();
+  const KernelSchedule ks = kernel_schedule(plan);
+  int8_t* const fake = reinterpret_cast<int8_t*>(256);  // shape-only problem for the scratch sizes
+  rns8cuda::PlaneGemmTask task{fake, fake, fake};
+  rns8cuda::PlaneGemmProblem prob = rns_problem(plan, P, &task, 1, 0);
+  const bool scheduled = !plan.tile_schedule.empty();
+  const uint64_t gemm_scratch = scheduled ? rns8cuda::plane_gemm_scheduled_scratch_bytes(prob, ks.view, ctx->sm_count)
+                                          : rns8cuda::plane_gemm_scratch_bytes(prob, ctx->sm_count);
+  const uint64_t jobs = rns8cuda::export_scheduled_scratch_bytes(ks.view);
+  const uint64_t a_nat = static_cast<uint64_t>(m) * k * 8, b_nat = static_cast<uint64_t>(k) * n * 8;
+  const uint64_t a_res = static_cast<uint64_t>(P) * m * k, b_res = static_cast<uint64_t>(P) * k * n;
+  const uint64_t c_res = static_cast<uint64_t>(P) * m * n, c_nat = static_cast<uint64_t>(m) * n * 8;
+  const uint64_t total = round256(a_nat) + round256(b_nat) + round256(a_res) + round256(b_res) + round256(c_res) +
+                         round256(c_nat) + round256(gemm_scratch) + round256(jobs);
+  std::unique_lock<std::mutex> lock(ctx->oneshot_mutex, std::try_to_lock);
+  DevBuf local;
+  DevBuf& arena = lock.owns_lock() ? ctx->oneshot_arena : local;
+  rns8_status st = arena.ensure(ctx->device_id, total);
+  if (st != RNS8_SUCCESS) return st;
+  Carve cv{static_cast<uint8_t*>(arena.ptr)};
+  T* dA = static_cast<T*>(cv.take(a_nat));
+  T* dB = static_cast<T*>(cv.take(b_nat));
+  int8_t* rA = static_cast<int8_t*>(cv.take(a_res));
+  int8_t* rB = static_cast<int8_t*>(cv.take(b_res));
+  int8_t* rC = static_cast<int8_t*>(cv.take(c_res));
+  void* dC = cv.take(c_nat);
+  void* dS = cv.take(gemm_scratch);
+  void* dJ = cv.take(jobs);
+  if ((st = copy_in_2d(*ctx, dA, A, m, k, lda, sizeof(T))) != RNS8_SUCCESS) return st;
+  if ((st = copy_in_2d(*ctx, dB, B, k, n, ldb, sizeof(T))) != RNS8_SUCCESS) return st;
+  // A fresh C is zero in every plane, as a newly created matrix is.
+  if (cudaMemsetAsync(rC, 0, c_res, ctx->stream) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  cudaError_t e = kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(dA), m, k, k, P, rA, ctx->stream)
+                          : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(dA), m, k, k, P, rA, ctx->stream);
+  if (e == cudaSuccess)
+    e = kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(dB), k, n, n, P, rB, ctx->stream)
+                : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(dB), k, n, n, P, rB, ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  if ((st = clear_status(*ctx)) != RNS8_SUCCESS) return st;
+  task = {rA, rB, rC};
+  e = scheduled ? rns8cuda::plane_gemm_scheduled(prob, ks.view, ctx->sm_count, dS, gemm_scratch, ctx->dev_status,
+                                                 ctx->stream)
+                : rns8cuda::plane_gemm(prob, rns8cuda::GemmPath::Auto, ctx->sm_count, dS, gemm_scratch,
+                                       ctx->dev_status, ctx->stream);
+  if (e != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  uint32_t word = 0;
+  if ((st = read_status(*ctx, &word)) != RNS8_SUCCESS) return st;
+  if (word != 0) return RNS8_BACKEND_FAILURE;
+  if ((st = clear_status(*ctx)) != RNS8_SUCCESS) return st;
+  if (rns8cuda::export_scheduled(rC, m, n, kSigned, ks.view, plan.tile_bounds.data(), dC, ctx->dev_status, dJ, jobs,
+                                 ctx->stream) != cudaSuccess)
+    return RNS8_BACKEND_FAILURE;
+  if ((st = read_status(*ctx, &word)) != RNS8_SUCCESS) return st;
+  if ((st = status_from_device(word)) != RNS8_SUCCESS) return st;
+  if ((st = copy_out_2d(*ctx, C, ldc, dC, m, n, sizeof(T))) != RNS8_SUCCESS) return st;
+  return sync(*ctx);
+}
+
 template <typename T>
 rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const T* A, int64_t lda, const T* B,
                             int64_t ldb, T* C, int64_t ldc) {
@@ -377,6 +490,7 @@ rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const
   if (st != RNS8_SUCCESS) return st;
   DeviceScope dev(ctx->device_id);
   if (!dev.ok) return RNS8_BACKEND_FAILURE;
+  if (!plan.tile_bounds.empty()) return bounded_oneshot_per_tile<T>(ctx, plan, A, lda, B, ldb, C, ldc);
   const int64_t m = plan.desc.m, n = plan.desc.n, k = plan.desc.k;
   const uint32_t P = plan.prefix;
   const uint64_t a_nat = static_cast<uint64_t>(m) * k * 8, b_nat = static_cast<uint64_t>(k) * n * 8;
@@ -513,10 +627,19 @@ rns8_status grouped_gemm(rns8_context* ctx, const rns8_plan* plan, const rns8_gr
   std::vector<rns8cuda::PlaneGemmTask> list(count);
   for (uint32_t i = 0; i < count; ++i) list[i] = {tasks[i].a->residues, tasks[i].b->residues, tasks[i].c->residues};
   for (uint32_t i = 0; i < count; ++i) tasks[i].c->device_current = false;
-  const rns8cuda::PlaneGemmProblem prob =
-      rns_problem(*plan, finite ? 1 : plan->prefix, list.data(), count, finite ? modulus : 0);
-  const rns8_status st = run_plane_gemm(*ctx, prob, tasks[0].workspace);
-  if (st != RNS8_SUCCESS) return st;
+  if (!finite && !plan->tile_schedule.empty()) {
+    // Scheduled plans run task by task with the plan's tile schedule.
+    for (uint32_t i = 0; i < count; ++i) {
+      const rns8cuda::PlaneGemmProblem one = rns_problem(*plan, plan->storage_prefix(), &list[i], 1, 0);
+      const rns8_status st = run_plane_gemm_scheduled(*ctx, *plan, one, tasks[i].workspace);
+      if (st != RNS8_SUCCESS) return st;
+    }
+  } else {
+    const rns8cuda::PlaneGemmProblem prob =
+        rns_problem(*plan, finite ? 1 : plan->prefix, list.data(), count, finite ? modulus : 0);
+    const rns8_status st = run_plane_gemm(*ctx, prob, tasks[0].workspace);
+    if (st != RNS8_SUCCESS) return st;
+  }
   for (uint32_t i = 0; i < count; ++i) {
     rns8_matrix& C = *tasks[i].c;
     C.device_current = true;
@@ -589,8 +712,9 @@ extern "C" rns8_status rns8_gemm_rns(rns8_context* ctx, const rns8_plan* plan, c
     if (!dev.ok) return RNS8_BACKEND_FAILURE;
     C->device_current = false;
     rns8cuda::PlaneGemmTask task{A->residues, B->residues, C->residues};
-    const rns8cuda::PlaneGemmProblem prob = rns_problem(*plan, plan->prefix, &task, 1, 0);
-    st = run_plane_gemm(*ctx, prob, workspace);
+    const rns8cuda::PlaneGemmProblem prob = rns_problem(*plan, plan->storage_prefix(), &task, 1, 0);
+    st = plan->tile_schedule.empty() ? run_plane_gemm(*ctx, prob, workspace)
+                                     : run_plane_gemm_scheduled(*ctx, *plan, prob, workspace);
     if (st != RNS8_SUCCESS) return st;
     C->device_current = true;
     C->source_version = combine_source_versions(A->source_version, B->source_version);

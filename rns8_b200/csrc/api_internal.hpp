@@ -74,6 +74,16 @@ struct rns8_plan {
   uint32_t min_required = 0, max_required = 0, min_selected = 0, max_selected = 0;
   uint32_t group_count = 0, range_bit_length = 0, adaptive_prefix = 0, adaptive_skip = 0, schedule_flags = 0;
   uint64_t fingerprint = 0;
+  // Per-tile bound plans (api_plan_schedule.inc:109-261): one entry per
+  // tile_m x tile_n output tile, empty when every tile runs the plan prefix.
+  std::vector<uint64_t> tile_bounds;
+  std::vector<rns8_plan_tile_schedule_entry> tile_schedule;
+  std::vector<uint8_t> zero_a_rows, zero_b_cols;
+  uint64_t zero_a_row_count = 0, zero_b_col_count = 0, zero_row_col_product_count = 0;
+  // Residue planes the plan's matrices must hold: the largest selected prefix.
+  uint32_t storage_prefix() const {
+    return !tile_schedule.empty() && max_selected > 0 ? max_selected : prefix;
+  }
 };
 
 struct rns8_matrix {
@@ -89,6 +99,7 @@ struct rns8_matrix {
   bool device_current = false;
   rns8host::DevBuf upload;      // native input staging
   rns8host::DevBuf staging;     // export staging
+  rns8host::DevBuf export_jobs; // per-tile export descriptors (scheduled plans)
   // Exact-wide proof (reference internal.hpp:96-99); zero prefix = unknown.
   rns8host::i256 exact_max_magnitude;
   uint32_t exact_range_prefix = 0;

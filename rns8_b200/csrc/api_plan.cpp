@@ -274,6 +274,129 @@ uint64_t plan_fingerprint(const rns8_plan& p) {
   return h;
 }
 
+static bool mask_range_has_set(const std::vector<uint8_t>& mask, int64_t begin, int64_t end) {
+  for (int64_t i = begin; i < end; ++i)
+    if (mask[static_cast<size_t>(i)]) return true;
+  return false;
+}
+
+static rns8_plan_tile_schedule_entry make_tile_entry(const rns8_plan& plan, uint64_t index, uint32_t required,
+                                                     uint32_t selected, uint32_t group, uint32_t range_bits,
+                                                     uint32_t flags) {
+  rns8_plan_tile_schedule_entry e{};
+  e.struct_size = sizeof(e);
+  e.abi_version = RNS8_ABI_VERSION;
+  e.flags = flags;
+  e.tile_row = index / plan.tile_cols;
+  e.tile_col = index % plan.tile_cols;
+  e.row_offset = static_cast<int64_t>(e.tile_row * plan.desc.tile_m);
+  e.col_offset = static_cast<int64_t>(e.tile_col * plan.desc.tile_n);
+  e.row_extent = std::min<int64_t>(plan.desc.tile_m, plan.desc.m - e.row_offset);
+  e.col_extent = std::min<int64_t>(plan.desc.tile_n, plan.desc.n - e.col_offset);
+  e.required_prefix = required;
+  e.selected_prefix = selected;
+  e.group_index = group;
+  e.range_bit_length = range_bits;
+  return e;
+}
+
+// configure_plan_schedule for per-tile bounds (api_plan_schedule.inc:109-261):
+// each tile gets the smallest prefix its bound needs (or the plan prefix when
+// forced), proven-zero tiles and zero row/column products are flagged, and a
+// schedule where every tile runs the plan prefix unflagged collapses to none.
+rns8_status build_tile_schedule(const rns8_gemm_desc& desc, rns8_plan& plan) {
+  if (!desc.tile_bounds || desc.tile_bounds_count != plan.tile_count) return RNS8_INVALID_ARGUMENT;
+  plan.tile_bounds.assign(desc.tile_bounds, desc.tile_bounds + desc.tile_bounds_count);
+  plan.desc.tile_bounds_count = plan.tile_bounds.size();
+  if ((desc.flags & RNS8_PLAN_ALLOW_PROVEN_ZERO_ROW_COL_SKIPS) != 0) {
+    plan.zero_a_rows.assign(desc.zero_a_rows, desc.zero_a_rows + desc.zero_a_rows_count);
+    plan.zero_b_cols.assign(desc.zero_b_cols, desc.zero_b_cols + desc.zero_b_cols_count);
+    for (uint8_t v : plan.zero_a_rows) plan.zero_a_row_count += v;
+    for (uint8_t v : plan.zero_b_cols) plan.zero_b_col_count += v;
+    const uint64_t nonzero_rows = static_cast<uint64_t>(plan.desc.m) - plan.zero_a_row_count;
+    plan.zero_row_col_product_count =
+        plan.zero_a_row_count * static_cast<uint64_t>(plan.desc.n) + nonzero_rows * plan.zero_b_col_count;
+  }
+  plan.desc.zero_a_rows_count = plan.zero_a_rows.size();
+  plan.desc.zero_b_cols_count = plan.zero_b_cols.size();
+  const bool fixed = (plan.desc.flags & RNS8_PLAN_FORCE_FIXED_PREFIX) != 0;
+  const bool zero_tiles = (plan.desc.flags & RNS8_PLAN_ALLOW_PROVEN_ZERO_TILE_SKIPS) != 0;
+  const bool zero_rc = !plan.zero_a_rows.empty();
+  uint32_t min_req = UINT32_MAX, max_req = 0, min_sel = UINT32_MAX, max_sel = 0, max_bits = 0;
+  std::vector<uint32_t> groups;
+  plan.tile_schedule.reserve(plan.tile_bounds.size());
+  for (uint64_t index = 0; index < plan.tile_count; ++index) {
+    const uint64_t bound = plan.tile_bounds[index];
+    if (plan.desc.semantics == RNS8_BOUNDED_I64 && bound > (uint64_t{1} << 63)) return RNS8_INVALID_ARGUMENT;
+    const i256 range = plan.desc.semantics == RNS8_BOUNDED_I64 ? i256::from_u64(2) * i256::from_u64(bound)
+                                                                : i256::from_u64(bound);
+    const uint32_t bits = bit_length(range);
+    const uint32_t req = required_prefix_for_range(range);
+    if (req == 0 || req > plan.prefix) return RNS8_RANGE_ERROR;
+    const uint32_t sel = fixed ? plan.prefix : req;
+    min_req = std::min(min_req, req);
+    max_req = std::max(max_req, req);
+    min_sel = std::min(min_sel, sel);
+    max_sel = std::max(max_sel, sel);
+    max_bits = std::max(max_bits, bits);
+    if (std::find(groups.begin(), groups.end(), sel) == groups.end()) groups.push_back(sel);
+    uint32_t flags = zero_tiles && bound == 0 ? RNS8_TILE_SCHEDULE_ZERO_OUTPUT : 0u;
+    if (zero_rc) {
+      const rns8_plan_tile_schedule_entry e = make_tile_entry(plan, index, 0, 0, 0, 0, 0);
+      if (mask_range_has_set(plan.zero_a_rows, e.row_offset, e.row_offset + e.row_extent) ||
+          mask_range_has_set(plan.zero_b_cols, e.col_offset, e.col_offset + e.col_extent))
+        flags |= RNS8_TILE_SCHEDULE_ZERO_ROW_COL_PRODUCT;
+    }
+    plan.schedule_flags |= flags;
+    plan.tile_schedule.push_back(make_tile_entry(plan, index, req, sel, 0, bits, flags));
+  }
+  std::sort(groups.begin(), groups.end());
+  for (auto& e : plan.tile_schedule)
+    e.group_index = static_cast<uint32_t>(std::lower_bound(groups.begin(), groups.end(), e.selected_prefix) -
+                                          groups.begin());
+  plan.min_required = min_req == UINT32_MAX ? 0 : min_req;
+  plan.max_required = max_req;
+  plan.min_selected = min_sel == UINT32_MAX ? 0 : min_sel;
+  plan.max_selected = max_sel;
+  plan.group_count = static_cast<uint32_t>(groups.size());
+  plan.range_bit_length = max_bits;
+  plan.adaptive_prefix = groups.size() > 1 ? 1u : 0u;
+  plan.adaptive_skip = max_sel < plan.prefix ? 1u : 0u;
+  if (plan.group_count == 1 && plan.min_required == plan.prefix && plan.max_required == plan.prefix &&
+      plan.min_selected == plan.prefix && plan.max_selected == plan.prefix && plan.adaptive_prefix == 0 &&
+      plan.adaptive_skip == 0 && plan.schedule_flags == 0)
+    plan.tile_schedule.clear();
+  plan.modulus_product = modulus_product(plan.prefix);
+  plan.fingerprint = plan_fingerprint(plan);
+  return RNS8_SUCCESS;
+}
+
+// rns8_get_plan_tile_schedule (api_plan_public_api.inc:119-167).
+rns8_status plan_tile_schedule(const rns8_plan& plan, rns8_plan_tile_schedule_entry* entries, uint64_t capacity,
+                               uint64_t* written) {
+  *written = plan.tile_count;
+  if (!entries || capacity == 0) return RNS8_SUCCESS;
+  if (capacity < plan.tile_count) return RNS8_WORKSPACE_TOO_SMALL;
+  if (!plan.tile_schedule.empty()) {
+    std::copy(plan.tile_schedule.begin(), plan.tile_schedule.end(), entries);
+    return RNS8_SUCCESS;
+  }
+  const bool per_tile = plan.desc.bound_kind == RNS8_BOUND_PER_TILE_MAX_ABS ||
+                        plan.desc.bound_kind == RNS8_BOUND_PER_TILE_MAX_UNSIGNED;
+  for (uint64_t index = 0; index < plan.tile_count; ++index) {
+    if (per_tile && plan.tile_bounds.size() == plan.tile_count) {
+      const uint64_t bound = plan.tile_bounds[index];
+      const i256 range = plan.desc.semantics == RNS8_BOUNDED_I64 ? i256::from_u64(2) * i256::from_u64(bound)
+                                                                  : i256::from_u64(bound);
+      entries[index] = make_tile_entry(plan, index, required_prefix_for_range(range), plan.min_selected, 0,
+                                       bit_length(range), 0);
+      continue;
+    }
+    entries[index] = make_tile_entry(plan, index, plan.min_required, plan.min_selected, 0, plan.range_bit_length, 0);
+  }
+  return RNS8_SUCCESS;
+}
+
 // rns8_create_plan minus the context checks (api_plan_public_api.inc:3-73)
 // and configure_plan_schedule for global bounds (api_plan_schedule.inc:109-279).
 rns8_status build_plan(const rns8_gemm_desc& desc, rns8_plan& plan) {
@@ -304,12 +427,8 @@ rns8_status build_plan(const rns8_gemm_desc& desc, rns8_plan& plan) {
     plan.fingerprint = plan_fingerprint(plan);
     return RNS8_SUCCESS;
   }
-  if (plan.desc.bound_kind == RNS8_BOUND_PER_TILE_MAX_ABS || plan.desc.bound_kind == RNS8_BOUND_PER_TILE_MAX_UNSIGNED) {
-    // Per-tile adaptive schedules are a separate execution mode this backend
-    // does not run; the request is well-formed, so the backend declines it.
-    if (!desc.tile_bounds || desc.tile_bounds_count != plan.tile_count) return RNS8_INVALID_ARGUMENT;
-    return RNS8_UNSUPPORTED_BACKEND;
-  }
+  if (plan.desc.bound_kind == RNS8_BOUND_PER_TILE_MAX_ABS || plan.desc.bound_kind == RNS8_BOUND_PER_TILE_MAX_UNSIGNED)
+    return build_tile_schedule(desc, plan);
   const uint32_t req = required_prefix_for_range(required_range);
   if (req == 0 || req > prefix) return RNS8_RANGE_ERROR;
   const bool fixed = (plan.desc.flags & RNS8_PLAN_FORCE_FIXED_PREFIX) != 0;
@@ -438,6 +557,9 @@ extern "C" rns8_status rns8_get_plan_schedule_info(const rns8_plan* plan, rns8_p
     out->effective_bound = plan->desc.bound;
     out->lhs_bound = plan->desc.lhs_bound;
     out->rhs_bound = plan->desc.rhs_bound;
+    out->zero_a_row_count = plan->zero_a_row_count;
+    out->zero_b_col_count = plan->zero_b_col_count;
+    out->zero_row_col_product_count = plan->zero_row_col_product_count;
     set_text(out->bound_contract, sizeof(out->bound_contract), bound_contract_name(*plan));
     return RNS8_SUCCESS;
   });
@@ -448,9 +570,24 @@ extern "C" rns8_status rns8_get_plan_schedule_info(const rns8_plan* plan, rns8_p
 extern "C" rns8_status rns8_get_plan_tile_schedule(const rns8_plan* plan, rns8_plan_tile_schedule_entry* entries,
                                                    uint64_t capacity, uint64_t* written) {
   return guard([&]() -> rns8_status {
-    if (!plan || !written || (capacity != 0 && !entries)) return RNS8_INVALID_ARGUMENT;
-    *written = 0;
-    return RNS8_SUCCESS;
+    if (!plan || !written) return RNS8_INVALID_ARGUMENT;
+    return plan_tile_schedule(*plan, entries, capacity, written);
+  });
+}
+
+extern "C" rns8_status rns8_cuda_plan_tile_schedule_probe(const rns8_gemm_desc* desc,
+                                                          rns8_plan_tile_schedule_entry* entries, uint64_t capacity,
+                                                          uint64_t* written, rns8_plan_schedule_info* info) {
+  return guard([&]() -> rns8_status {
+    if (!desc || !written) return RNS8_INVALID_ARGUMENT;
+    rns8_plan plan;
+    const rns8_status s = build_plan(*desc, plan);
+    if (s != RNS8_SUCCESS) return s;
+    if (info) {
+      const rns8_status i = rns8_get_plan_schedule_info(&plan, info);
+      if (i != RNS8_SUCCESS) return i;
+    }
+    return plan_tile_schedule(plan, entries, capacity, written);
   });
 }
 

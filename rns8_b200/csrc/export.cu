@@ -8,6 +8,9 @@
 // atomicCAS(status, 0, 5) (hip_direct_export_kernels.cuh:137-177).
 //
 // The digit recurrence and Horner rebuild live in garner.cuh.
+#include <algorithm>
+#include <vector>
+
 #include "garner.cuh"
 #include "kernels.hpp"
 
@@ -303,6 +306,77 @@ __global__ void __launch_bounds__(256) export_u8_kernel(const int8_t* __restrict
   }
 }
 
+// ---- scheduled export: per-tile prefix and bound ----------------------------------
+struct TileJob {
+  int64_t row0, col0, rows, cols;
+  BoundedLimits lim;
+  FracLimits frac;
+};
+
+// One job (schedule tile) per block iteration; warps over rows, lanes over
+// columns. Every cell: the fractional CRT with the tile's limits, the exact
+// Garner path for undecided cells (or all cells when the fraction is off).
+template <int P, bool kSigned>
+__global__ void __launch_bounds__(256) export_tiles_kernel(const int8_t* __restrict__ planes, int64_t m, int64_t n,
+                                                           const TileJob* __restrict__ jobs, uint32_t count,
+                                                           uint64_t* __restrict__ dst, uint32_t* status) {
+  const int64_t mn = m * n;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  bool bad = false;
+  for (uint32_t j = blockIdx.x; j < count; j += gridDim.x) {
+    const TileJob job = jobs[j];
+    for (int64_t r = warp; r < job.rows; r += blockDim.x / 32) {
+      const int64_t row = job.row0 + r;
+      for (int64_t c = lane; c < job.cols; c += 32) {
+        const int64_t cell = row * n + job.col0 + c;
+        uint32_t u[P];
+#pragma unroll
+        for (int p = 0; p < P; ++p) u[p] = static_cast<uint32_t>(static_cast<int>(planes[p * mn + cell]) + 128);
+        uint64_t v = 0;
+        int verdict = job.frac.enabled ? frac_reconstruct<P>(u, job.frac, &v) : -1;
+        if (verdict < 0) {
+          int rr[P];
+#pragma unroll
+          for (int p = 0; p < P; ++p) rr[p] = static_cast<int>(u[p]) - 128;
+          verdict = reconstruct_bounded<P, kSigned>(rr, job.lim, &v) ? 1 : 0;
+        }
+        bad |= verdict == 0;
+        dst[cell] = v;
+      }
+    }
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(status, kDevRangeError);
+}
+
+__global__ void __launch_bounds__(256) zero_jobs_kernel(const TileJob* __restrict__ jobs, uint32_t count, int64_t n,
+                                                        uint64_t* __restrict__ dst) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (uint32_t j = blockIdx.x; j < count; j += gridDim.x) {
+    const TileJob job = jobs[j];
+    for (int64_t r = warp; r < job.rows; r += blockDim.x / 32)
+      for (int64_t c = lane; c < job.cols; c += 32) dst[(job.row0 + r) * n + job.col0 + c] = 0;
+  }
+}
+
+template <bool kSigned>
+cudaError_t launch_tiles(uint32_t prefix, const int8_t* planes, int64_t m, int64_t n, const TileJob* jobs,
+                         uint32_t count, uint64_t* dst, uint32_t* status, cudaStream_t stream) {
+  const unsigned blocks = count < 148u * 8u ? count : 148u * 8u;
+  switch (prefix) {
+#define RNS8_TILE_CASE(P)                                                                                   \
+  case P:                                                                                                   \
+    export_tiles_kernel<P, kSigned><<<blocks, 256, 0, stream>>>(planes, m, n, jobs, count, dst, status); \
+    break;
+    RNS8_TILE_CASE(1) RNS8_TILE_CASE(2) RNS8_TILE_CASE(3) RNS8_TILE_CASE(4) RNS8_TILE_CASE(5)
+    RNS8_TILE_CASE(6) RNS8_TILE_CASE(7) RNS8_TILE_CASE(8) RNS8_TILE_CASE(9) RNS8_TILE_CASE(10)
+    RNS8_TILE_CASE(11) RNS8_TILE_CASE(12) RNS8_TILE_CASE(13) RNS8_TILE_CASE(14) RNS8_TILE_CASE(15)
+    RNS8_TILE_CASE(16) RNS8_TILE_CASE(17) RNS8_TILE_CASE(18) RNS8_TILE_CASE(19) RNS8_TILE_CASE(20)
+#undef RNS8_TILE_CASE
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t export_i64(const int8_t* planes, int64_t m, int64_t n, uint32_t prefix, uint64_t bound, int64_t* dst,
@@ -367,6 +441,57 @@ cudaError_t export_finite_u8(const int8_t* residues, int64_t m, int64_t n, uint3
   export_u8_kernel<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(by)), 256, 0, stream>>>(residues, m, n,
                                                                                                     modulus, dst, ld);
   return cudaGetLastError();
+}
+
+uint64_t export_scheduled_scratch_bytes(const PlaneSchedule& sched) {
+  return (sched.tile_rows * sched.tile_cols * sizeof(TileJob) + 255) & ~uint64_t(255);
+}
+
+cudaError_t export_scheduled(const int8_t* planes, int64_t m, int64_t n, bool is_signed, const PlaneSchedule& sched,
+                             const uint64_t* tile_bounds, void* dst, uint32_t* dev_status, void* scratch,
+                             uint64_t scratch_bytes, cudaStream_t stream) {
+  const uint64_t tiles = sched.tile_rows * sched.tile_cols;
+  if (!scratch || scratch_bytes < export_scheduled_scratch_bytes(sched) || !tile_bounds) return cudaErrorInvalidValue;
+  // Jobs ordered by prefix: proven-zero tiles first (prefix 0), then one run per prefix.
+  std::vector<std::vector<TileJob>> by_prefix(21);
+  for (uint64_t t = 0; t < tiles; ++t) {
+    const uint8_t sel = sched.tile_sel[t];
+    const uint32_t prefix = (sel & 0x80u) ? 0u : (sel & 0x7Fu);
+    if (prefix > 20) return cudaErrorInvalidValue;
+    TileJob job{};
+    job.row0 = static_cast<int64_t>((t / sched.tile_cols) * sched.tile_m);
+    job.col0 = static_cast<int64_t>((t % sched.tile_cols) * sched.tile_n);
+    job.rows = std::min<int64_t>(sched.tile_m, m - job.row0);
+    job.cols = std::min<int64_t>(sched.tile_n, n - job.col0);
+    if (prefix > 0) {
+      job.lim = host_limits(prefix, tile_bounds[t]);
+      job.frac = host_frac_limits(prefix, tile_bounds[t], is_signed, frac_sum_f128(prefix));
+    }
+    by_prefix[prefix].push_back(job);
+  }
+  std::vector<TileJob> all;
+  all.reserve(tiles);
+  for (const auto& v : by_prefix) all.insert(all.end(), v.begin(), v.end());
+  auto* jobs = static_cast<TileJob*>(scratch);
+  cudaError_t e = cudaMemcpyAsync(jobs, all.data(), all.size() * sizeof(TileJob), cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return e;
+  auto* out = static_cast<uint64_t*>(dst);
+  uint64_t offset = 0;
+  for (uint32_t prefix = 0; prefix <= 20; ++prefix) {
+    const uint32_t count = static_cast<uint32_t>(by_prefix[prefix].size());
+    if (count == 0) continue;
+    if (prefix == 0) {
+      zero_jobs_kernel<<<count < 148u * 8u ? count : 148u * 8u, 256, 0, stream>>>(jobs + offset, count, n, out);
+      e = cudaGetLastError();
+    } else if (is_signed) {
+      e = launch_tiles<true>(prefix, planes, m, n, jobs + offset, count, out, dev_status, stream);
+    } else {
+      e = launch_tiles<false>(prefix, planes, m, n, jobs + offset, count, out, dev_status, stream);
+    }
+    if (e != cudaSuccess) return e;
+    offset += count;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace rns8cuda

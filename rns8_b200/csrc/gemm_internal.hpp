@@ -20,8 +20,22 @@ struct TcSchedule {
   uint64_t units;
 };
 TcSchedule tc_schedule(const PlaneGemmProblem& prob, int sm_count);
+
+// Scheduled (per-tile prefix) runs of the tensor-core kernel: the explicit
+// unit list and the per-schedule-tile mask, both in device memory.
+struct TcScheduleUnits {
+  const uint64_t* units_dev;
+  uint64_t unit_count;
+  const uint8_t* tile_sel_dev;
+  uint32_t shift_m, shift_n, cols;
+};
+// A proven-zero schedule tile: planes [0, planes) of its cells are zero.
+struct ZeroTile {
+  int64_t row0, col0, rows, cols;
+  uint32_t planes, pad;
+};
 cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
-                          uint32_t* dev_status, cudaStream_t stream);
+                          uint32_t* dev_status, cudaStream_t stream, const TcScheduleUnits* sched = nullptr);
 
 // wrap64 on the tensor cores: c (m x n uint64, row-major) = A x B mod 2^64 from
 // 8 byte planes each (k % 16 == 0, n % 16 == 0, 16-byte aligned planes).

@@ -24,8 +24,10 @@
 // memory and exits.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "device_common.cuh"
 #include "gemm_internal.hpp"
@@ -56,6 +58,13 @@ struct __align__(64) TcParams {
   uint64_t units;
   uint32_t* status;
   uint16_t moduli[20];
+  // Scheduled plans: the units to run (plane | split << 8 | mt << 24 | nt << 44)
+  // and, per schedule tile, its selected prefix (| 0x80 for a proven-zero
+  // output, which is filled elsewhere); the epilogue stores a cell only when
+  // the cell's tile needs the plane.
+  const uint64_t* unit_list;
+  const uint8_t* tile_sel;
+  uint32_t sched_shift_m, sched_shift_n, sched_cols;
 };
 
 struct Unit {
@@ -63,6 +72,18 @@ struct Unit {
 };
 
 __device__ __forceinline__ Unit decode_unit(const TcParams& prm, uint64_t u) {
+  if (prm.unit_list) {
+    const uint64_t e = prm.unit_list[u];
+    Unit w;
+    w.t = 0;
+    w.p = static_cast<uint32_t>(e & 0xFFu);
+    const uint32_t s = static_cast<uint32_t>((e >> 8) & 0xFFFFu);
+    w.mt = static_cast<uint32_t>((e >> 24) & 0xFFFFFu);
+    w.nt = static_cast<uint32_t>((e >> 44) & 0xFFFFFu);
+    w.kb0 = s * prm.kb_per_split;
+    w.kb1 = min(prm.total_kb, w.kb0 + prm.kb_per_split);
+    return w;
+  }
   const uint64_t tiles = static_cast<uint64_t>(prm.m_tiles) * prm.n_tiles;
   const uint64_t tile = u % tiles;
   const uint64_t rest = u / tiles;
@@ -237,6 +258,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
         tmem_wait_ld();
         const int64_t col = static_cast<int64_t>(w.nt) * BN + c * 32;
         if (!row_ok || col >= prm.n) continue;
+        if (prm.tile_sel) {  // schedule tiles are >= 64 wide: a 32-column chunk lies in one
+          const uint8_t sel = prm.tile_sel[(row >> prm.sched_shift_m) * prm.sched_cols + (col >> prm.sched_shift_n)];
+          if ((sel & 0x80u) || w.p >= (sel & 0x7Fu)) continue;
+        }
         if (srow) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
@@ -273,15 +298,41 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
   }
 }
 
-// Split-K finalize: C = centered(sum of partial residues mod m).
+// Split-K finalize: C = centered(sum of partial residues mod m). With a
+// schedule, only the cells whose tile needs the plane are written.
+struct SchedMask {
+  const uint8_t* tile_sel;
+  uint32_t shift_m, shift_n, cols;
+  int64_t n;
+};
+
 __global__ void __launch_bounds__(256) split_finalize_kernel(const int32_t* __restrict__ scratch, int64_t plane_elems,
                                                              uint32_t planes, PlaneModuli moduli,
-                                                             int8_t* __restrict__ c) {
+                                                             int8_t* __restrict__ c, SchedMask mask) {
   const int64_t total = plane_elems * planes;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint32_t p = static_cast<uint32_t>(i / plane_elems);
+    if (mask.tile_sel) {
+      const int64_t e = i - static_cast<int64_t>(p) * plane_elems;
+      const int64_t row = e / mask.n, col = e - row * mask.n;
+      const uint8_t sel = mask.tile_sel[(row >> mask.shift_m) * mask.cols + (col >> mask.shift_n)];
+      if ((sel & 0x80u) || p >= (sel & 0x7Fu)) continue;
+    }
     c[i] = static_cast<int8_t>(reduce_i32_centered(scratch[i], make_mod_const(moduli.m[p])));
+  }
+}
+
+// Proven-zero tiles (RNS8_TILE_SCHEDULE_ZERO_OUTPUT): planes below the tile's
+// selected prefix are zero (cpu_reference.cpp:236-238). One block per tile.
+__global__ void __launch_bounds__(256) zero_tiles_kernel(const ZeroTile* __restrict__ tiles, uint32_t count,
+                                                         int8_t* __restrict__ c, int64_t m, int64_t n) {
+  for (uint32_t t = blockIdx.x; t < count; t += gridDim.x) {
+    const ZeroTile z = tiles[t];
+    for (uint32_t p = 0; p < z.planes; ++p)
+      for (int64_t r = threadIdx.x / 32; r < z.rows; r += blockDim.x / 32)
+        for (int64_t col = threadIdx.x % 32; col < z.cols; col += 32)
+          c[static_cast<int64_t>(p) * m * n + (z.row0 + r) * n + z.col0 + col] = 0;
   }
 }
 
@@ -562,7 +613,7 @@ TcSchedule tc_schedule(const PlaneGemmProblem& prob, int sm_count) {
 }
 
 cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
-                          uint32_t* dev_status, cudaStream_t stream) {
+                          uint32_t* dev_status, cudaStream_t stream, const TcScheduleUnits* sched) {
   if (prob.task_count == 0 || prob.task_count > kMaxGroupTasks || prob.planes == 0 || prob.planes > 20)
     return cudaErrorInvalidValue;
   static std::once_flag attr_once;
@@ -601,13 +652,22 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
   prm.units = s.units;
   prm.status = dev_status;
   for (uint32_t p = 0; p < prob.planes; ++p) prm.moduli[p] = prob.moduli[p];
+  if (sched) {
+    if (prob.task_count != 1) return cudaErrorInvalidValue;
+    prm.unit_list = sched->units_dev;
+    prm.units = sched->unit_count;
+    prm.tile_sel = sched->tile_sel_dev;
+    prm.sched_shift_m = sched->shift_m;
+    prm.sched_shift_n = sched->shift_n;
+    prm.sched_cols = sched->cols;
+  }
 
   if (split) {
     const cudaError_t e = cudaMemsetAsync(scratch, 0, need, stream);
     if (e != cudaSuccess) return e;
   }
-  const uint64_t grid = s.units < static_cast<uint64_t>(sm_count) ? s.units : static_cast<uint64_t>(sm_count);
-  tc_plane_gemm_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM_BYTES, stream>>>(prm);
+  const uint64_t grid = prm.units < static_cast<uint64_t>(sm_count) ? prm.units : static_cast<uint64_t>(sm_count);
+  if (grid > 0) tc_plane_gemm_kernel<<<static_cast<unsigned>(grid), THREADS, SMEM_BYTES, stream>>>(prm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !split) return e;
   PlaneModuli pm{};
@@ -615,9 +675,11 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
   for (uint32_t t = 0; t < prob.task_count; ++t) {
     int64_t blocks = static_cast<int64_t>((plane_elems * prob.planes + 255) / 256);
     if (blocks > sm_count * 8) blocks = sm_count * 8;
+    SchedMask mask{sched ? sched->tile_sel_dev : nullptr, sched ? sched->shift_m : 0u, sched ? sched->shift_n : 0u,
+                   sched ? sched->cols : 0u, prob.n};
     split_finalize_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         static_cast<const int32_t*>(scratch) + static_cast<uint64_t>(t) * prob.planes * plane_elems,
-        static_cast<int64_t>(plane_elems), prob.planes, pm, prob.tasks[t].c);
+        static_cast<int64_t>(plane_elems), prob.planes, pm, prob.tasks[t].c, mask);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -708,6 +770,157 @@ cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+// ---- scheduled (per-tile prefix) plane GEMM --------------------------------------
+namespace {
+
+uint32_t log2_u32(uint32_t v) {
+  uint32_t s = 0;
+  while ((1u << s) < v) ++s;
+  return s;
+}
+
+// Host-side work lists of a scheduled run.
+struct ScheduledWork {
+  std::vector<uint64_t> units;  // tensor-core units, plane-outer
+  std::vector<ZeroTile> zeros;  // proven-zero schedule tiles
+  TcSchedule s{};
+  bool tc = false;
+};
+
+ScheduledWork scheduled_work(const PlaneGemmProblem& prob, const PlaneSchedule& sched, int sm_count) {
+  ScheduledWork w;
+  const uint64_t tiles = sched.tile_rows * sched.tile_cols;
+  for (uint64_t t = 0; t < tiles; ++t) {
+    const uint8_t sel = sched.tile_sel[t];
+    if (!(sel & 0x80u) || (sel & 0x7Fu) == 0) continue;
+    const uint64_t tr = t / sched.tile_cols, tc = t % sched.tile_cols;
+    ZeroTile z{};
+    z.row0 = static_cast<int64_t>(tr * sched.tile_m);
+    z.col0 = static_cast<int64_t>(tc * sched.tile_n);
+    z.rows = std::min<int64_t>(sched.tile_m, prob.m - z.row0);
+    z.cols = std::min<int64_t>(sched.tile_n, prob.n - z.col0);
+    z.planes = sel & 0x7Fu;
+    w.zeros.push_back(z);
+  }
+  w.tc = tensor_core_path_supported(prob);
+  if (!w.tc) return w;
+  w.s = tc_schedule(prob, sm_count);
+  // Planes each 128 x 256 kernel tile must compute: the largest selected
+  // prefix among the schedule tiles it covers that are not proven zero.
+  std::vector<uint8_t> need(static_cast<size_t>(w.s.m_tiles) * w.s.n_tiles, 0);
+  for (uint32_t mt = 0; mt < w.s.m_tiles; ++mt)
+    for (uint32_t nt = 0; nt < w.s.n_tiles; ++nt) {
+      const uint64_t r0 = static_cast<uint64_t>(mt) * BM / sched.tile_m;
+      const uint64_t r1 = std::min<uint64_t>((static_cast<uint64_t>(mt) * BM + BM - 1) / sched.tile_m,
+                                             sched.tile_rows - 1);
+      const uint64_t c0 = static_cast<uint64_t>(nt) * BN / sched.tile_n;
+      const uint64_t c1 = std::min<uint64_t>((static_cast<uint64_t>(nt) * BN + BN - 1) / sched.tile_n,
+                                             sched.tile_cols - 1);
+      uint8_t v = 0;
+      for (uint64_t r = r0; r <= r1; ++r)
+        for (uint64_t c = c0; c <= c1; ++c) {
+          const uint8_t sel = sched.tile_sel[r * sched.tile_cols + c];
+          if (!(sel & 0x80u)) v = std::max<uint8_t>(v, sel & 0x7Fu);
+        }
+      need[static_cast<size_t>(mt) * w.s.n_tiles + nt] = v;
+    }
+  const uint64_t raster = static_cast<uint64_t>(w.s.m_tiles) * w.s.n_tiles;
+  for (uint32_t p = 0; p < prob.planes; ++p)
+    for (uint32_t sp = 0; sp < w.s.splits; ++sp)
+      for (uint64_t tile = 0; tile < raster; ++tile) {
+        // the grouped raster order of decode_unit
+        const uint32_t span = GROUP_M * w.s.n_tiles;
+        const uint32_t group = static_cast<uint32_t>(tile / span);
+        const uint32_t first_m = group * GROUP_M;
+        const uint32_t gsize = std::min<uint32_t>(w.s.m_tiles - first_m, GROUP_M);
+        const uint32_t in_group = static_cast<uint32_t>(tile % span);
+        const uint32_t mt = first_m + in_group % gsize, nt = in_group / gsize;
+        if (p >= need[static_cast<size_t>(mt) * w.s.n_tiles + nt]) continue;
+        w.units.push_back(static_cast<uint64_t>(p) | (static_cast<uint64_t>(sp) << 8) |
+                          (static_cast<uint64_t>(mt) << 24) | (static_cast<uint64_t>(nt) << 44));
+      }
+  return w;
+}
+
+uint64_t r256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+// Cells whose tile needs plane p take the value computed into `src`.
+__global__ void __launch_bounds__(256) masked_copy_kernel(const int8_t* __restrict__ src, int8_t* __restrict__ dst,
+                                                          int64_t m, int64_t n, uint32_t planes,
+                                                          const uint8_t* __restrict__ tile_sel, uint32_t shift_m,
+                                                          uint32_t shift_n, uint32_t cols) {
+  for (int64_t row = blockIdx.y; row < m; row += gridDim.y)
+    for (int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; col < n;
+         col += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const uint8_t sel = tile_sel[(row >> shift_m) * cols + (col >> shift_n)];
+      if (sel & 0x80u) continue;
+      for (uint32_t p = 0; p < (sel & 0x7Fu) && p < planes; ++p)
+        dst[static_cast<int64_t>(p) * m * n + row * n + col] = src[static_cast<int64_t>(p) * m * n + row * n + col];
+    }
+}
+
+}  // namespace
+
+uint64_t plane_gemm_scheduled_scratch_bytes(const PlaneGemmProblem& prob, const PlaneSchedule& sched, int sm_count) {
+  const ScheduledWork w = scheduled_work(prob, sched, sm_count);
+  const uint64_t tiles = sched.tile_rows * sched.tile_cols;
+  uint64_t bytes = r256(tiles) + r256(w.zeros.size() * sizeof(ZeroTile));
+  if (w.tc)
+    bytes += r256(w.units.size() * sizeof(uint64_t)) + r256(plane_gemm_scratch_bytes(prob, sm_count));
+  else
+    bytes += r256(static_cast<uint64_t>(prob.planes) * prob.m * prob.n);  // SIMT result before the masked copy
+  return bytes;
+}
+
+cudaError_t plane_gemm_scheduled(const PlaneGemmProblem& prob, const PlaneSchedule& sched, int sm_count,
+                                 void* scratch, uint64_t scratch_bytes, uint32_t* dev_status, cudaStream_t stream) {
+  if (prob.task_count != 1 || sched.tile_m < 64 || sched.tile_n < 64) return cudaErrorInvalidValue;
+  const ScheduledWork w = scheduled_work(prob, sched, sm_count);
+  if (scratch_bytes < plane_gemm_scheduled_scratch_bytes(prob, sched, sm_count) || !scratch)
+    return cudaErrorInvalidValue;
+  const uint64_t tiles = sched.tile_rows * sched.tile_cols;
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  uint8_t* sel_dev = base;
+  base += r256(tiles);
+  auto* zeros_dev = reinterpret_cast<ZeroTile*>(base);
+  base += r256(w.zeros.size() * sizeof(ZeroTile));
+  cudaError_t e = cudaMemcpyAsync(sel_dev, sched.tile_sel, tiles, cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return e;
+  int8_t* c = prob.tasks[0].c;
+  const uint32_t shift_m = log2_u32(sched.tile_m), shift_n = log2_u32(sched.tile_n);
+  const uint32_t cols = static_cast<uint32_t>(sched.tile_cols);
+  if (!w.zeros.empty()) {
+    e = cudaMemcpyAsync(zeros_dev, w.zeros.data(), w.zeros.size() * sizeof(ZeroTile), cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return e;
+    const unsigned blocks = static_cast<unsigned>(std::min<size_t>(w.zeros.size(), 148 * 8));
+    zero_tiles_kernel<<<blocks, 256, 0, stream>>>(zeros_dev, static_cast<uint32_t>(w.zeros.size()), c, prob.m, prob.n);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (!w.tc) {
+    // Unaligned shapes: every plane into scratch with the SIMT kernel, then the
+    // cells each tile needs into C.
+    int8_t* tmp = reinterpret_cast<int8_t*>(base);
+    PlaneGemmTask task = prob.tasks[0];
+    task.c = tmp;
+    PlaneGemmProblem p2 = prob;
+    p2.tasks = &task;
+    if ((e = simt_plane_gemm(p2, stream)) != cudaSuccess) return e;
+    const int64_t by = prob.m < 65535 ? prob.m : 65535;
+    const int64_t bx = std::min<int64_t>((prob.n + 255) / 256, 64);
+    masked_copy_kernel<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(by)), 256, 0, stream>>>(
+        tmp, c, prob.m, prob.n, prob.planes, sel_dev, shift_m, shift_n, cols);
+    return cudaGetLastError();
+  }
+  if (w.units.empty()) return cudaSuccess;
+  auto* units_dev = reinterpret_cast<uint64_t*>(base);
+  base += r256(w.units.size() * sizeof(uint64_t));
+  e = cudaMemcpyAsync(units_dev, w.units.data(), w.units.size() * sizeof(uint64_t), cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return e;
+  TcScheduleUnits su{units_dev, w.units.size(), sel_dev, shift_m, shift_n, cols};
+  const uint64_t rest = scratch_bytes - static_cast<uint64_t>(base - static_cast<uint8_t*>(scratch));
+  return tc_plane_gemm(prob, sm_count, base, rest, dev_status, stream, &su);
 }
 
 // ---- GEMM followed by the bounded export --------------------------------------

@@ -43,6 +43,29 @@ struct PlaneGemmProblem {
 };
 enum class GemmPath : int { Auto = 0, TensorCore = 1, Simt = 2 };
 
+// Per-tile prefix schedule of a plan (reference api_plan_schedule.inc:109-261)
+// for scheduled GEMM and export: tile_sel[tile_row * tile_cols + tile_col] is
+// the tile's selected prefix, | 0x80 when its output is proven zero.
+struct PlaneSchedule {
+  uint32_t tile_m, tile_n;  // powers of two in [64, 512]
+  uint64_t tile_rows, tile_cols;
+  const uint8_t* tile_sel;  // host array
+};
+// Plane GEMM of one task under a schedule (cpu_reference.cpp:221-260): each
+// schedule tile gets the planes below its selected prefix; proven-zero tiles
+// are zero-filled there; planes at or above a tile's prefix are not written.
+uint64_t plane_gemm_scheduled_scratch_bytes(const PlaneGemmProblem& prob, const PlaneSchedule& sched, int sm_count);
+cudaError_t plane_gemm_scheduled(const PlaneGemmProblem& prob, const PlaneSchedule& sched, int sm_count,
+                                 void* scratch, uint64_t scratch_bytes, uint32_t* dev_status, cudaStream_t stream);
+// Bounded export under a per-tile schedule (api_export.cpp:365-414): each
+// cell is reconstructed from its tile's selected prefix and checked against
+// its tile's bound (tile_bounds, host array); proven-zero tiles export 0.
+// dst is uint64 m x n (ld = n); range errors are ORed into *dev_status.
+uint64_t export_scheduled_scratch_bytes(const PlaneSchedule& sched);
+cudaError_t export_scheduled(const int8_t* planes, int64_t m, int64_t n, bool is_signed, const PlaneSchedule& sched,
+                             const uint64_t* tile_bounds, void* dst, uint32_t* dev_status, void* scratch,
+                             uint64_t scratch_bytes, cudaStream_t stream);
+
 // Scratch the tensor-core path needs for split-K (int32 per output element
 // of the largest chunk). Returns 0 when the problem runs without split-K.
 uint64_t plane_gemm_scratch_bytes(const PlaneGemmProblem& prob, int sm_count);

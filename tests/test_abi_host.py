@@ -160,3 +160,69 @@ def test_reference_reducer_fixture_matches_kernel_reduction(oracle):
         r = np.where(r >= off, r - off, r + m - off).astype(np.int64)
         r = np.where(r >= (int(m_str) + 1) // 2, r - int(m_str), r)
         assert r.tolist() == expected
+
+
+# ---- per-tile bound schedules (host-only probe against the oracle) -----------------
+def _schedule_cases():
+    rng = np.random.default_rng(77)
+    I64, U64 = 1, 2
+    cases = []
+    for trial in range(60):
+        sem = I64 if trial % 2 == 0 else U64
+        tile_m, tile_n = [64, 128, 256][trial % 3], [64, 128, 512][(trial // 3) % 3]
+        m, n = int(rng.integers(1, 900)), int(rng.integers(1, 900))
+        tiles = -(-m // tile_m) * -(-n // tile_n)
+        top = 2**63 if sem == I64 else 2**64 - 1
+        kind = trial % 5
+        if kind == 0:
+            bounds = [int(rng.integers(0, 2**20)) for _ in range(tiles)]
+        elif kind == 1:
+            bounds = [0 if rng.random() < 0.4 else int(rng.integers(1, top, dtype=np.uint64)) for _ in range(tiles)]
+        elif kind == 2:
+            bounds = [top] * tiles  # collapses: every tile needs the plan prefix
+        elif kind == 3:
+            bounds = [int(2 ** int(rng.integers(0, 60))) for _ in range(tiles)]
+        else:
+            bounds = [int(rng.integers(0, top, dtype=np.uint64)) for _ in range(tiles)]
+        flags = [0, 1, 2, 3, 6, 7][trial % 6]  # FORCE_FIXED_PREFIX | ZERO_TILE_SKIPS | ZERO_ROW_COL_SKIPS
+        za = (rng.random(m) < 0.05).astype(np.uint8) if flags & 4 else None
+        zb = (rng.random(n) < 0.05).astype(np.uint8) if flags & 4 else None
+        max_prefix = [0, 9, 12][trial % 3] if kind != 2 else 0
+        cases.append((sem, m, n, tile_m, tile_n, max_prefix, flags, bounds, za, zb))
+    return cases
+
+
+@pytest.mark.parametrize("case", _schedule_cases())
+def test_tile_schedule_matches_oracle(rns8, oracle, case):
+    """configure_plan_schedule for per-tile bounds (api_plan_schedule.inc:178-261)
+    and rns8_get_plan_tile_schedule (api_plan_public_api.inc:119-167)."""
+    sem, m, n, tile_m, tile_n, max_prefix, flags, bounds, za, zb = case
+    bk = rns8.BoundKind.PER_TILE_MAX_ABS if sem == 1 else rns8.BoundKind.PER_TILE_MAX_UNSIGNED
+    desc = rns8.gemm_desc(sem, bk, m, n, 16, max_prefix=max_prefix, flags=flags, tile_m=tile_m, tile_n=tile_n)
+    rns8.api.set_tile_bounds(desc, bounds, za, zb)
+    ost, rows, summ = oracle.plan_tile_schedule(sem, m, n, tile_m, tile_n, max_prefix, flags, bounds, za, zb)
+    try:
+        entries, info = rns8.api.plan_tile_schedule_probe(desc)
+        st = 0
+    except rns8.Error as e:
+        st = int(e.status)
+    assert st == ost
+    if st != 0:
+        return
+    assert len(entries) == len(rows)
+    assert (info.min_required_prefix, info.max_required_prefix, info.min_selected_prefix,
+            info.max_selected_prefix, info.prefix_group_count, info.range_bit_length, info.adaptive_prefix_active,
+            info.adaptive_skip_active, info.flags) == tuple(summ[k] for k in (
+                "min_required", "max_required", "min_selected", "max_selected", "group_count", "range_bits",
+                "adaptive_prefix", "adaptive_skip", "flags"))
+    tile_cols = -(-n // tile_n)
+    for t, (e, row) in enumerate(zip(entries, rows)):
+        assert (e.tile_row, e.tile_col) == (t // tile_cols, t % tile_cols)
+        assert (e.row_offset, e.col_offset) == (e.tile_row * tile_m, e.tile_col * tile_n)
+        assert e.row_extent == min(tile_m, m - e.row_offset) and e.col_extent == min(tile_n, n - e.col_offset)
+        assert e.required_prefix == row[0] and e.range_bit_length == row[3]
+        if summ["collapsed"]:
+            # a cleared schedule reports every tile at the plan's selected prefix, group 0, no flags
+            assert (e.selected_prefix, e.group_index, e.flags) == (summ["min_selected"], 0, 0)
+        else:
+            assert (e.selected_prefix, e.group_index, e.flags) == (row[1], row[2], row[4])
