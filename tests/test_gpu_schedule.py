@@ -170,3 +170,30 @@ def test_zero_row_col_flags_and_grouped_scheduled(r8, ctx, oracle):
         np.testing.assert_array_equal(r8.export_i64(ctx, plan, c), A @ B)
     for h in handles + [plan]:
         h.close()
+
+
+def test_resident_bounded_chain(r8, ctx):
+    """C = A x B stays resident as residues and feeds D = C x E without an
+    export (the persistent-residue model, api_gemm.cpp:938-961); only D is
+    exported, with the second plan's bound."""
+    rng = np.random.default_rng(9)
+    m, k, n, n2 = 256, 64, 128, 96
+    A = rng.integers(-(2**12), 2**12, (m, k), dtype=np.int64, endpoint=True)
+    B = rng.integers(-(2**12), 2**12, (k, n), dtype=np.int64, endpoint=True)
+    E = rng.integers(-(2**12), 2**12, (n, n2), dtype=np.int64, endpoint=True)
+    D = (A @ B) @ E  # |D| < 2^49
+    bound = int(np.abs(D).max())
+    sem, bk = r8.Semantics.BOUNDED_I64, r8.BoundKind.GLOBAL_MAX_ABS
+    p1 = r8.Plan(ctx, r8.gemm_desc(sem, bk, m, n, k, bound=2**40, max_prefix=8, flags=r8.PLAN_FORCE_FIXED_PREFIX))
+    p2 = r8.Plan(ctx, r8.gemm_desc(sem, bk, m, n2, n, bound=bound, max_prefix=8, flags=r8.PLAN_FORCE_FIXED_PREFIX))
+    a, b, c = (r8.Matrix.for_plan(ctx, p1, role) for role in "abc")
+    e, d = r8.Matrix.for_plan(ctx, p2, "b"), r8.Matrix.for_plan(ctx, p2, "c")
+    w1, w2 = r8.Workspace(ctx, p1), r8.Workspace(ctx, p2)
+    a.pack_i64(A)
+    b.pack_i64(B)
+    e.pack_i64(E)
+    r8.gemm_rns(ctx, p1, a, b, c, w1)
+    r8.gemm_rns(ctx, p2, c, e, d, w2)  # C's residue planes are the next A
+    np.testing.assert_array_equal(r8.export_i64(ctx, p2, d), D)
+    for h in (a, b, c, e, d, w1, w2, p1, p2):
+        h.close()
