@@ -14,6 +14,13 @@ struct PlaneModuli {
 
 cudaError_t simt_plane_gemm(const PlaneGemmProblem& prob, cudaStream_t stream);
 
+// Narrow outputs (1 <= n < 16): B^T staging in scratch, then a dp4a stream
+// over A's planes (gemm_skinny.cu).
+bool skinny_path_supported(const PlaneGemmProblem& prob);
+uint64_t skinny_scratch_bytes(const PlaneGemmProblem& prob);
+cudaError_t skinny_plane_gemm(const PlaneGemmProblem& prob, void* scratch, uint64_t scratch_bytes,
+                              cudaStream_t stream);
+
 // Split-K decomposition chosen for the tensor-core kernel.
 struct TcSchedule {
   uint32_t m_tiles, n_tiles, total_kb, splits, kb_per_split;

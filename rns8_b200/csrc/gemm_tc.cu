@@ -743,7 +743,7 @@ bool tensor_core_path_supported(const PlaneGemmProblem& prob) {
 }
 
 uint64_t plane_gemm_scratch_bytes(const PlaneGemmProblem& prob, int sm_count) {
-  if (!tensor_core_path_supported(prob)) return 0;
+  if (!tensor_core_path_supported(prob)) return skinny_scratch_bytes(prob);  // 0 unless n < 16
   const uint32_t chunk = prob.task_count < kMaxGroupTasks ? prob.task_count : kMaxGroupTasks;
   PlaneGemmProblem one = prob;
   one.task_count = chunk;
@@ -756,6 +756,11 @@ cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count
                        uint64_t scratch_bytes, uint32_t* dev_status, cudaStream_t stream, GemmPath* used) {
   const bool tc_ok = tensor_core_path_supported(prob);
   if (path == GemmPath::TensorCore && !tc_ok) return cudaErrorInvalidValue;
+  if (path == GemmPath::Auto && !tc_ok && skinny_path_supported(prob) && scratch &&
+      scratch_bytes >= skinny_scratch_bytes(prob)) {
+    if (used) *used = GemmPath::Simt;  // the narrow-output kernel (CUDA cores)
+    return skinny_plane_gemm(prob, scratch, scratch_bytes, stream);
+  }
   if (path == GemmPath::Simt || !tc_ok) {
     if (used) *used = GemmPath::Simt;
     return simt_plane_gemm(prob, stream);

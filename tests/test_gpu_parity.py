@@ -172,6 +172,32 @@ def test_plane_gemm_k_longer_than_safe_block(lib, oracle, k):
         np.testing.assert_array_equal(got, want, err_msg=f"path {path}")
 
 
+@pytest.mark.parametrize("m,n,k", [
+    (300, 1, 4096),     # GEMV
+    (37, 3, 40),        # K not a multiple of 16: 4-byte steps with bounds checks
+    (513, 8, 1000),
+    (64, 12, 4096),
+    (300, 15, 70000),   # K above 65536: two exact int32 segments per row
+    (1, 15, 33),
+])
+def test_narrow_output_gemm_matches_oracle(lib, oracle, m, n, k):
+    """n < 16 runs the narrow-output kernel (B^T staging + dp4a stream); it
+    must agree with the oracle and with the SIMT kernel byte for byte."""
+    rng = np.random.default_rng(m * 31 + n * 7 + k)
+    P = 9
+    a = random_residues(rng, P, m, k)
+    b = random_residues(rng, P, k, n)
+    for p in range(P):  # the most negative residue of each plane along the first row
+        a[p, 0, :] = -128 if LADDER[p] % 2 == 0 else -(LADDER[p] // 2)
+    st, got, word = run_gemm(lib, a, b, P, 0)
+    assert st == OK and word == 0
+    want = oracle.gemm_rns(a, b, P)
+    np.testing.assert_array_equal(got, want)
+    st, simt, _ = run_gemm(lib, a, b, P, 2)
+    assert st == OK
+    np.testing.assert_array_equal(simt, want)
+
+
 def test_finite_grouped_gemm_matches_oracle(lib, oracle):
     rng = np.random.default_rng(11)
     tasks, m, n, k, mod = 5, 256, 256, 512, 251
