@@ -412,6 +412,101 @@ rns8_status validate_typed_oneshot(const rns8_gemm_desc& d, rns8_semantics expec
   return RNS8_SUCCESS;
 }
 
+// One-shot with the upload overlapped (SURVEY's host-boundary row): B, then A
+// in row slabs, go up on the context's copy stream, each slab followed by an
+// event; the compute stream packs B, then for every slab waits for its event
+// and runs pack, plane GEMM and export into device staging. Copies and compute
+// are enqueued interleaved, so pageable host memory (whose copies return only
+// when done) overlaps too. The result goes down only after every slab passed
+// the range check, so a RANGE_ERROR leaves C untouched.
+template <typename T>
+rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, const T* A, int64_t lda, const T* B,
+                                      int64_t ldb, T* C, int64_t ldc, int slabs) {
+  constexpr bool kSigned = std::numeric_limits<T>::is_signed;
+  const int64_t m = plan.desc.m, n = plan.desc.n, k = plan.desc.k;
+  const uint32_t P = plan.prefix;
+  const int64_t rows = (m + slabs - 1) / slabs;
+  const int64_t slab_rows = (rows + 127) / 128 * 128;  // whole 128-row tiles per slab
+  int8_t* const fake = reinterpret_cast<int8_t*>(256);
+  rns8cuda::PlaneGemmTask task{fake, fake, fake};
+  rns8cuda::PlaneGemmProblem prob = rns_problem(plan, P, &task, 1, 0);
+  // Split-K scratch of the largest slab and of the last, shorter one (fewer
+  // tiles can mean more K splits).
+  const int64_t last_rows = m - (m - 1) / slab_rows * slab_rows;
+  prob.m = last_rows;
+  const uint64_t scratch_last = rns8cuda::plane_gemm_scratch_bytes(prob, ctx->sm_count);
+  prob.m = std::min<int64_t>(slab_rows, m);
+  const uint64_t scratch = std::max(rns8cuda::plane_gemm_scratch_bytes(prob, ctx->sm_count), scratch_last);
+  const uint64_t a_nat = static_cast<uint64_t>(m) * k * sizeof(T), b_nat = static_cast<uint64_t>(k) * n * sizeof(T);
+  const uint64_t a_res = static_cast<uint64_t>(P) * prob.m * k, b_res = static_cast<uint64_t>(P) * k * n;
+  const uint64_t c_res = static_cast<uint64_t>(P) * prob.m * n, c_nat = static_cast<uint64_t>(m) * n * sizeof(T);
+  const uint64_t total = round256(a_nat) + round256(b_nat) + round256(a_res) + round256(b_res) + round256(c_res) +
+                         round256(c_nat) + round256(scratch);
+  std::unique_lock<std::mutex> lock(ctx->oneshot_mutex, std::try_to_lock);
+  DevBuf local;
+  DevBuf& arena = lock.owns_lock() ? ctx->oneshot_arena : local;
+  rns8_status st = arena.ensure(ctx->device_id, total);
+  if (st != RNS8_SUCCESS) return st;
+  Carve cv{static_cast<uint8_t*>(arena.ptr)};
+  T* dA = static_cast<T*>(cv.take(a_nat));
+  T* dB = static_cast<T*>(cv.take(b_nat));
+  int8_t* rA = static_cast<int8_t*>(cv.take(a_res));
+  int8_t* rB = static_cast<int8_t*>(cv.take(b_res));
+  int8_t* rC = static_cast<int8_t*>(cv.take(c_res));
+  T* dC = static_cast<T*>(cv.take(c_nat));
+  void* dS = cv.take(scratch);
+  auto pack = [&](const T* src, int64_t r, int64_t c, int8_t* planes) {
+    return kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(src), r, c, c, P, planes, ctx->stream)
+                   : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(src), r, c, c, P, planes, ctx->stream);
+  };
+  std::vector<cudaEvent_t> events(static_cast<size_t>(slabs) + 1, nullptr);
+  auto destroy = [&] {
+    for (cudaEvent_t& e : events)
+      if (e) cudaEventDestroy(e);
+  };
+  for (cudaEvent_t& e : events)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      destroy();
+      return RNS8_BACKEND_FAILURE;
+    }
+  auto upload = [&](void* dst, const T* src, int64_t r, int64_t c, int64_t ld, cudaEvent_t done) {
+    return cudaMemcpy2DAsync(dst, static_cast<size_t>(c) * sizeof(T), src, static_cast<size_t>(ld) * sizeof(T),
+                             static_cast<size_t>(c) * sizeof(T), static_cast<size_t>(r), cudaMemcpyHostToDevice,
+                             ctx->copy_stream) == cudaSuccess &&
+           cudaEventRecord(done, ctx->copy_stream) == cudaSuccess;
+  };
+  bool ok = clear_status(*ctx) == RNS8_SUCCESS && upload(dB, B, k, n, ldb, events[0]) &&
+            cudaStreamWaitEvent(ctx->stream, events[0], 0) == cudaSuccess && pack(dB, k, n, rB) == cudaSuccess;
+  for (int i = 0; ok && i < slabs; ++i) {
+    const int64_t r0 = i * slab_rows;
+    if (r0 >= m) break;
+    const int64_t r = std::min<int64_t>(slab_rows, m - r0);
+    ok = upload(dA + r0 * k, A + r0 * lda, r, k, lda, events[i + 1]) &&
+         cudaStreamWaitEvent(ctx->stream, events[i + 1], 0) == cudaSuccess &&
+         pack(dA + r0 * k, r, k, rA) == cudaSuccess;
+    if (!ok) break;
+    task = {rA, rB, rC};
+    prob.m = r;
+    ok = rns8cuda::plane_gemm(prob, rns8cuda::GemmPath::Auto, ctx->sm_count, dS, scratch, ctx->dev_status,
+                              ctx->stream) == cudaSuccess;
+    if (ok)
+      ok = (kSigned ? rns8cuda::export_i64(rC, r, n, P, plan.desc.bound, reinterpret_cast<int64_t*>(dC) + r0 * n, n,
+                                           ctx->dev_status, ctx->stream)
+                    : rns8cuda::export_u64(rC, r, n, P, plan.desc.bound, reinterpret_cast<uint64_t*>(dC) + r0 * n, n,
+                                           ctx->dev_status, ctx->stream)) == cudaSuccess;
+  }
+  // Both streams finish before the events go and before any result is read.
+  const bool copies_ok = cudaStreamSynchronize(ctx->copy_stream) == cudaSuccess;
+  uint32_t word = 0;
+  st = read_status(*ctx, &word);
+  destroy();
+  if (!ok || !copies_ok) return RNS8_BACKEND_FAILURE;
+  if (st != RNS8_SUCCESS) return st;
+  if ((st = status_from_device(word)) != RNS8_SUCCESS) return st;
+  if ((st = copy_out_2d(*ctx, C, ldc, dC, m, n, sizeof(T))) != RNS8_SUCCESS) return st;
+  return sync(*ctx);
+}
+
 // One-shot under a per-tile bound plan: pack the storage prefix, the
 // scheduled plane GEMM, the per-tile export, all in the context's arena.
 template <typename T>
@@ -491,6 +586,11 @@ rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const
   DeviceScope dev(ctx->device_id);
   if (!dev.ok) return RNS8_BACKEND_FAILURE;
   if (!plan.tile_bounds.empty()) return bounded_oneshot_per_tile<T>(ctx, plan, A, lda, B, ldb, C, ldc);
+  // Large calls overlap the upload with pack, GEMM and export, slab by slab.
+  if (plan.desc.m >= 1024 && static_cast<uint64_t>(plan.desc.m) * plan.desc.k * 8 >= (uint64_t{64} << 20)) {
+    const int slabs = static_cast<int>(std::min<int64_t>(8, plan.desc.m / 512));
+    return bounded_oneshot_pipelined<T>(ctx, plan, A, lda, B, ldb, C, ldc, slabs);
+  }
   const int64_t m = plan.desc.m, n = plan.desc.n, k = plan.desc.k;
   const uint32_t P = plan.prefix;
   const uint64_t a_nat = static_cast<uint64_t>(m) * k * 8, b_nat = static_cast<uint64_t>(k) * n * 8;

@@ -53,6 +53,7 @@ struct rns8_context {
   int device_id = 0;
   int sm_count = 148;
   cudaStream_t stream = nullptr;
+  cudaStream_t copy_stream = nullptr;  // host-to-device uploads overlapped with `stream`
   rns8_device_info info{};
   uint32_t* dev_status = nullptr;  // 4 status words
   // Device arena reused by the one-shot entry points (serialised by the mutex).

@@ -74,8 +74,10 @@ extern "C" rns8_status rns8_create_context(int device_id, const rns8_context_opt
     ctx->device_id = dev;
     ctx->sm_count = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(reinterpret_cast<void**>(&ctx->dev_status), 4 * sizeof(uint32_t)) != cudaSuccess) {
       if (ctx->stream) cudaStreamDestroy(ctx->stream);
+      if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
       delete ctx;
       return RNS8_BACKEND_FAILURE;
     }
@@ -104,9 +106,12 @@ extern "C" rns8_status rns8_destroy_context(rns8_context* ctx) {
   if (!ctx) return RNS8_SUCCESS;
   cudaSetDevice(ctx->device_id);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
   ctx->oneshot_arena.release();
+  ctx->admission.release();
   if (ctx->dev_status) cudaFree(ctx->dev_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   delete ctx;
   return RNS8_SUCCESS;
 }

@@ -656,3 +656,31 @@ def test_full_size_bounded_i64_exact(lib, n, forced, one_call):
     assert int(status[0].item()) == 0
     want = exact_i64_matmul_fp64(A, B)
     assert torch.equal(out, want)
+
+
+@pytest.mark.parametrize("signed", [True, False])
+def test_pipelined_oneshot_matches_exact(rns8, ctx, signed):
+    """Large one-shot calls upload A in row slabs on a copy stream overlapped
+    with pack / GEMM / export: 1100 rows make two slabs of 640 and 460 rows;
+    pageable inputs with padded leading dimensions; a bound the values exceed
+    returns RANGE_ERROR and leaves C untouched."""
+    rng = np.random.default_rng(1100 + signed)
+    m, n, k = 1100, 64, 8192
+    lo = -(2**20) if signed else 0
+    dt = np.int64 if signed else np.uint64
+    A = rng.integers(lo, 2**20, (m, k + 3), dtype=dt, endpoint=True)
+    B = rng.integers(lo, 2**20, (k, n + 5), dtype=dt, endpoint=True)
+    want = A[:, :k] @ B[:, :n]  # |C| <= 2^53: exact in 64-bit integers
+    bound = int(np.abs(want.astype(np.float64)).max()) + 1
+    sem = rns8.Semantics.BOUNDED_I64 if signed else rns8.Semantics.BOUNDED_U64
+    bk = rns8.BoundKind.GLOBAL_MAX_ABS if signed else rns8.BoundKind.GLOBAL_MAX_UNSIGNED
+    fn = rns8.gemm_i64_oneshot if signed else rns8.gemm_u64_oneshot
+    out = np.full((m, n + 2), 7, dt)
+    fn(ctx, rns8.gemm_desc(sem, bk, m, n, k, bound=bound), A[:, :k], B[:, :n], out=out[:, :n])
+    np.testing.assert_array_equal(out[:, :n], want)
+    assert (out[:, n:] == 7).all()
+    untouched = np.full((m, n), 9, dt)
+    with pytest.raises(rns8.Error) as err:
+        fn(ctx, rns8.gemm_desc(sem, bk, m, n, k, bound=bound // 4), A[:, :k], B[:, :n], out=untouched)
+    assert err.value.status == rns8.Status.RANGE_ERROR
+    assert (untouched == 9).all()
