@@ -36,7 +36,7 @@ namespace rns8cuda {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4, UMMA_K = 32;
-constexpr int GROUP_M = 16;  // raster: 16 M-tiles per column sweep for L2 reuse
+constexpr int GROUP_M = 32;  // raster: 32 M-tiles per column sweep for L2 reuse
 constexpr uint32_t A_BYTES = BM * BK;
 constexpr uint32_t B_HALF_BYTES = BK * 128;
 constexpr uint32_t B_BYTES = BK * BN;
