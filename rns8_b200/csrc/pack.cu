@@ -3,16 +3,18 @@
 // layout res[p*rows*cols + r*cols + c] from :46-51).
 //
 // Reduction of a 64-bit value modulo a ladder modulus m (m <= 256): with the
-// eight bytes b_j of its two's-complement bits u,
+// eight bytes b_j of an unsigned 64-bit u,
 //   u = sum_j b_j * 2^(8j)  =  sum_j b_j * w_j  (mod m),  w_j = 2^(8j) mod m < 256,
-// which is two dp4a instructions. A negative value x = u - 2^64 adds
-// (-2^64) mod m. Centering is folded in: with h = ceil(m/2),
-//   centered(x mod m) = ((x + m - h) mod m) - (m - h),
-// so the constant m - h joins the dp4a accumulator. The folded sum is below
-// 2^19, where q = mulhi(S, ceil(2^32/m)) is the exact quotient, so each
-// residue costs two dp4a, one mul-hi and two integer ops. The byte split is
-// shared by every plane; per-plane constants are immediates because the
-// prefix is a template parameter.
+// which is two dp4a instructions. A signed x is packed as u = x + 2^63 (its
+// top bit flipped), and the constant (-2^63) mod m starts the dp4a sum, so
+// both signs take the same path. The sum t is below 2^20, where
+// q = mulhi(t + h, ceil(2^32/m)) is the exact quotient of t + h by m; with
+// h = floor(m/2), t - q*m is the centered residue (in [-h, m - 1 - h]). The
+// +h folds into the 64-bit addend of one wide multiply-add, so a residue
+// costs two dp4a, one wide multiply-add and one multiply-add. Modulus 256 is
+// the low byte itself (two's complement). The byte split is shared by every
+// plane; per-plane constants are immediates because the prefix is a
+// template parameter.
 #include "device_common.cuh"
 #include "kernels.hpp"
 
@@ -30,39 +32,40 @@ __host__ __device__ __forceinline__ uint32_t ladder_modulus(int i) {
 }
 
 struct Words {
-  uint32_t lo, hi, neg;
+  uint32_t lo, hi;  // the value as unsigned 64 bits (signed: x + 2^63)
 };
 
 template <typename T>
 __device__ __forceinline__ Words split_words(T v) {
   const uint64_t u = static_cast<uint64_t>(v);
-  Words w;
-  w.lo = static_cast<uint32_t>(u);
-  w.hi = static_cast<uint32_t>(u >> 32);
-  w.neg = (static_cast<T>(-1) < 0) ? (w.hi >> 31) : 0u;
-  return w;
+  constexpr uint32_t kBias = (static_cast<T>(-1) < 0) ? 0x80000000u : 0u;
+  return Words{static_cast<uint32_t>(u), static_cast<uint32_t>(u >> 32) ^ kBias};
 }
 
 // Low byte of the centered residue of the element modulo ladder entry p.
 template <bool kSigned>
 __device__ __forceinline__ uint32_t residue_byte(const Words& w, int p) {
   const uint32_t m = ladder_modulus(p);
-  const uint32_t shift = m - (m + 1) / 2;  // m - ceil(m/2)
+  if (m == 256) return w.lo;  // the low byte; the signed bias only touches bit 63
+  const uint32_t h = m / 2;
   uint32_t wl = 0, wh = 0;
   uint64_t pow = 1;  // 2^(8j) mod m
+  uint64_t pow56 = 1;
   for (int j = 0; j < 8; ++j) {
     if (j < 4)
       wl |= static_cast<uint32_t>(pow) << (8 * j);
     else
       wh |= static_cast<uint32_t>(pow) << (8 * (j - 4));
+    if (j == 7) pow56 = pow;
     pow = (pow * 256) % m;
   }
-  const uint32_t wneg = (m - static_cast<uint32_t>(pow)) % m;  // pow == 2^64 mod m here
-  uint32_t s = kSigned ? shift + w.neg * wneg : shift;
-  s = __dp4a(w.hi, wh, s);
-  s = __dp4a(w.lo, wl, s);
-  const uint32_t q = __umulhi(s, static_cast<uint32_t>(((1ull << 32) + m - 1) / m));
-  return s - q * m - shift;  // low byte = centered residue
+  const uint32_t pow63 = static_cast<uint32_t>((pow56 * 128) % m);  // 2^63 mod m
+  const uint32_t start = kSigned ? (m - pow63) % m : 0u;           // (-2^63) mod m
+  const uint32_t magic = static_cast<uint32_t>(((1ull << 32) + m - 1) / m);
+  uint32_t t = __dp4a(w.hi, wh, start);
+  t = __dp4a(w.lo, wl, t);
+  const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(t) * magic + static_cast<uint64_t>(h) * magic) >> 32);
+  return t - q * m;  // low byte = centered residue
 }
 
 // Bytes 0 of a, b, c, d -> one word.
