@@ -412,7 +412,7 @@ rns8_status validate_typed_oneshot(const rns8_gemm_desc& d, rns8_semantics expec
   return RNS8_SUCCESS;
 }
 
-// One-shot with the upload overlapped (SURVEY's host-boundary row): B, then A
+// One-shot with the upload overlapped with compute: B, then A
 // in row slabs, go up on the context's copy stream, each slab followed by an
 // event; the compute stream packs B, then for every slab waits for its event
 // and runs pack, plane GEMM and export into device staging. Copies and compute

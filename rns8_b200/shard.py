@@ -2,7 +2,7 @@
 
 Output rows are independent: rank r of `world` computes rows
 [row0, row0 + rows) of C from the same rows of A and all of B, with no
-exchange between ranks (the path shards by output row slabs).
+exchange between ranks: output row slabs are independent units.
 The split is as even as possible; earlier ranks take the remainder rows.
 """
 

@@ -111,7 +111,7 @@ def reference_kats() -> dict:
         "example_bounded_i64": {"source": "examples/bounded_i64_oneshot.cpp:14-27", "m": 2, "n": 2, "k": 3,
                                 "bound": 100, "A": [2, -3, 4, -5, 6, 7], "B": [1, 8, -2, 9, 3, -4],
                                 "expected": [20, -27, 4, -14]},
-        "prefix_selection": {"source": "SURVEY configs; api_plan_schedule.inc:263-278",
+        "prefix_selection": {"source": "BASELINE.json configs; api_plan_schedule.inc:263-278",
                              "cases": [["i64", 2**49, 0, 0, 7], ["i64", 2**61, 0, 0, 8], ["i64", 2**61, 9, 1, 9],
                                        ["u64", 2**62, 0, 0, 8], ["i64", 2**63, 0, 0, 9], ["u64", 2**64 - 1, 0, 0, 9]]},
     }
