@@ -109,7 +109,15 @@ def parse():
     ap.add_argument("--cpu-rows", type=int, default=0, help="rows of A in the CPU baseline sample (0: the config's)")
     ap.add_argument("--size", type=int, default=0,
                     help="C3 only: M = N = K = size (8192 is the benchmark; smaller sizes are for ncu captures)")
+    ap.add_argument("--shard", choices=["weak-rows", "rows", "planes"], default="weak-rows",
+                    help="weak-rows: each rank owns an M-row slab (the benchmark line); rows / planes: the "
+                         "config's one product split across ranks by row slabs / by residue planes with the "
+                         "fused NVLink exchange (strong scaling, device-resident, for comparing the two)")
+    ap.add_argument("--exchange", choices=["fused", "copy"], default="fused",
+                    help="--shard planes: epilogue stores into the slab owners' buffers, or local planes + copies")
     args = ap.parse_args()
+    if args.shard != "weak-rows" and cfg_kind(args.config) not in ("i64", "u64", "exact"):
+        ap.error("--shard rows|planes applies to the int64/uint64/exact-wide configs")
     cfg = CONFIGS[args.config]
     if args.size:
         if cfg.name != "C3":
@@ -118,6 +126,10 @@ def parse():
     if args.cpu_rows:
         cfg = dataclasses.replace(cfg, cpu_rows=args.cpu_rows)
     return args, cfg
+
+
+def cfg_kind(name: str) -> str:
+    return CONFIGS[name].kind
 
 
 def dist_env():
@@ -539,10 +551,196 @@ class EndToEnd:
         self.ctx.close()
 
 
+class ShardedProduct:
+    """The config's single product split across ranks (strong scaling).
+
+    rows:   rank r packs its row slab of A and all of B into every plane,
+            multiplies and exports its slab (no exchange).
+    planes: rank r packs all of A and B into its planes {p : p mod world == r},
+            multiplies them for all of C with the row-slab scatter epilogue
+            (each output row stored into its owner's receive buffer, over
+            NVLink for peers), one NCCL barrier, then exports its own slab from
+            all planes. Receive buffers alternate between steps so that the
+            next step's scatter never overwrites a slab still being exported."""
+
+    def __init__(self, torch, dist, lib, cfg: Config, dev: int, rank: int, world: int, mode: str, exchange: str,
+                 sptr):
+        from rns8_b200 import shard
+
+        self.torch, self.dist, self.lib, self.cfg, self.dev, self.sptr = torch, dist, lib, cfg, dev, sptr
+        self.mode, self.world, self.rank = mode, world, rank
+        m, n, k, P = cfg.m, cfg.n, cfg.k, cfg.prefix
+        g = torch.Generator(device="cuda").manual_seed(999)
+        if cfg.kind == "exact":
+            self.A = torch.randint(0, 256, (m, k, 8), dtype=torch.uint8, device="cuda", generator=g).view(
+                torch.int64).reshape(m, k)
+            self.B = torch.randint(0, 256, (k, n, 8), dtype=torch.uint8, device="cuda", generator=g).view(
+                torch.int64).reshape(k, n)
+        else:
+            self.A = torch.randint(cfg.lo, cfg.hi + 1, (m, k), dtype=torch.int64, device="cuda", generator=g)
+            self.B = torch.randint(cfg.lo, cfg.hi + 1, (k, n), dtype=torch.int64, device="cuda", generator=g)
+        self.signed = cfg.kind != "u64"
+        if mode == "planes":
+            self.row0, self.rows = shard.slab_of_rank(rank, m, world)
+        else:
+            self.row0, self.rows = shard.row_slab(rank, world, m)
+        self.status = torch.zeros(4, dtype=torch.int32, device="cuda")
+        shape = (max(self.rows, 1), n, cfg.limbs) if cfg.kind == "exact" else (max(self.rows, 1), n)
+        self.out = torch.empty(shape, dtype=torch.int64, device="cuda")
+        self.launches_per_step = 0
+        if mode == "planes":
+            self.mine = shard.planes_of_rank(rank, world, P)
+            self.idx = (C.c_uint32 * max(1, len(self.mine)))(*self.mine)
+            self.ra = torch.empty((max(1, len(self.mine)), m, k), dtype=torch.int8, device="cuda")
+            self.rb = torch.empty((max(1, len(self.mine)), k, n), dtype=torch.int8, device="cuda")
+            self.ex = shard.PlaneExchange(shard.LibraryIpc(lib, dev), rank, world, m, n, P, buffers=2)
+            self.tables = [(C.c_void_p * self.ex.slab_count)(*self.ex.slab_table(b)) for b in range(2)]
+            self.copy = exchange == "copy"
+            self.sbytes = lib.rns8_cuda_gemm_rns_slabs_scratch_bytes(dev, m, n, k, max(1, len(self.mine)),
+                                                                     1 if self.copy else 0) if self.mine else 0
+            self.flag = torch.ones(1, device="cuda")
+            self.fused = C.c_uint32(0)
+            self.step_index = 0
+        else:
+            self.ex = None
+            r = max(self.rows, 1)
+            self.ra = torch.empty((P, r, k), dtype=torch.int8, device="cuda")
+            self.rb = torch.empty((P, k, n), dtype=torch.int8, device="cuda")
+            self.rc = torch.empty((P, r, n), dtype=torch.int8, device="cuda")
+            self.sbytes = lib.rns8_cuda_gemm_rns_scratch_bytes(dev, r, n, k, P)
+        self.scratch = torch.empty(max(1, self.sbytes), dtype=torch.uint8, device="cuda")
+
+    def step(self):
+        cfg, lib, d, s = self.cfg, self.lib, self.dev, self.sptr
+        m, n, k, P = cfg.m, cfg.n, cfg.k, cfg.prefix
+        chk = DevicePipeline._check
+        launches = 0
+        if self.mode == "planes":
+            b = self.step_index % 2
+            self.step_index += 1
+            if self.mine:
+                pk = lib.rns8_cuda_pack_i64_planes_device if self.signed else lib.rns8_cuda_pack_u64_planes_device
+                chk(pk(d, self.A.data_ptr(), m, k, k, self.idx, len(self.mine), self.ra.data_ptr(), s), "pack A")
+                chk(pk(d, self.B.data_ptr(), k, n, n, self.idx, len(self.mine), self.rb.data_ptr(), s), "pack B")
+                chk(lib.rns8_cuda_gemm_rns_slabs_device(d, self.ra.data_ptr(), self.rb.data_ptr(), m, n, k, self.idx,
+                                                        len(self.mine), self.tables[b], self.ex.slab_count,
+                                                        self.ex.slab_rows, 1 if self.copy else 0,
+                                                        self.scratch.data_ptr(), self.sbytes, self.status.data_ptr(),
+                                                        C.byref(self.fused), s), "gemm slabs")
+                launches += 3
+            if self.world > 1:
+                self.dist.all_reduce(self.flag)  # every rank's scatter into this rank's buffer has completed
+            planes = self.ex.receive_buffer(b)
+        else:
+            if self.rows:
+                pk = lib.rns8_cuda_pack_i64_device if self.signed else lib.rns8_cuda_pack_u64_device
+                chk(pk(d, self.A.data_ptr() + self.row0 * k * 8, self.rows, k, k, P, self.ra.data_ptr(), s), "pack A")
+                chk(pk(d, self.B.data_ptr(), k, n, n, P, self.rb.data_ptr(), s), "pack B")
+                chk(lib.rns8_cuda_gemm_rns_device(d, self.ra.data_ptr(), self.rb.data_ptr(), self.rc.data_ptr(),
+                                                  self.rows, n, k, P, 0, self.scratch.data_ptr(), self.sbytes,
+                                                  self.status.data_ptr(), s), "gemm")
+                launches += 3
+            planes = self.rc.data_ptr()
+        if self.rows:
+            if cfg.kind == "exact":
+                st = lib.rns8_cuda_export_limbs_device(d, planes, self.rows, n, P, 1, cfg.limbs, self.out.data_ptr(),
+                                                       n, self.status.data_ptr(), s)
+            else:
+                fn = lib.rns8_cuda_export_i64_device if self.signed else lib.rns8_cuda_export_u64_device
+                st = fn(d, planes, self.rows, n, P, cfg.bound, self.out.data_ptr(), n, self.status.data_ptr(), s)
+            chk(st, "export")
+            launches += 1
+        self.launches_per_step = launches
+
+    def check_against_rows(self):
+        """This rank's slab against the unsharded pipeline on this GPU."""
+        cfg = self.cfg
+        if not self.rows:
+            return True
+        sub = dataclasses.replace(cfg, m=self.rows)
+        pipe = DevicePipeline(self.torch, self.lib, sub, self.dev, 0, self.sptr)
+        pipe.A.copy_(self.A[self.row0:self.row0 + self.rows])
+        pipe.B.copy_(self.B)
+        pipe.step()
+        self.torch.cuda.synchronize()
+        return bool(self.torch.equal(pipe.out, self.out[: self.rows])) and pipe.device_status() == 0
+
+    def close(self):
+        if self.ex is not None:
+            self.ex.close()
+
+
+def run_sharded(args, cfg: Config) -> None:
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    import rns8_b200 as r8
+
+    lib = r8.lib()
+    stream = torch.cuda.current_stream()
+    sptr = C.c_void_p(stream.cuda_stream)
+    job = ShardedProduct(torch, dist, lib, cfg, local, rank, world, args.shard, args.exchange, sptr)
+    for _ in range(max(3, args.warmup)):
+        job.step()
+    torch.cuda.synchronize()
+    ok = job.check_against_rows()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        job.step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    status = int(job.status[0].item())
+    t = torch.tensor([start.elapsed_time(stop), 0.0 if (ok and status == 0) else 1.0], dtype=torch.float64,
+                     device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if float(t[1].item()) != 0.0:
+        raise RuntimeError("sharded result differs from the unsharded pipeline (or a device status was set)")
+    ms_per_step = float(t[0].item()) / args.steps
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": cfg.ops / (ms_per_step * 1e-3) / 1e9, "unit": "GOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic",
+            "config": {"workload": cfg.workload, "name": cfg.name, "m": cfg.m, "n": cfg.n, "k": cfg.k,
+                       "prefix": cfg.prefix, "parallelism": f"{args.shard} x{world}",
+                       "exchange": (("fused epilogue scatter" if job.fused.value else "local planes + copies")
+                                    if args.shard == "planes" else "none"),
+                       "l2": "inputs larger than L2"},
+            "e2e": None, "note": "strong-scaling variant (device-resident); the benchmark line is --shard weak-rows",
+            "checked": "every rank's slab equals the unsharded pipeline's", "clocks": clock_info,
+            "gpu_launches": job.launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    job.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args, cfg = parse()
     if args.impl == "reference":
         reference_arm(args, cfg)
+        return
+    if args.shard != "weak-rows":
+        run_sharded(args, cfg)
         return
     import torch
     import torch.distributed as dist

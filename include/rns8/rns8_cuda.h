@@ -173,6 +173,55 @@ RNS8_API rns8_status rns8_cuda_plan_tile_schedule_probe(const rns8_gemm_desc* de
                                                         rns8_plan_tile_schedule_entry* entries, uint64_t capacity,
                                                         uint64_t* written, rns8_plan_schedule_info* info);
 
+/* ---- Plane sharding across GPUs (no counterpart in the reference, which runs
+ * on one device; its research spec describes splitting by modulus). Every GPU
+ * packs and multiplies a subset of the residue planes for all of C, and every
+ * GPU then needs all planes of its own row slab of C to reconstruct it. The
+ * exchange is a row-slab scatter: the plane GEMM's epilogue stores each output
+ * row straight into the slab owner's buffer, over NVLink when the owner is a
+ * peer GPU whose buffer is mapped into this process (rns8_cuda_ipc_*). */
+
+/* Pack only the planes plane_index[0..plane_count) (ladder indices < 20):
+ * plane j of d_planes holds the centered residues modulo ladder entry
+ * plane_index[j], compact (rows x cols). */
+RNS8_API rns8_status rns8_cuda_pack_i64_planes_device(int device_id, const int64_t* d_src, int64_t rows, int64_t cols,
+                                                      int64_t ld, const uint32_t* plane_index, uint32_t plane_count,
+                                                      int8_t* d_planes, void* stream);
+RNS8_API rns8_status rns8_cuda_pack_u64_planes_device(int device_id, const uint64_t* d_src, int64_t rows,
+                                                      int64_t cols, int64_t ld, const uint32_t* plane_index,
+                                                      uint32_t plane_count, int8_t* d_planes, void* stream);
+
+#define RNS8_CUDA_EXCHANGE_FUSED 0u /* epilogue stores into the slab buffers (copy form when it cannot) */
+#define RNS8_CUDA_EXCHANGE_COPY 1u  /* local planes in scratch, then one device copy per (plane, slab) */
+
+/* Scratch for rns8_cuda_gemm_rns_slabs_device (0 when the fused form runs). */
+RNS8_API uint64_t rns8_cuda_gemm_rns_slabs_scratch_bytes(int device_id, int64_t m, int64_t n, int64_t k,
+                                                         uint32_t plane_count, uint32_t exchange);
+/* Per local plane j: C_j = (A_j x B_j) mod ladder[plane_index[j]], A (m x k)
+ * and B (k x n) compact planes as packed above. Output rows are split into
+ * slab_count (<= 8) slabs of slab_rows rows (the last may be shorter, none
+ * empty); slab s's rows go to slab_dst[s] (a host array of device pointers,
+ * this GPU's or a mapped peer's), which holds planes at stride rows_s * n:
+ * local plane j lands in plane slot plane_index[j], row r at (r - s *
+ * slab_rows) * n. The call only enqueues; the caller orders it against the
+ * slab owners' readers (a barrier across GPUs before the owners export).
+ * *out_fused (may be NULL) tells whether the fused form ran. */
+RNS8_API rns8_status rns8_cuda_gemm_rns_slabs_device(int device_id, const int8_t* d_a, const int8_t* d_b, int64_t m,
+                                                     int64_t n, int64_t k, const uint32_t* plane_index,
+                                                     uint32_t plane_count, int8_t* const* slab_dst,
+                                                     uint32_t slab_count, int64_t slab_rows, uint32_t exchange,
+                                                     void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
+                                                     uint32_t* out_fused, void* stream);
+
+/* Device buffers shared between processes (one process per GPU): allocate a
+ * buffer and its 64-byte IPC handle, open a peer's handle in this process
+ * (peer access enabled), close an opened mapping, free an allocation. */
+#define RNS8_CUDA_IPC_HANDLE_BYTES 64
+RNS8_API rns8_status rns8_cuda_ipc_alloc(int device_id, uint64_t bytes, void** d_ptr, uint8_t* handle);
+RNS8_API rns8_status rns8_cuda_ipc_free(int device_id, void* d_ptr);
+RNS8_API rns8_status rns8_cuda_ipc_open(int device_id, const uint8_t* handle, void** d_ptr);
+RNS8_API rns8_status rns8_cuda_ipc_close(int device_id, void* d_ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -260,6 +260,15 @@ SIGNATURES = {
     "rns8_cuda_pack_wrap_u64_device": (c_status, [C.c_int, vp, i64, i64, i64, vp, vp]),
     "rns8_cuda_gemm_wrap_u64_device": (c_status, [C.c_int, vp, vp, vp, i64, i64, i64, u32, vp, vp]),
     "rns8_cuda_export_wrap_u64_device": (c_status, [C.c_int, vp, i64, i64, vp, i64, vp]),
+    "rns8_cuda_pack_i64_planes_device": (c_status, [C.c_int, vp, i64, i64, i64, vp, u32, vp, vp]),
+    "rns8_cuda_pack_u64_planes_device": (c_status, [C.c_int, vp, i64, i64, i64, vp, u32, vp, vp]),
+    "rns8_cuda_gemm_rns_slabs_scratch_bytes": (u64, [C.c_int, i64, i64, i64, u32, u32]),
+    "rns8_cuda_gemm_rns_slabs_device": (c_status, [C.c_int, vp, vp, i64, i64, i64, vp, u32, vp, u32, i64, u32, vp,
+                                                   u64, vp, vp, vp]),
+    "rns8_cuda_ipc_alloc": (c_status, [C.c_int, u64, P(vp), vp]),
+    "rns8_cuda_ipc_free": (c_status, [C.c_int, vp]),
+    "rns8_cuda_ipc_open": (c_status, [C.c_int, vp, P(vp)]),
+    "rns8_cuda_ipc_close": (c_status, [C.c_int, vp]),
 }
 
 _LIB: C.CDLL | None = None

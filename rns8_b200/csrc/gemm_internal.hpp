@@ -41,8 +41,11 @@ struct ZeroTile {
   int64_t row0, col0, rows, cols;
   uint32_t planes, pad;
 };
+// With `scatter`, C's rows go to the slab destinations instead of tasks[0].c
+// (one task, no split-K).
 cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
-                          uint32_t* dev_status, cudaStream_t stream, const TcScheduleUnits* sched = nullptr);
+                          uint32_t* dev_status, cudaStream_t stream, const TcScheduleUnits* sched = nullptr,
+                          const SlabScatter* scatter = nullptr);
 
 // wrap64 on the tensor cores: c (m x n uint64, row-major) = A x B mod 2^64 from
 // 8 byte planes each (k % 16 == 0, n % 16 == 0, 16-byte aligned planes).

@@ -65,6 +65,15 @@ struct __align__(64) TcParams {
   const uint64_t* unit_list;
   const uint8_t* tile_sel;
   uint32_t sched_shift_m, sched_shift_n, sched_cols;
+  // Row-slab exchange (slab_count > 0, one task, no split-K): output row r
+  // belongs to slab s = r / slab_rows and its plane p is stored at
+  // slab_dst[s] + dst_plane[p] * slab_stride[s] + (r - s * slab_rows) * n,
+  // in this GPU's memory or a peer's over NVLink.
+  int8_t* slab_dst[kMaxSlabs];
+  int64_t slab_stride[kMaxSlabs];
+  int64_t slab_rows;
+  uint32_t slab_count;
+  uint8_t dst_plane[20];
 };
 
 struct Unit {
@@ -247,7 +256,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
       const int64_t row = static_cast<int64_t>(w.mt) * BM + quarter * 32 + lane;
       const bool row_ok = row < prm.m;
       const int64_t plane_elems = prm.m * prm.n;
-      int8_t* crow = prm.C[w.t] + static_cast<int64_t>(w.p) * plane_elems + row * prm.n;
+      int8_t* crow;
+      if (prm.slab_count) {
+        const int64_t s = row_ok ? row / prm.slab_rows : 0;
+        crow = prm.slab_dst[s] + prm.dst_plane[w.p] * prm.slab_stride[s] + (row - s * prm.slab_rows) * prm.n;
+      } else {
+        crow = prm.C[w.t] + static_cast<int64_t>(w.p) * plane_elems + row * prm.n;
+      }
       int32_t* srow = prm.scratch
                           ? prm.scratch + (static_cast<int64_t>(w.t) * prm.planes + w.p) * plane_elems + row * prm.n
                           : nullptr;
@@ -289,6 +304,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
         acc_phase ^= 1u;
       }
     }
+    // Slab stores may target a peer GPU: make them visible system-wide before
+    // this kernel counts as complete to the host-side exchange barrier.
+    if (prm.slab_count) __threadfence_system();
   }
 
   __syncthreads();
@@ -613,7 +631,8 @@ TcSchedule tc_schedule(const PlaneGemmProblem& prob, int sm_count) {
 }
 
 cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
-                          uint32_t* dev_status, cudaStream_t stream, const TcScheduleUnits* sched) {
+                          uint32_t* dev_status, cudaStream_t stream, const TcScheduleUnits* sched,
+                          const SlabScatter* scatter) {
   if (prob.task_count == 0 || prob.task_count > kMaxGroupTasks || prob.planes == 0 || prob.planes > 20)
     return cudaErrorInvalidValue;
   static std::once_flag attr_once;
@@ -629,6 +648,9 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
   const uint64_t plane_elems = static_cast<uint64_t>(prob.m) * prob.n;
   const uint64_t need = split ? plane_elems * prob.planes * prob.task_count * sizeof(int32_t) : 0;
   if (split && (scratch == nullptr || scratch_bytes < need)) return cudaErrorInvalidValue;
+  if (scatter && (split || sched || prob.task_count != 1 || scatter->slab_count == 0 ||
+                  scatter->slab_count > static_cast<uint32_t>(kMaxSlabs) || scatter->slab_rows <= 0))
+    return cudaErrorInvalidValue;
 
   static thread_local TcParams prm;  // 8+ KiB: keep it off the stack
   std::memset(&prm, 0, sizeof(prm));
@@ -662,6 +684,21 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
     prm.sched_cols = sched->cols;
   }
 
+  if (scatter) {
+    prm.slab_rows = scatter->slab_rows;
+    prm.slab_count = scatter->slab_count;
+    for (uint32_t sl = 0; sl < scatter->slab_count; ++sl) {
+      const int64_t rows = std::min<int64_t>(scatter->slab_rows, prob.m - static_cast<int64_t>(sl) * scatter->slab_rows);
+      if (rows <= 0 || scatter->slab_dst[sl] == nullptr || reinterpret_cast<uintptr_t>(scatter->slab_dst[sl]) % 16)
+        return cudaErrorInvalidValue;
+      prm.slab_dst[sl] = scatter->slab_dst[sl];
+      prm.slab_stride[sl] = rows * prob.n;
+    }
+    for (uint32_t p = 0; p < prob.planes; ++p) {
+      if (scatter->dst_plane[p] >= 20) return cudaErrorInvalidValue;
+      prm.dst_plane[p] = static_cast<uint8_t>(scatter->dst_plane[p]);
+    }
+  }
   if (split) {
     const cudaError_t e = cudaMemsetAsync(scratch, 0, need, stream);
     if (e != cudaSuccess) return e;
@@ -773,6 +810,69 @@ cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count
                                                                                    : static_cast<uint32_t>(kMaxGroupTasks);
     const cudaError_t e = tc_plane_gemm(chunk, sm_count, scratch, scratch_bytes, dev_status, stream);
     if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// ---- row-slab exchange (plane sharding) ------------------------------------------
+bool plane_gemm_scatter_fusable(const PlaneGemmProblem& prob, int sm_count) {
+  if (prob.task_count != 1 || !tensor_core_path_supported(prob)) return false;
+  return tc_schedule(prob, sm_count).splits <= 1;
+}
+
+namespace {
+uint64_t local_planes_bytes(const PlaneGemmProblem& prob) {
+  return (static_cast<uint64_t>(prob.m) * prob.n * prob.planes + 255) / 256 * 256;
+}
+}  // namespace
+
+uint64_t plane_gemm_scatter_scratch_bytes(const PlaneGemmProblem& prob, int sm_count, bool copy_exchange) {
+  if (!copy_exchange && plane_gemm_scatter_fusable(prob, sm_count)) return 0;
+  return local_planes_bytes(prob) + plane_gemm_scratch_bytes(prob, sm_count);
+}
+
+cudaError_t plane_gemm_scatter(const PlaneGemmProblem& prob, const SlabScatter& sc, bool copy_exchange,
+                               int sm_count, void* scratch, uint64_t scratch_bytes, uint32_t* dev_status,
+                               cudaStream_t stream, bool* fused_used) {
+  if (prob.task_count != 1 || prob.planes == 0 || prob.planes > 20 || !sc.slab_dst || !sc.dst_plane ||
+      sc.slab_count == 0 || sc.slab_count > static_cast<uint32_t>(kMaxSlabs) || sc.slab_rows <= 0)
+    return cudaErrorInvalidValue;
+  // Every slab holds at least one row and together they cover exactly m rows.
+  if (static_cast<int64_t>(sc.slab_count - 1) * sc.slab_rows >= prob.m ||
+      static_cast<int64_t>(sc.slab_count) * sc.slab_rows < prob.m)
+    return cudaErrorInvalidValue;
+  for (uint32_t sl = 0; sl < sc.slab_count; ++sl)
+    if (sc.slab_dst[sl] == nullptr) return cudaErrorInvalidValue;
+  for (uint32_t p = 0; p < prob.planes; ++p)
+    if (sc.dst_plane[p] >= 20) return cudaErrorInvalidValue;
+  PlaneGemmTask task = prob.tasks[0];
+  task.c = sc.slab_dst[0];  // stands in for C in the alignment check of the fused form
+  PlaneGemmProblem one = prob;
+  one.tasks = &task;
+  bool aligned = true;
+  for (uint32_t sl = 0; sl < sc.slab_count; ++sl) aligned &= reinterpret_cast<uintptr_t>(sc.slab_dst[sl]) % 16 == 0;
+  if (!copy_exchange && aligned && plane_gemm_scatter_fusable(one, sm_count)) {
+    if (fused_used) *fused_used = true;
+    return tc_plane_gemm(one, sm_count, nullptr, 0, dev_status, stream, nullptr, &sc);
+  }
+  if (fused_used) *fused_used = false;
+  const uint64_t local = local_planes_bytes(prob);
+  if (!scratch || scratch_bytes < local) return cudaErrorInvalidValue;
+  task.c = static_cast<int8_t*>(scratch);
+  cudaError_t e = plane_gemm(one, GemmPath::Auto, sm_count, static_cast<uint8_t*>(scratch) + local,
+                             scratch_bytes - local, dev_status, stream);
+  if (e != cudaSuccess) return e;
+  const uint64_t plane_elems = static_cast<uint64_t>(prob.m) * prob.n;
+  for (uint32_t p = 0; p < prob.planes; ++p) {
+    for (uint32_t sl = 0; sl < sc.slab_count; ++sl) {
+      const int64_t row0 = static_cast<int64_t>(sl) * sc.slab_rows;
+      const int64_t rows = std::min<int64_t>(sc.slab_rows, prob.m - row0);
+      const uint64_t bytes = static_cast<uint64_t>(rows) * prob.n;
+      e = cudaMemcpyAsync(sc.slab_dst[sl] + static_cast<uint64_t>(sc.dst_plane[p]) * bytes,
+                          task.c + p * plane_elems + static_cast<uint64_t>(row0) * prob.n, bytes, cudaMemcpyDefault,
+                          stream);
+      if (e != cudaSuccess) return e;
+    }
   }
   return cudaSuccess;
 }

@@ -26,6 +26,14 @@ cudaError_t pack_u64(const uint64_t* src, int64_t rows, int64_t cols, int64_t ld
 cudaError_t pack_finite_u8(const uint8_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t modulus,
                            int8_t* residues, cudaStream_t stream);
 
+// Pack of selected planes only: plane j of `planes` holds the residues modulo
+// ladder entry plane_index[j] (host array, plane_count entries, each < 20).
+// A GPU that computes a subset of the planes (plane sharding) packs just those.
+cudaError_t pack_planes_i64(const int64_t* src, int64_t rows, int64_t cols, int64_t ld, const uint32_t* plane_index,
+                            uint32_t plane_count, int8_t* planes, cudaStream_t stream);
+cudaError_t pack_planes_u64(const uint64_t* src, int64_t rows, int64_t cols, int64_t ld, const uint32_t* plane_index,
+                            uint32_t plane_count, int8_t* planes, cudaStream_t stream);
+
 // ---- plane GEMM -------------------------------------------------------------
 // One GEMM family: tasks[t] x planes[p]; every plane of every task has the
 // same shape. Plane p reduces modulo moduli[p].
@@ -81,6 +89,30 @@ uint64_t gemm_export_bounded_scratch_bytes(const PlaneGemmProblem& prob, int sm_
 cudaError_t gemm_export_bounded(const PlaneGemmProblem& prob, bool is_signed, uint64_t bound, void* out, int64_t ld,
                                 int sm_count, void* scratch, uint64_t scratch_bytes, uint32_t* dev_status,
                                 cudaStream_t stream);
+
+// Plane GEMM whose output rows are split into row slabs, each slab going to
+// its own destination (this GPU's memory or a peer GPU's, mapped into this
+// process): the plane-sharded exchange, where every GPU computes some planes
+// of all of C and every GPU then needs all planes of its own row slab.
+// Slab s covers rows [s * slab_rows, min(m, (s + 1) * slab_rows)); its
+// destination holds planes at stride rows_s * n, and local plane p lands in
+// plane slot dst_plane[p]. Fused: the GEMM epilogue stores straight into the
+// destinations (peer stores over NVLink, ordered by a system fence before the
+// kernel completes). Copy: the GEMM writes local planes into scratch and one
+// device-to-device copy per (plane, slab) moves them. The fused form needs the
+// tensor-core path without split-K; otherwise the copy form runs.
+constexpr int kMaxSlabs = 8;
+struct SlabScatter {
+  int8_t* const* slab_dst;    // host array of slab_count device pointers
+  int64_t slab_rows;
+  uint32_t slab_count;
+  const uint32_t* dst_plane;  // host array, one plane slot per local plane
+};
+bool plane_gemm_scatter_fusable(const PlaneGemmProblem& prob, int sm_count);
+uint64_t plane_gemm_scatter_scratch_bytes(const PlaneGemmProblem& prob, int sm_count, bool copy_exchange);
+cudaError_t plane_gemm_scatter(const PlaneGemmProblem& prob, const SlabScatter& scatter, bool copy_exchange,
+                               int sm_count, void* scratch, uint64_t scratch_bytes, uint32_t* dev_status,
+                               cudaStream_t stream, bool* fused_used = nullptr);
 
 // ---- export (residue planes -> native values) ------------------------------
 // Bounded i64: every cell must reconstruct to a value v with |v| <= bound;

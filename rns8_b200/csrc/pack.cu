@@ -157,6 +157,137 @@ cudaError_t dispatch_pack(const T* src, int64_t rows, int64_t cols, int64_t ld, 
   }
 }
 
+// ---- selected planes (plane sharding) -------------------------------------------
+// The same arithmetic as residue_byte with the per-plane constants read from
+// the kernel parameters instead of immediates; modulus 256 needs no special
+// case (weights 1,0,...; start 0; magic 2^24 gives q = (b0 + 128) >> 8).
+constexpr int kSubsetMax = 10;  // planes per launch; larger subsets take two launches
+
+struct SubsetConsts {
+  uint32_t wl[kSubsetMax], wh[kSubsetMax], start[kSubsetMax], magic[kSubsetMax], m[kSubsetMax];
+  uint64_t hmagic[kSubsetMax];  // floor(m / 2) * magic
+};
+
+template <bool kSigned>
+SubsetConsts subset_consts(const uint32_t* plane_index, uint32_t count) {
+  SubsetConsts c{};
+  for (uint32_t j = 0; j < count; ++j) {
+    const uint32_t m = ladder_modulus(static_cast<int>(plane_index[j]));
+    uint64_t pow = 1, pow56 = 1;
+    for (int b = 0; b < 8; ++b) {
+      if (b < 4)
+        c.wl[j] |= static_cast<uint32_t>(pow) << (8 * b);
+      else
+        c.wh[j] |= static_cast<uint32_t>(pow) << (8 * (b - 4));
+      if (b == 7) pow56 = pow;
+      pow = (pow * 256) % m;
+    }
+    const uint32_t pow63 = static_cast<uint32_t>((pow56 * 128) % m);
+    c.start[j] = kSigned ? (m - pow63) % m : 0u;
+    c.magic[j] = static_cast<uint32_t>(((1ull << 32) + m - 1) / m);
+    c.m[j] = m;
+    c.hmagic[j] = static_cast<uint64_t>(m / 2) * c.magic[j];
+  }
+  return c;
+}
+
+__device__ __forceinline__ uint32_t residue_byte_rt(const Words& w, const SubsetConsts& c, int j) {
+  uint32_t t = __dp4a(w.hi, c.wh[j], c.start[j]);
+  t = __dp4a(w.lo, c.wl[j], t);
+  const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(t) * c.magic[j] + c.hmagic[j]) >> 32);
+  return t - q * c.m[j];
+}
+
+template <int NP, typename T>
+__global__ void __launch_bounds__(256) pack_subset_vec8_kernel(const T* __restrict__ src, int64_t rows, int64_t cols,
+                                                                int64_t ld, int8_t* __restrict__ planes,
+                                                                const __grid_constant__ SubsetConsts c) {
+  const int64_t groups_per_row = cols >> 3;
+  const int64_t total = rows * groups_per_row;
+  const int64_t plane_elems = rows * cols;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = g / groups_per_row;
+    const int64_t col = (g - row * groups_per_row) << 3;
+    const int4* in = reinterpret_cast<const int4*>(src + row * ld + col);
+    Words d[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int4 v = __ldcs(in + q);
+      d[2 * q] = split_words<T>(static_cast<T>((static_cast<uint64_t>(static_cast<uint32_t>(v.y)) << 32) |
+                                               static_cast<uint32_t>(v.x)));
+      d[2 * q + 1] = split_words<T>(static_cast<T>((static_cast<uint64_t>(static_cast<uint32_t>(v.w)) << 32) |
+                                                   static_cast<uint32_t>(v.z)));
+    }
+    int8_t* out = planes + row * cols + col;
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      uint2 w;
+      w.x = pack4(residue_byte_rt(d[0], c, j), residue_byte_rt(d[1], c, j), residue_byte_rt(d[2], c, j),
+                  residue_byte_rt(d[3], c, j));
+      w.y = pack4(residue_byte_rt(d[4], c, j), residue_byte_rt(d[5], c, j), residue_byte_rt(d[6], c, j),
+                  residue_byte_rt(d[7], c, j));
+      __stcs(reinterpret_cast<uint2*>(out + static_cast<int64_t>(j) * plane_elems), w);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) pack_subset_scalar_kernel(const T* __restrict__ src, int64_t rows,
+                                                                  int64_t cols, int64_t ld, uint32_t count,
+                                                                  int8_t* __restrict__ planes,
+                                                                  const __grid_constant__ SubsetConsts c) {
+  const int64_t total = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / cols, col = i - row * cols;
+    const Words d = split_words<T>(src[row * ld + col]);
+    for (uint32_t j = 0; j < count; ++j)
+      planes[static_cast<int64_t>(j) * total + i] = static_cast<int8_t>(residue_byte_rt(d, c, static_cast<int>(j)) & 0xFFu);
+  }
+}
+
+template <typename T>
+cudaError_t launch_subset(const T* src, int64_t rows, int64_t cols, int64_t ld, const uint32_t* plane_index,
+                          uint32_t count, int8_t* planes, cudaStream_t stream) {
+  constexpr bool kSigned = static_cast<T>(-1) < 0;
+  const SubsetConsts c = subset_consts<kSigned>(plane_index, count);
+  const bool vec = (cols % 8 == 0) && (ld % 2 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(planes) % 8 == 0);
+  const int64_t work = vec ? rows * (cols / 8) : rows * cols;
+  int64_t blocks = (work + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  const unsigned grid = static_cast<unsigned>(blocks);
+  if (!vec) {
+    pack_subset_scalar_kernel<T><<<grid, 256, 0, stream>>>(src, rows, cols, ld, count, planes, c);
+    return cudaGetLastError();
+  }
+  switch (count) {
+#define RNS8_SUBSET_CASE(NP)   case NP: pack_subset_vec8_kernel<NP, T><<<grid, 256, 0, stream>>>(src, rows, cols, ld, planes, c); break;
+    RNS8_SUBSET_CASE(1) RNS8_SUBSET_CASE(2) RNS8_SUBSET_CASE(3) RNS8_SUBSET_CASE(4) RNS8_SUBSET_CASE(5)
+    RNS8_SUBSET_CASE(6) RNS8_SUBSET_CASE(7) RNS8_SUBSET_CASE(8) RNS8_SUBSET_CASE(9) RNS8_SUBSET_CASE(10)
+#undef RNS8_SUBSET_CASE
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch_subset(const T* src, int64_t rows, int64_t cols, int64_t ld, const uint32_t* plane_index,
+                            uint32_t count, int8_t* planes, cudaStream_t stream) {
+  if (!plane_index || count == 0 || count > 20) return cudaErrorInvalidValue;
+  for (uint32_t j = 0; j < count; ++j)
+    if (plane_index[j] >= 20) return cudaErrorInvalidValue;
+  const int64_t plane_elems = rows * cols;
+  for (uint32_t j0 = 0; j0 < count; j0 += kSubsetMax) {
+    const uint32_t n = count - j0 < static_cast<uint32_t>(kSubsetMax) ? count - j0 : static_cast<uint32_t>(kSubsetMax);
+    const cudaError_t e = launch_subset<T>(src, rows, cols, ld, plane_index + j0, n, planes + j0 * plane_elems, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 // Finite u8: residues of bytes modulo an arbitrary m in [2, 256].
 enum class U8Kind : int {
   General = 0,   // m < 128: magic-multiply modulo per byte
@@ -224,6 +355,14 @@ cudaError_t pack_i64(const int64_t* src, int64_t rows, int64_t cols, int64_t ld,
 cudaError_t pack_u64(const uint64_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t prefix, int8_t* planes,
                      cudaStream_t stream) {
   return dispatch_pack<uint64_t>(src, rows, cols, ld, prefix, planes, stream);
+}
+cudaError_t pack_planes_i64(const int64_t* src, int64_t rows, int64_t cols, int64_t ld, const uint32_t* plane_index,
+                            uint32_t plane_count, int8_t* planes, cudaStream_t stream) {
+  return dispatch_subset<int64_t>(src, rows, cols, ld, plane_index, plane_count, planes, stream);
+}
+cudaError_t pack_planes_u64(const uint64_t* src, int64_t rows, int64_t cols, int64_t ld, const uint32_t* plane_index,
+                            uint32_t plane_count, int8_t* planes, cudaStream_t stream) {
+  return dispatch_subset<uint64_t>(src, rows, cols, ld, plane_index, plane_count, planes, stream);
 }
 cudaError_t pack_finite_u8(const uint8_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t modulus,
                            int8_t* residues, cudaStream_t stream) {
