@@ -222,6 +222,16 @@ RNS8_API rns8_status rns8_cuda_ipc_free(int device_id, void* d_ptr);
 RNS8_API rns8_status rns8_cuda_ipc_open(int device_id, const uint8_t* handle, void** d_ptr);
 RNS8_API rns8_status rns8_cuda_ipc_close(int device_id, void* d_ptr);
 
+/* Failure detection without a fault: launches one CTA that waits on an
+ * mbarrier with the bounded wait the GEMM kernels use. arrive = 1: a thread
+ * arrives first and the call returns RNS8_SUCCESS. arrive = 0: nothing arrives,
+ * the wait gives up after budget_cycles SM cycles (1 .. 4e9), the kernel sets
+ * the timeout bit in *d_status and the call returns RNS8_BACKEND_FAILURE, as
+ * any call whose kernel wait ran out does; the context stays usable.
+ * Synchronises `stream`. */
+RNS8_API rns8_status rns8_cuda_wait_probe(int device_id, uint32_t arrive, uint64_t budget_cycles,
+                                          uint32_t* d_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

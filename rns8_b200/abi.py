@@ -269,6 +269,7 @@ SIGNATURES = {
     "rns8_cuda_ipc_free": (c_status, [C.c_int, vp]),
     "rns8_cuda_ipc_open": (c_status, [C.c_int, vp, P(vp)]),
     "rns8_cuda_ipc_close": (c_status, [C.c_int, vp]),
+    "rns8_cuda_wait_probe": (c_status, [C.c_int, u32, u64, vp, vp]),
 }
 
 _LIB: C.CDLL | None = None

@@ -92,15 +92,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // Wait until the barrier phase with the given parity completes, for at most
 // `budget` SM cycles. Returns false when the budget ran out.
 constexpr long long kWaitBudgetCycles = 4000000000ll;  // about two seconds
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, long long budget) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const long long start = clock64();
   while (true) {
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(addr, parity)) return true;
-    if (clock64() - start > kWaitBudgetCycles) return false;
+    if (clock64() - start > budget) return false;
   }
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_bounded(bar, parity, kWaitBudgetCycles);
 }
 
 // 3-D tiled TMA load global -> shared, completion signalled on an mbarrier.
