@@ -7,14 +7,13 @@
 //   u = sum_j b_j * 2^(8j)  =  sum_j b_j * w_j  (mod m),  w_j = 2^(8j) mod m < 256,
 // which is two dp4a instructions. A signed x is packed as u = x + 2^63 (its
 // top bit flipped), and the constant (-2^63) mod m starts the dp4a sum, so
-// both signs take the same path. The sum t is below 2^20, where
-// q = mulhi(t + h, ceil(2^32/m)) is the exact quotient of t + h by m; with
-// h = floor(m/2), t - q*m is the centered residue (in [-h, m - 1 - h]). The
-// +h folds into the 64-bit addend of one wide multiply-add, so a residue
-// costs two dp4a, one wide multiply-add and one multiply-add. Modulus 256 is
-// the low byte itself (two's complement). The byte split is shared by every
-// plane; per-plane constants are immediates because the prefix is a
-// template parameter.
+// both signs take the same path. With h = floor(m/2) added to that start
+// constant the sum s = t + h is below 2^20, where q = mulhi(s, ceil(2^32/m))
+// is the exact quotient of s by m, and s - (q*m + h) is the centered residue
+// (in [-h, m - 1 - h]): two dp4a, one mul-hi, one multiply-add and one add
+// per residue. Modulus 256 is the low byte itself (two's complement). The
+// byte split is shared by every plane; per-plane constants are immediates
+// because the prefix is a template parameter.
 #include "device_common.cuh"
 #include "kernels.hpp"
 
@@ -62,10 +61,10 @@ __device__ __forceinline__ uint32_t residue_byte(const Words& w, int p) {
   const uint32_t pow63 = static_cast<uint32_t>((pow56 * 128) % m);  // 2^63 mod m
   const uint32_t start = kSigned ? (m - pow63) % m : 0u;           // (-2^63) mod m
   const uint32_t magic = static_cast<uint32_t>(((1ull << 32) + m - 1) / m);
-  uint32_t t = __dp4a(w.hi, wh, start);
+  uint32_t t = __dp4a(w.hi, wh, start + h);  // + h: the centering shift rides in the start constant
   t = __dp4a(w.lo, wl, t);
-  const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(t) * magic + static_cast<uint64_t>(h) * magic) >> 32);
-  return t - q * m;  // low byte = centered residue
+  const uint32_t q = __umulhi(t, magic);
+  return t - (q * m + h);  // low byte = centered residue
 }
 
 // Bytes 0 of a, b, c, d -> one word.
