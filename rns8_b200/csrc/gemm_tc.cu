@@ -617,12 +617,24 @@ TcSchedule tc_schedule(const PlaneGemmProblem& prob, int sm_count) {
   const uint64_t tiles = static_cast<uint64_t>(prob.task_count) * prob.planes * s.m_tiles * s.n_tiles;
   uint32_t splits = (s.total_kb + kMaxKbPerUnit - 1) / kMaxKbPerUnit;
   if (tiles * splits < static_cast<uint64_t>(sm_count) && s.total_kb >= 8) {
-    // Too few output tiles to occupy every SM: split K until about one wave,
-    // keeping at least four K blocks per unit.
-    const uint64_t want = (static_cast<uint64_t>(sm_count) + tiles - 1) / tiles;
-    const uint32_t cap = s.total_kb / 4;
-    uint32_t target = static_cast<uint32_t>(want < cap ? want : cap);
-    if (target > splits) splits = target;
+    // Too few output tiles to occupy every SM: split K. The kernel's time is
+    // about (waves of units) x (K blocks per unit + ~2 for the unit's fill and
+    // epilogue); take the smallest split count that minimises it, keeping at
+    // least four K blocks per unit. (Rounding the unit count up to just past
+    // one wave would leave most SMs idle in a second wave.)
+    const uint32_t cap = std::max(splits, s.total_kb / 4);
+    const uint32_t limit = std::min<uint64_t>(cap, 4 * (static_cast<uint64_t>(sm_count) / tiles + 1));
+    uint64_t best_cost = ~0ull;
+    uint32_t best = splits;
+    for (uint32_t c = splits; c <= limit; ++c) {
+      const uint64_t waves = (tiles * c + sm_count - 1) / static_cast<uint64_t>(sm_count);
+      const uint64_t cost = waves * ((s.total_kb + c - 1) / c + 2);
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = c;
+      }
+    }
+    splits = best;
   }
   s.kb_per_split = (s.total_kb + splits - 1) / splits;
   s.splits = (s.total_kb + s.kb_per_split - 1) / s.kb_per_split;
