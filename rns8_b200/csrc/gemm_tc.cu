@@ -47,6 +47,22 @@ constexpr int THREADS = 192;
 constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
 constexpr int kMaxKbPerUnit = static_cast<int>(kSafeKBlock / BK);  // 512
 
+// Division of a 32-bit n by a fixed d as a multiply-high and a shift
+// (Granlund-Montgomery, round-up multiplier; the 33-bit sum in 64 bits), so
+// that decoding a work unit costs a few dozen cycles instead of a chain of
+// division subroutines.
+struct FastDiv {
+  uint32_t d, mul, shift;
+};
+inline FastDiv make_fast_div(uint32_t d) {
+  uint32_t l = 0;
+  while (l < 32 && (1ull << l) < d) ++l;
+  return FastDiv{d, static_cast<uint32_t>(((1ull << 32) * ((1ull << l) - d)) / d + 1), l};
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, f.mul)) + n) >> f.shift);
+}
+
 struct __align__(64) TcParams {
   CUtensorMap tmA[kMaxGroupTasks];
   CUtensorMap tmB[kMaxGroupTasks];
@@ -74,13 +90,17 @@ struct __align__(64) TcParams {
   int64_t slab_rows;
   uint32_t slab_count;
   uint8_t dst_plane[20];
+  FastDiv div_tiles, div_splits, div_planes, div_span;  // m_tiles*n_tiles, splits, planes, GROUP_M*n_tiles
 };
 
 struct Unit {
   uint32_t t, p, mt, nt, kb0, kb1;
 };
 
-__device__ __forceinline__ Unit decode_unit(const TcParams& prm, uint64_t u) {
+// 32-bit arithmetic with precomputed divisors (the host keeps the unit count
+// below 2^32): the producer and the MMA thread decode every unit at its start,
+// and a chain of division subroutines there would idle the tensor pipe.
+__device__ __forceinline__ Unit decode_unit(const TcParams& prm, uint32_t u) {
   if (prm.unit_list) {
     const uint64_t e = prm.unit_list[u];
     Unit w;
@@ -93,21 +113,24 @@ __device__ __forceinline__ Unit decode_unit(const TcParams& prm, uint64_t u) {
     w.kb1 = min(prm.total_kb, w.kb0 + prm.kb_per_split);
     return w;
   }
-  const uint64_t tiles = static_cast<uint64_t>(prm.m_tiles) * prm.n_tiles;
-  const uint64_t tile = u % tiles;
-  const uint64_t rest = u / tiles;
-  const uint32_t s = static_cast<uint32_t>(rest % prm.splits);
-  const uint32_t tp = static_cast<uint32_t>(rest / prm.splits);
+  const uint32_t rest = fast_div(u, prm.div_tiles);
+  const uint32_t tile = u - rest * prm.div_tiles.d;
+  const uint32_t tp = fast_div(rest, prm.div_splits);
+  const uint32_t s = rest - tp * prm.div_splits.d;
   Unit w;
-  w.t = tp / prm.planes;
+  w.t = fast_div(tp, prm.div_planes);
   w.p = tp - w.t * prm.planes;
-  const uint32_t span = GROUP_M * prm.n_tiles;
-  const uint32_t group = static_cast<uint32_t>(tile / span);
+  const uint32_t group = fast_div(tile, prm.div_span);
   const uint32_t first_m = group * GROUP_M;
-  const uint32_t gsize = min(prm.m_tiles - first_m, static_cast<uint32_t>(GROUP_M));
-  const uint32_t in_group = static_cast<uint32_t>(tile % span);
-  w.mt = first_m + in_group % gsize;
-  w.nt = in_group / gsize;
+  const uint32_t in_group = tile - group * prm.div_span.d;
+  if (prm.m_tiles - first_m >= static_cast<uint32_t>(GROUP_M)) {
+    w.mt = first_m + in_group % GROUP_M;
+    w.nt = in_group / GROUP_M;
+  } else {  // the last, narrower group
+    const uint32_t gsize = prm.m_tiles - first_m;
+    w.mt = first_m + in_group % gsize;
+    w.nt = in_group / gsize;
+  }
   w.kb0 = s * prm.kb_per_split;
   w.kb1 = min(prm.total_kb, w.kb0 + prm.kb_per_split);
   return w;
@@ -165,7 +188,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
       uint32_t pending = 0, pending_parity = 0;
       bool ok = true;
       for (uint64_t u = blockIdx.x; ok && u < prm.units; u += gridDim.x) {
-        const Unit w = decode_unit(prm, u);
+        const Unit w = decode_unit(prm, static_cast<uint32_t>(u));
         for (uint32_t kb = w.kb0; kb < w.kb1; ++kb) {
           if (*abort_flag || !mbar_wait_bounded(&empty[stage], phase ^ 1u)) {
             if (!*abort_flag) report_timeout(prm, abort_flag);
@@ -200,7 +223,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       for (uint64_t u = blockIdx.x; ok && u < prm.units; u += gridDim.x) {
-        const Unit w = decode_unit(prm, u);
+        const Unit w = decode_unit(prm, static_cast<uint32_t>(u));
         if (*abort_flag || !mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u)) {
           if (!*abort_flag) report_timeout(prm, abort_flag);
           break;
@@ -246,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
     const uint32_t quarter = static_cast<uint32_t>(warp & 3);  // TMEM lanes this warp may read
     uint32_t acc = 0, acc_phase = 0;
     for (uint64_t u = blockIdx.x; u < prm.units; u += gridDim.x) {
-      const Unit w = decode_unit(prm, u);
+      const Unit w = decode_unit(prm, static_cast<uint32_t>(u));
       if (*abort_flag || !mbar_wait_bounded(&acc_full[acc], acc_phase)) {
         if (!*abort_flag) report_timeout(prm, abort_flag);
         break;
@@ -656,6 +679,9 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
   if (attr_err != cudaSuccess) return attr_err;
 
   const TcSchedule s = tc_schedule(prob, sm_count);
+  if (s.units >= (1ull << 32) || static_cast<uint64_t>(s.m_tiles) * s.n_tiles >= (1ull << 32) ||
+      (sched && sched->unit_count >= (1ull << 32)))
+    return cudaErrorInvalidValue;  // the kernel decodes units in 32-bit arithmetic
   const bool split = s.splits > 1;
   const uint64_t plane_elems = static_cast<uint64_t>(prob.m) * prob.n;
   const uint64_t need = split ? plane_elems * prob.planes * prob.task_count * sizeof(int32_t) : 0;
@@ -685,6 +711,10 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
   prm.kb_per_split = s.kb_per_split;
   prm.units = s.units;
   prm.status = dev_status;
+  prm.div_tiles = make_fast_div(s.m_tiles * s.n_tiles);
+  prm.div_splits = make_fast_div(s.splits);
+  prm.div_planes = make_fast_div(prob.planes);
+  prm.div_span = make_fast_div(static_cast<uint32_t>(GROUP_M) * s.n_tiles);
   for (uint32_t p = 0; p < prob.planes; ++p) prm.moduli[p] = prob.moduli[p];
   if (sched) {
     if (prob.task_count != 1) return cudaErrorInvalidValue;
