@@ -180,21 +180,64 @@ rns8_status exact_gemm_bound(rns8_context& ctx, int64_t m, int64_t n, int64_t k,
 }
 
 // exact_gemm_range (exact_range.hpp:146-154): the bound must fit the plan's prefix.
+// With `defer`, a GEMM whose cheap bound K * max|A| * max|B| already fits the
+// prefix is admitted at once: the per-cell pass could only lower the bound,
+// and its results (the output's tightened bound and row/column records) are
+// produced on demand by resolve_exact_range, from the inputs kept in *defer.
 rns8_status exact_gemm_range(rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& A, const rns8_matrix& B,
-                             i256& bound, ExactRanges* out_ranges) {
+                             i256& bound, ExactRanges* out_ranges, DeferredExactRange* defer) {
   if (!exact_wide(plan.desc.semantics)) return RNS8_SUCCESS;
   if (A.exact_range_prefix < plan.prefix || B.exact_range_prefix < plan.prefix) return RNS8_RANGE_ERROR;
+  rns8_status st = resolve_exact_range(ctx, A);
+  if (st == RNS8_SUCCESS) st = resolve_exact_range(ctx, B);
+  if (st != RNS8_SUCCESS) return st;
   const int64_t m = plan.desc.m, n = plan.desc.n;
   const bool a_rows = A.exact_axes.rows.size() == static_cast<size_t>(m);
   const bool b_cols = B.exact_axes.cols.size() == static_cast<size_t>(n);
-  const rns8_status st = exact_gemm_bound(ctx, m, n, plan.desc.k, A.exact_max_magnitude,
-                                          a_rows ? &A.exact_axes.rows : nullptr, B.exact_max_magnitude,
-                                          b_cols ? &B.exact_axes.cols : nullptr, bound, out_ranges);
+  if (defer && (a_rows || b_cols)) {
+    const i256 cheap = i256::from_i64(plan.desc.k) * A.exact_max_magnitude * B.exact_max_magnitude;
+    if (exact_range_fits(plan.desc.semantics, cheap, plan.modulus_product)) {
+      bound = cheap;
+      if (out_ranges) {
+        out_ranges->rows.clear();
+        out_ranges->cols.clear();
+      }
+      defer->pending = true;
+      defer->m = m;
+      defer->n = n;
+      defer->k = plan.desc.k;
+      defer->a_max = A.exact_max_magnitude;
+      defer->b_max = B.exact_max_magnitude;
+      defer->a_rows_known = a_rows;
+      defer->b_cols_known = b_cols;
+      defer->a_rows = a_rows ? A.exact_axes.rows : std::vector<AxisRange>{};
+      defer->b_cols = b_cols ? B.exact_axes.cols : std::vector<AxisRange>{};
+      return RNS8_SUCCESS;
+    }
+  }
+  st = exact_gemm_bound(ctx, m, n, plan.desc.k, A.exact_max_magnitude, a_rows ? &A.exact_axes.rows : nullptr,
+                        B.exact_max_magnitude, b_cols ? &B.exact_axes.cols : nullptr, bound, out_ranges);
   if (st != RNS8_SUCCESS) return st;
   return exact_range_fits(plan.desc.semantics, bound, plan.modulus_product) ? RNS8_SUCCESS : RNS8_RANGE_ERROR;
 }
 
-void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, ExactRanges* ranges) {
+rns8_status resolve_exact_range(rns8_context& ctx, const rns8_matrix& M) {
+  DeferredExactRange& d = M.exact_deferred;
+  if (!d.pending) return RNS8_SUCCESS;
+  i256 bound;
+  ExactRanges ranges;
+  const rns8_status st = exact_gemm_bound(ctx, d.m, d.n, d.k, d.a_max, d.a_rows_known ? &d.a_rows : nullptr,
+                                          d.b_max, d.b_cols_known ? &d.b_cols : nullptr, bound, &ranges);
+  if (st != RNS8_SUCCESS) return st;
+  M.exact_max_magnitude = bound;
+  M.exact_axes.rows.swap(ranges.rows);
+  M.exact_axes.cols.swap(ranges.cols);
+  M.exact_deferred = DeferredExactRange{};
+  return RNS8_SUCCESS;
+}
+
+void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, ExactRanges* ranges,
+                        DeferredExactRange* defer) {
   if (!exact_wide(plan.desc.semantics)) return;
   C.exact_max_magnitude = bound;
   C.exact_axes.rows.clear();
@@ -203,6 +246,8 @@ void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, Exac
     C.exact_axes.rows.swap(ranges->rows);
     C.exact_axes.cols.swap(ranges->cols);
   }
+  C.exact_deferred = DeferredExactRange{};
+  if (defer && defer->pending) std::swap(C.exact_deferred, *defer);
   C.exact_range_prefix = plan.prefix;
 }
 

@@ -308,6 +308,7 @@ rns8_status pack_native(rns8_context* ctx, rns8_matrix* matrix, const T* src, in
     matrix->exact_max_magnitude = exact_bound;
     matrix->exact_axes.rows.swap(ranges.rows);
     matrix->exact_axes.cols.swap(ranges.cols);
+    matrix->exact_deferred = DeferredExactRange{};
     matrix->exact_range_prefix = matrix->prefix;
   }
   matrix->source_version = source_version;
@@ -708,6 +709,7 @@ rns8_status grouped_gemm(rns8_context* ctx, const rns8_plan* plan, const rns8_gr
   }
   std::vector<i256> bounds(exact_wide(plan->desc.semantics) ? count : 0);
   std::vector<ExactRanges> ranges(bounds.size());
+  std::vector<DeferredExactRange> deferred(bounds.size());
   for (uint32_t i = 0; i < count; ++i) {
     const auto& t = tasks[i];
     const rns8_status v = finite ? validate_finite_operands(*ctx, *plan, modulus, *t.a, *t.b, *t.c)
@@ -718,7 +720,7 @@ rns8_status grouped_gemm(rns8_context* ctx, const rns8_plan* plan, const rns8_gr
       if (t.c == tasks[j].a || t.c == tasks[j].b || (i != j && t.c == tasks[j].c)) return RNS8_INVALID_ARGUMENT;
     }
     if (!bounds.empty()) {
-      const rns8_status r = exact_gemm_range(*ctx, *plan, *t.a, *t.b, bounds[i], &ranges[i]);
+      const rns8_status r = exact_gemm_range(*ctx, *plan, *t.a, *t.b, bounds[i], &ranges[i], &deferred[i]);
       if (r != RNS8_SUCCESS) return r;
     }
   }
@@ -745,7 +747,7 @@ rns8_status grouped_gemm(rns8_context* ctx, const rns8_plan* plan, const rns8_gr
     C.device_current = true;
     C.source_version = combine_source_versions(tasks[i].a->source_version, tasks[i].b->source_version);
     if (finite) C.finite_modulus = modulus;
-    if (!bounds.empty()) commit_exact_range(C, *plan, bounds[i], &ranges[i]);
+    if (!bounds.empty()) commit_exact_range(C, *plan, bounds[i], &ranges[i], &deferred[i]);
   }
   return RNS8_SUCCESS;
 }
@@ -804,8 +806,9 @@ extern "C" rns8_status rns8_gemm_rns(rns8_context* ctx, const rns8_plan* plan, c
     if (st != RNS8_SUCCESS) return st;
     i256 bound;
     ExactRanges ranges;
+    DeferredExactRange defer;
     if (exact_wide(plan->desc.semantics)) {
-      st = exact_gemm_range(*ctx, *plan, *A, *B, bound, &ranges);
+      st = exact_gemm_range(*ctx, *plan, *A, *B, bound, &ranges, &defer);
       if (st != RNS8_SUCCESS) return st;
     }
     DeviceScope dev(ctx->device_id);
@@ -818,7 +821,7 @@ extern "C" rns8_status rns8_gemm_rns(rns8_context* ctx, const rns8_plan* plan, c
     if (st != RNS8_SUCCESS) return st;
     C->device_current = true;
     C->source_version = combine_source_versions(A->source_version, B->source_version);
-    if (exact_wide(plan->desc.semantics)) commit_exact_range(*C, *plan, bound, &ranges);
+    if (exact_wide(plan->desc.semantics)) commit_exact_range(*C, *plan, bound, &ranges, &defer);
     return RNS8_SUCCESS;
   });
 }

@@ -45,6 +45,18 @@ struct AxisRange {
 struct ExactRanges {
   std::vector<AxisRange> rows, cols;
 };
+// The per-cell bound pass of an exact-wide GEMM whose cheap bound
+// K * max|A| * max|B| already fitted the prefix: its only results are the
+// output's recorded bound and row/column records, which no decision needs
+// until the output feeds another exact-wide GEMM. The pass's inputs are kept
+// here and it runs then (resolve_exact_range), with the same result.
+struct DeferredExactRange {
+  bool pending = false;
+  int64_t m = 0, n = 0, k = 0;
+  i256 a_max, b_max;
+  bool a_rows_known = false, b_cols_known = false;
+  std::vector<AxisRange> a_rows, b_cols;
+};
 
 }  // namespace rns8host
 
@@ -102,9 +114,12 @@ struct rns8_matrix {
   rns8host::DevBuf staging;     // export staging
   rns8host::DevBuf export_jobs; // per-tile export descriptors (scheduled plans)
   // Exact-wide proof (reference internal.hpp:96-99); zero prefix = unknown.
-  rns8host::i256 exact_max_magnitude;
+  // Mutable: a GEMM output's records may be completed lazily when it is read
+  // as an operand (DeferredExactRange).
+  mutable rns8host::i256 exact_max_magnitude;
   uint32_t exact_range_prefix = 0;
-  rns8host::ExactRanges exact_axes;
+  mutable rns8host::ExactRanges exact_axes;
+  mutable rns8host::DeferredExactRange exact_deferred;
 };
 
 struct rns8_workspace {
@@ -172,8 +187,11 @@ rns8_status exact_gemm_bound(rns8_context& ctx, int64_t m, int64_t n, int64_t k,
                              const std::vector<AxisRange>* a_rows, const i256& b_max,
                              const std::vector<AxisRange>* b_cols, i256& bound, ExactRanges* out_ranges);
 rns8_status exact_gemm_range(rns8_context& ctx, const rns8_plan& plan, const rns8_matrix& A, const rns8_matrix& B,
-                             i256& bound, ExactRanges* out_ranges);
-void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, ExactRanges* ranges);
+                             i256& bound, ExactRanges* out_ranges, DeferredExactRange* defer = nullptr);
+// Runs a matrix's deferred per-cell bound pass, if any.
+rns8_status resolve_exact_range(rns8_context& ctx, const rns8_matrix& M);
+void commit_exact_range(rns8_matrix& C, const rns8_plan& plan, i256& bound, ExactRanges* ranges,
+                        DeferredExactRange* defer = nullptr);
 
 uint64_t next_matrix_id();
 uint64_t plan_fingerprint(const rns8_plan& plan);
