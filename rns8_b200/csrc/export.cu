@@ -38,6 +38,31 @@ __device__ __forceinline__ int64_t dst_index(const ExportArgs& a, int64_t cell) 
   return row * a.ld + (cell - row * a.n);
 }
 
+// Writes a cell's limbs from its 192-bit value w32 (two's complement for the
+// signed mode, the canonical value for the unsigned one): limb_count limbs,
+// sign (or zero) filled above 192 bits; false when the value does not fit.
+template <Mode kMode>
+__device__ __forceinline__ bool store_limbs(const ExportArgs& a, int64_t cell, const uint32_t (&w32)[6]) {
+  uint64_t v[3];
+#pragma unroll
+  for (int l = 0; l < 3; ++l) v[l] = static_cast<uint64_t>(w32[2 * l]) | (static_cast<uint64_t>(w32[2 * l + 1]) << 32);
+  const uint32_t limbs = a.limb_count;
+  const uint64_t sign_fill = (kMode == Mode::LimbsSigned && (v[2] >> 63)) ? ~0ull : 0ull;
+  if (limbs == 1) {
+    const uint64_t ext = (kMode == Mode::LimbsSigned && (v[0] >> 63)) ? ~0ull : 0ull;
+    if (v[1] != ext || v[2] != ext) return false;
+  } else if (limbs == 2) {
+    const uint64_t ext = (kMode == Mode::LimbsSigned && (v[1] >> 63)) ? ~0ull : 0ull;
+    if (v[2] != ext) return false;
+  }
+  uint64_t* out = static_cast<uint64_t*>(a.dst) + dst_index(a, cell) * static_cast<int64_t>(limbs);
+  out[0] = v[0];
+  if (limbs > 1) out[1] = v[1];
+  if (limbs > 2) out[2] = v[2];
+  for (uint32_t l = 3; l < limbs; ++l) out[l] = sign_fill;
+  return true;
+}
+
 // Reconstructs one cell into dst (one int64/uint64, or limb_count limbs).
 template <int P, Mode kMode>
 __device__ __forceinline__ bool export_cell(const ExportArgs& a, int64_t cell, const int (&r)[P]) {
@@ -68,25 +93,74 @@ __device__ __forceinline__ bool export_cell(const ExportArgs& a, int64_t cell, c
         w32[l] = static_cast<uint32_t>(cur - sub);
       }
     }
-    uint64_t v[3];
-#pragma unroll
-    for (int l = 0; l < 3; ++l) v[l] = static_cast<uint64_t>(w32[2 * l]) | (static_cast<uint64_t>(w32[2 * l + 1]) << 32);
-    const uint32_t limbs = a.limb_count;
-    const uint64_t sign_fill = (kMode == Mode::LimbsSigned && (v[2] >> 63)) ? ~0ull : 0ull;
-    if (limbs == 1) {
-      const uint64_t ext = (kMode == Mode::LimbsSigned && (v[0] >> 63)) ? ~0ull : 0ull;
-      if (v[1] != ext || v[2] != ext) return false;
-    } else if (limbs == 2) {
-      const uint64_t ext = (kMode == Mode::LimbsSigned && (v[1] >> 63)) ? ~0ull : 0ull;
-      if (v[2] != ext) return false;
-    }
-    uint64_t* out = static_cast<uint64_t*>(a.dst) + dst_index(a, cell) * static_cast<int64_t>(limbs);
-    out[0] = v[0];
-    if (limbs > 1) out[1] = v[1];
-    if (limbs > 2) out[2] = v[2];
-    for (uint32_t l = 3; l < limbs; ++l) out[l] = sign_fill;
-    return true;
+    return store_limbs<kMode>(a, cell, w32);
   }
+}
+
+// Exact-wide limbs by the fractional CRT (garner.cuh, wide_frac_reconstruct):
+// each thread takes 4 consecutive cells (one 32-bit load per plane), turns
+// the P plane words into 4-plane cell words with byte permutes, reconstructs
+// every cell with dp4a byte-slice sums, and sends the rare cells whose
+// quotient is in doubt (|v| within rounding error of M/2) to the exact
+// Garner path.
+template <int P, Mode kMode>
+__global__ void __launch_bounds__(256) export_limbs_frac_kernel(ExportArgs a) {
+  constexpr int kG = (P + 3) / 4;
+  constexpr GarnerTable<P> GT = make_table<P>();
+  const int64_t cells = a.m * a.n;
+  const int64_t groups = cells / 4;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  bool bad = false;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += step) {
+    uint32_t w[4 * kG];
+#pragma unroll
+    for (int p = 0; p < 4 * kG; ++p)
+      w[p] = p < P ? (__ldcs(reinterpret_cast<const uint32_t*>(a.planes + static_cast<int64_t>(p) * cells) + g) ^
+                      0x80808080u)
+                   : 0u;
+    uint32_t cw[4][kG];
+#pragma unroll
+    for (int q = 0; q < kG; ++q) {  // 4 x 4 byte transpose: plane words -> cell words
+      const uint32_t t0 = __byte_perm(w[4 * q], w[4 * q + 1], 0x5140);
+      const uint32_t t1 = __byte_perm(w[4 * q + 2], w[4 * q + 3], 0x5140);
+      const uint32_t t2 = __byte_perm(w[4 * q], w[4 * q + 1], 0x7362);
+      const uint32_t t3 = __byte_perm(w[4 * q + 2], w[4 * q + 3], 0x7362);
+      cw[0][q] = __byte_perm(t0, t1, 0x5410);
+      cw[1][q] = __byte_perm(t0, t1, 0x7632);
+      cw[2][q] = __byte_perm(t2, t3, 0x5410);
+      cw[3][q] = __byte_perm(t2, t3, 0x7632);
+    }
+    uint32_t undecided = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t v[6];
+      if (!wide_frac_reconstruct<P>(cw[c], v)) {
+        undecided |= 1u << c;
+        continue;
+      }
+      if constexpr (kMode == Mode::LimbsUnsigned) {
+        if (v[5] >> 31) {  // centered value below zero: the canonical value is v + M
+          uint64_t carry = 0;
+#pragma unroll
+          for (int l = 0; l < 6; ++l) {
+            const uint64_t t = static_cast<uint64_t>(v[l]) + (l < kLimbs32 ? GT.product[l] : 0u) + carry;
+            v[l] = static_cast<uint32_t>(t);
+            carry = t >> 32;
+          }
+        }
+      }
+      bad |= !store_limbs<kMode>(a, 4 * g + c, v);
+    }
+    while (undecided != 0) {
+      const int c = __ffs(undecided) - 1;
+      undecided &= undecided - 1;
+      int r[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) r[p] = static_cast<int>((w[p] >> (8 * c)) & 0xFFu) - 128;
+      bad |= !export_cell<P, kMode>(a, 4 * g + c, r);
+    }
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(a.status, kDevRangeError);
 }
 
 // Each thread reconstructs 4 consecutive cells (one 32-bit load per plane).
@@ -235,6 +309,12 @@ cudaError_t launch_export(const ExportArgs& a, cudaStream_t stream) {
   int64_t blocks = (work + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
+  if constexpr (kMode == Mode::LimbsSigned || kMode == Mode::LimbsUnsigned) {
+    if (vec && P >= 2) {
+      export_limbs_frac_kernel<P, kMode><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+      return cudaGetLastError();
+    }
+  }
   if (vec)
     export_kernel<P, kMode, true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
   else

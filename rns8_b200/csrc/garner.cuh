@@ -266,6 +266,173 @@ struct FracLimits {
   uint64_t s_init;
 };
 
+// ---- fractional CRT for exact-wide limbs ---------------------------------------
+// The same approximate-quotient CRT at full width: v = sum_i r_i * G_i - q*M
+// with G_i = E_i * inv_i (< M) is computed modulo 2^192, where the centered
+// value |v| <= M/2 < 2^155 is exact in two's complement, and q is the nearest
+// integer to sum_i r_i * inv_i / m_i (2^-31 fixed point). The quotient is
+// only in doubt when |v| is within the rounding error of M/2, which no
+// admitted exact-wide product reaches; such cells take the exact Garner path.
+// Four planes' bytes of one cell form a word, so every byte-slice sum
+// sum_i u_i * byte_b(G_i) over 4 planes is one dp4a.
+template <int P>
+constexpr int wide_bytes() {  // bytes of M_P
+  uint64_t prod[kLimbs32] = {1, 0, 0, 0, 0};
+  for (int i = 0; i < P; ++i) {
+    uint64_t carry = 0;
+    for (int l = 0; l < kLimbs32; ++l) {
+      const uint64_t v = prod[l] * ladder_at(i) + carry;
+      prod[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+  }
+  int bytes = 4 * kLimbs32;
+  while (bytes > 1 && ((prod[(bytes - 1) / 4] >> (8 * ((bytes - 1) % 4))) & 0xFFu) == 0) --bytes;
+  return bytes;
+}
+
+template <int P>
+struct WideFracTable {
+  static constexpr int kGroups = (P + 3) / 4;
+  static constexpr int kBytes = wide_bytes<P>();
+  uint32_t fpack[kGroups][4];       // byte b of F_i for planes 4g..4g+3
+  uint32_t gpack[kGroups][kBytes];  // byte b of G_i for planes 4g..4g+3
+  uint32_t c0[6];                   // 128 * sum G_i - kQuotientBias * M  (mod 2^192)
+  uint32_t product[kLimbs32];       // M
+  uint64_t s_init;                  // 2^30 + kQuotientBias * 2^31 - 128 * sum F_i
+  uint32_t t_dec;                   // the quotient is certain when |frac| <= t_dec
+};
+
+template <int P>
+__host__ __device__ constexpr WideFracTable<P> make_wide_frac_table() {
+  WideFracTable<P> t{};
+  constexpr int kG = WideFracTable<P>::kGroups;
+  constexpr int kB = WideFracTable<P>::kBytes;
+  uint64_t M[6] = {1, 0, 0, 0, 0, 0};  // 32-bit limbs in 64-bit words
+  for (int i = 0; i < P; ++i) {
+    uint64_t carry = 0;
+    for (int l = 0; l < 6; ++l) {
+      const uint64_t v = M[l] * ladder_at(i) + carry;
+      M[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+  }
+  for (int l = 0; l < kLimbs32; ++l) t.product[l] = static_cast<uint32_t>(M[l]);
+  uint64_t sumG[6] = {0, 0, 0, 0, 0, 0};
+  int64_t sumF = 0;
+  for (int g = 0; g < kG; ++g) {
+    for (int b = 0; b < 4; ++b) t.fpack[g][b] = 0;
+    for (int b = 0; b < kB; ++b) t.gpack[g][b] = 0;
+  }
+  for (int i = 0; i < P; ++i) {
+    const uint32_t mi = ladder_at(i);
+    uint64_t E[6] = {1, 0, 0, 0, 0, 0};  // M / m_i
+    uint32_t emod = 1;
+    for (int j = 0; j < P; ++j) {
+      if (j == i) continue;
+      uint64_t carry = 0;
+      for (int l = 0; l < 6; ++l) {
+        const uint64_t v = E[l] * ladder_at(j) + carry;
+        E[l] = v & 0xFFFFFFFFull;
+        carry = v >> 32;
+      }
+      emod = (emod * ladder_at(j)) % mi;
+    }
+    const uint32_t inv = inv_mod(emod, mi);
+    uint64_t G[6] = {0, 0, 0, 0, 0, 0};  // E_i * inv_i < M
+    uint64_t carry = 0;
+    for (int l = 0; l < 6; ++l) {
+      const uint64_t v = E[l] * inv + carry;
+      G[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+    const uint32_t F = static_cast<uint32_t>(((static_cast<uint64_t>(inv) << 31) + mi / 2) / mi);
+    sumF += F;
+    carry = 0;
+    for (int l = 0; l < 6; ++l) {
+      const uint64_t v = sumG[l] + G[l] + carry;
+      sumG[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+    const int g = i / 4, lane = i % 4;
+    for (int b = 0; b < 4; ++b) t.fpack[g][b] |= ((F >> (8 * b)) & 0xFFu) << (8 * lane);
+    for (int b = 0; b < kB; ++b) t.gpack[g][b] |= static_cast<uint32_t>((G[b / 4] >> (8 * (b % 4))) & 0xFFu) << (8 * lane);
+  }
+  // c0 = 128 * sumG - bias * M  (mod 2^192)
+  uint64_t a[6] = {0, 0, 0, 0, 0, 0}, bm[6] = {0, 0, 0, 0, 0, 0};
+  uint64_t carry = 0;
+  for (int l = 0; l < 6; ++l) {
+    const uint64_t v = sumG[l] * 128 + carry;
+    a[l] = v & 0xFFFFFFFFull;
+    carry = v >> 32;
+  }
+  carry = 0;
+  for (int l = 0; l < 6; ++l) {
+    const uint64_t v = M[l] * static_cast<uint64_t>(kQuotientBias) + carry;
+    bm[l] = v & 0xFFFFFFFFull;
+    carry = v >> 32;
+  }
+  uint64_t borrow = 0;
+  for (int l = 0; l < 6; ++l) {
+    const uint64_t sub = bm[l] + borrow;
+    borrow = a[l] < sub ? 1 : 0;
+    t.c0[l] = static_cast<uint32_t>((a[l] + (borrow << 32)) - sub);
+  }
+  t.s_init = (1ull << 30) + (static_cast<uint64_t>(kQuotientBias) << 31) - static_cast<uint64_t>(128 * sumF);
+  t.t_dec = (1u << 30) - 2u * (64u * P + 2u);
+  return t;
+}
+
+// v (192-bit two's complement, 32-bit limbs) of the cell whose four-plane
+// words are cw[g] (u_i = r_i + 128 in byte i % 4 of word i / 4). Returns false
+// when the quotient is in doubt.
+template <int P>
+__device__ __forceinline__ bool wide_frac_reconstruct(const uint32_t (&cw)[(P + 3) / 4], uint32_t (&v)[6]) {
+  constexpr WideFracTable<P> T = make_wide_frac_table<P>();
+  constexpr int kG = WideFracTable<P>::kGroups;
+  constexpr int kB = WideFracTable<P>::kBytes;
+  uint32_t tf[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int b = 0; b < 4; ++b)
+#pragma unroll
+    for (int g = 0; g < kG; ++g) tf[b] = __dp4a(cw[g], T.fpack[g][b], tf[b]);
+  const uint64_t s = T.s_init + tf[0] + (static_cast<uint64_t>(tf[1]) << 8) + (static_cast<uint64_t>(tf[2]) << 16) +
+                     (static_cast<uint64_t>(tf[3]) << 24);
+  const int32_t frac = static_cast<int32_t>(static_cast<uint32_t>(s) & 0x7FFFFFFFu) - (1 << 30);
+  if (static_cast<uint32_t>(frac < 0 ? -frac : frac) > T.t_dec) return false;
+  const uint32_t q = static_cast<uint32_t>(s >> 31);
+  // S = sum_i u_i * G_i (mod 2^192) from byte-slice sums (each < 2^21).
+  uint64_t carry = 0;
+#pragma unroll
+  for (int l = 0; l < 6; ++l) {
+    uint64_t acc = carry;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = 4 * l + j;
+      if (b < kB) {
+        uint32_t tb = 0;
+#pragma unroll
+        for (int g = 0; g < kG; ++g) tb = __dp4a(cw[g], T.gpack[g][b], tb);
+        acc += static_cast<uint64_t>(tb) << (8 * j);
+      }
+    }
+    v[l] = static_cast<uint32_t>(acc);
+    carry = acc >> 32;
+  }
+  // v = S - c0 - q * M  (mod 2^192)
+  uint64_t qm_carry = 0;
+  int64_t borrow = 0;
+#pragma unroll
+  for (int l = 0; l < 6; ++l) {
+    const uint64_t qm = static_cast<uint64_t>(q) * (l < kLimbs32 ? T.product[l] : 0u) + qm_carry;
+    qm_carry = qm >> 32;
+    const int64_t d = static_cast<int64_t>(v[l]) - T.c0[l] - static_cast<uint32_t>(qm) + borrow;
+    v[l] = static_cast<uint32_t>(d);
+    borrow = d >> 32;  // 0, -1 or -2
+  }
+  return true;
+}
+
 // 1 = value written to *out, 0 = out of range, -1 = undecided (use exact path).
 // u_i = r_i + 128.
 template <int P>

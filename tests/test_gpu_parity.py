@@ -414,6 +414,35 @@ def test_export_limbs_match_oracle(lib, oracle, prefix, limbs):
             np.testing.assert_array_equal(host(d_out, np.uint64), owant)
 
 
+@pytest.mark.parametrize("prefix", [2, 9, 18, 20])
+@pytest.mark.parametrize("limbs", [3, 1])
+def test_export_limbs_near_half_range(lib, oracle, prefix, limbs):
+    """Values at and around +-M/2, where the fractional CRT's quotient is in
+    doubt and the exact Garner path must take over, between ordinary values;
+    4-cell groups so the vector kernel runs."""
+    M = 1
+    for mm in LADDER[:prefix]:
+        M *= mm
+    h = M // 2
+    vals = [h - 1, -h, h - 2, -h + 1, 0, 1, -1, h // 3, -(h // 5), h - (1 << 20), -h + (1 << 20), 12345]
+    vals += [(i * 0x9E3779B97F4A7C15) % M - h for i in range(1, 21)]
+    m, n = 4, 8
+    centered = lambda v, mm: (lambda r: r - mm if r >= (mm + 1) // 2 else r)(v % mm)
+    planes = np.array([[[centered(vals[r * n + c], mm) for c in range(n)] for r in range(m)] for mm in LADDER[:prefix]],
+                      np.int8)
+    for signed in (True, False):
+        ost, owant = oracle.export_limbs(planes, prefix, limbs, signed)
+        d_p = dev(planes)
+        d_out = torch.zeros((m, n, limbs), dtype=torch.int64, device="cuda")
+        status = torch.zeros(4, dtype=torch.int32, device="cuda")
+        assert lib.rns8_cuda_export_limbs_device(0, d_p.data_ptr(), m, n, prefix, 1 if signed else 0, limbs,
+                                                 d_out.data_ptr(), n, status.data_ptr(), stream()) == OK
+        torch.cuda.synchronize()
+        assert (RANGE if int(status[0].item()) else OK) == ost, (signed, prefix, limbs)
+        if ost == OK:
+            np.testing.assert_array_equal(host(d_out, np.uint64), owant)
+
+
 # ---- public C ABI: the whole path ----------------------------------------------------
 @pytest.fixture(scope="module")
 def ctx(rns8):
