@@ -115,6 +115,8 @@ def parse():
                          "fused NVLink exchange (strong scaling, device-resident, for comparing the two)")
     ap.add_argument("--exchange", choices=["fused", "copy"], default="fused",
                     help="--shard planes: epilogue stores into the slab owners' buffers, or local planes + copies")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every step's kernels from the host instead of replaying a captured CUDA graph")
     args = ap.parse_args()
     if args.shard != "weak-rows" and cfg_kind(args.config) not in ("i64", "u64", "exact"):
         ap.error("--shard rows|planes applies to the int64/uint64/exact-wide configs")
@@ -339,8 +341,8 @@ class DevicePipeline:
     """Device-resident buffers and the three stages of one step (pack, plane
     GEMM, export), launched through the C-ABI device seam on one stream."""
 
-    def __init__(self, torch, lib, cfg: Config, dev: int, rank: int, sptr):
-        self.torch, self.lib, self.cfg, self.dev, self.sptr = torch, lib, cfg, dev, sptr
+    def __init__(self, torch, lib, cfg: Config, dev: int, rank: int, sptr=None):
+        self.torch, self.lib, self.cfg, self.dev = torch, lib, cfg, dev
         m, n, k, P, bt = cfg.m, cfg.n, cfg.k, cfg.prefix, cfg.batch
         g = torch.Generator(device="cuda").manual_seed(1000 + rank)
         gb = torch.Generator(device="cuda").manual_seed(999)
@@ -387,6 +389,11 @@ class DevicePipeline:
         self.launches_per_step = 2 + gemm_launches + (0 if cfg.kind == "wrap" else 1)
         footprint = sum(t.numel() * t.element_size() for t in (self.A, self.B, self.ra, self.rb, self.rc, self.out))
         self.fits_l2 = footprint < (512 << 20)  # L2 is 126 MB: below this, flush it between steps
+
+    @property
+    def sptr(self):
+        """The current stream (a graph capture's stream while capturing)."""
+        return C.c_void_p(self.torch.cuda.current_stream().cuda_stream)
 
     @staticmethod
     def _check(st, what):
@@ -768,8 +775,24 @@ def main():
     peak_int8, peak_note = int8_peak_tops(torch, peaks)
     torch.cuda.synchronize()
 
+    # One step's launches captured once as a CUDA graph and replayed: the
+    # kernels and their arguments are the same every step, and the replay
+    # removes the host's per-launch cost, which dominates the small configs.
+    graph, launch_mode = None, "host launches"
+    if not args.no_graph:
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                pipe.step()
+            g.replay()
+            torch.cuda.synchronize()
+            graph, launch_mode = g, "CUDA graph replay (one capture of the step's launches)"
+        except Exception as exc:  # capture unsupported: host launches
+            launch_mode = f"host launches (graph capture failed: {type(exc).__name__})"
+    if pipe.device_status() != 0:
+        raise RuntimeError(f"device status {pipe.device_status():#x} after graph warm-up")
+
     clocks = ClockSampler(local)
-    records = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -778,12 +801,18 @@ def main():
     # Small footprints are timed step by step with a 256 MiB write between
     # steps (outside the step's events) so that no step starts with a warm L2.
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if pipe.fits_l2 else None
+    step_events = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for i in range(args.steps):
         if flush is not None:
             flush.zero_()
-        pipe.step(records[i])
+        step_events[i][0].record(stream)
+        if graph is not None:
+            graph.replay()
+        else:
+            pipe.step()
+        step_events[i][1].record(stream)
     stop.record(stream)
     torch.cuda.synchronize()
     clock_info = clocks.stop()
@@ -792,11 +821,21 @@ def main():
     if flush is None:
         total_ms = start.elapsed_time(stop)
     else:
-        total_ms = sum(r[0].elapsed_time(r[3]) for r in records)
+        total_ms = sum(e0.elapsed_time(e1) for e0, e1 in step_events)
+    if pipe.device_status() != 0:
+        raise RuntimeError(f"device status {pipe.device_status():#x} in the timed region")
+    # Per-stage split (for the roofline): the same steps launched from the
+    # host with events between the stages, after the timed region.
+    records = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        if flush is not None:
+            flush.zero_()
+        pipe.step(records[i])
+    torch.cuda.synchronize()
     stage_ms = {name: statistics.mean(r[i].elapsed_time(r[i + 1]) for r in records)
                 for i, name in enumerate(("pack", "plane_gemm", "export"))}
     if pipe.device_status() != 0:
-        raise RuntimeError(f"device status {pipe.device_status():#x} in the timed region")
+        raise RuntimeError(f"device status {pipe.device_status():#x} in the stage timing")
 
     t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
     if world > 1:
@@ -860,6 +899,7 @@ def main():
             "data": "synthetic",
             "config": {"workload": cfg.workload, "name": cfg.name, "m_per_rank": cfg.m, "n": cfg.n, "k": cfg.k,
                        "batch": cfg.batch, "prefix": cfg.prefix, "parallelism": f"row-slab x{world}",
+                       "launch": launch_mode,
                        "l2": "L2 flushed between steps (256 MiB write outside the step's events)"
                              if pipe.fits_l2 else "inputs larger than L2"},
             "roofline": roof,
