@@ -290,14 +290,25 @@ cudaError_t dispatch_subset(const T* src, int64_t rows, int64_t cols, int64_t ld
 // Finite u8: residues of bytes modulo an arbitrary m in [2, 256].
 enum class U8Kind : int {
   General = 0,   // m < 128: magic-multiply modulo per byte
-  OneStep = 1,   // 128 <= m < 256: a byte needs at most one subtraction of m
+  OneStep = 1,   // 128 <= m < 171: a byte needs at most one subtraction of m
   Identity = 2,  // m = 256: the byte read as int8 is the centered residue
+  Centered = 3,  // 171 <= m < 256: x >= ceil(m/2) ? x - m : x, one compare per byte
 };
 
 template <U8Kind kKind>
 __device__ __forceinline__ uint32_t residues4(uint32_t x, uint32_t m, uint32_t magic, uint32_t m4, uint32_t h4) {
   if constexpr (kKind == U8Kind::Identity) {
     return x;
+  } else if constexpr (kKind == U8Kind::Centered) {
+    // For m >= 171 a byte x >= m is below ceil(m/2) after one subtraction, so
+    // the centered residue is x - m exactly when x >= h = ceil(m/2) (h in
+    // [86, 128]). Bit 7 of (x & 0x7F) + (128 - h) flags 7-bit values >= h;
+    // OR x's own bit 7 (x >= 128 >= h). The flagged bytes take m (no byte
+    // overflows: m < 256), subtracted bytewise without borrows between bytes.
+    constexpr uint32_t kHigh = 0x80808080u;
+    const uint32_t t = (x & 0x7F7F7F7Fu) + h4;  // h4 holds 128 - h per byte here
+    const uint32_t sub = (((t | x) & kHigh) >> 7) * m;
+    return ((x | kHigh) - (sub & ~kHigh)) ^ ((x ^ ~sub) & kHigh);
   } else if constexpr (kKind == U8Kind::OneStep) {
     // Per byte: t = x >= m ? x - m : x, then t >= ceil(m/2) ? t - m : t
     // (mod 256, i.e. the int8 of the centered residue).
@@ -319,7 +330,8 @@ __global__ void __launch_bounds__(256) pack_u8_vec16_kernel(const uint8_t* __res
                                                             int8_t* __restrict__ out) {
   const int64_t groups = cols >> 4;
   const uint32_t m4 = (m & 0xFFu) * 0x01010101u;
-  const uint32_t h4 = ((m + 1) / 2) * 0x01010101u;
+  const uint32_t h4 = kKind == U8Kind::Centered ? (128u - (m + 1) / 2) * 0x01010101u  // 128 - ceil(m/2)
+                                                : ((m + 1) / 2) * 0x01010101u;        // ceil(m/2)
   for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
     const uint4* s = reinterpret_cast<const uint4*>(src + row * ld);
     uint4* o = reinterpret_cast<uint4*>(out + row * cols);
@@ -385,6 +397,8 @@ cudaError_t pack_finite_u8(const uint8_t* src, int64_t rows, int64_t cols, int64
     pack_u8_scalar_kernel<<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
   else if (modulus == 256)
     pack_u8_vec16_kernel<U8Kind::Identity><<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
+  else if (modulus >= 171)
+    pack_u8_vec16_kernel<U8Kind::Centered><<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
   else if (modulus >= 128)
     pack_u8_vec16_kernel<U8Kind::OneStep><<<grid, 256, 0, stream>>>(src, rows, cols, ld, modulus, magic, residues);
   else

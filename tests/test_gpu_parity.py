@@ -71,7 +71,7 @@ def test_pack_i64_u64_match_oracle(lib, oracle, prefix, shape, ld):
         np.testing.assert_array_equal(host(d_out), want)
 
 
-U8_MODULI = [2, 97, 127, 128, 129, 251, 255, 256]   # per-byte modulo, one-subtraction, identity paths
+U8_MODULI = [2, 97, 127, 128, 129, 170, 171, 172, 251, 255, 256]  # per-byte modulo, one subtraction, one compare, identity
 U8_SHAPES = [((32, 64), 64),    # contiguous: 16-byte groups over the flattened matrix
              ((16, 48), 64),    # strided rows, 16-byte groups per row
              ((5, 9), 11)]      # ragged: one byte per thread
