@@ -289,16 +289,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
       int32_t* srow = prm.scratch
                           ? prm.scratch + (static_cast<int64_t>(w.t) * prm.planes + w.p) * plane_elems + row * prm.n
                           : nullptr;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS + c * 32, v);
-        tmem_wait_ld();
+      // One 32-column chunk of this thread's accumulator row: reduce, pack,
+      // store (or add into the split-K sums).
+      auto store_chunk = [&](int c, const uint32_t (&v)[32]) {
         const int64_t col = static_cast<int64_t>(w.nt) * BN + c * 32;
-        if (!row_ok || col >= prm.n) continue;
+        if (!row_ok || col >= prm.n) return;
         if (prm.tile_sel) {  // schedule tiles are >= 64 wide: a 32-column chunk lies in one
           const uint8_t sel = prm.tile_sel[(row >> prm.sched_shift_m) * prm.sched_cols + (col >> prm.sched_shift_n)];
-          if ((sel & 0x80u) || w.p >= (sel & 0x7Fu)) continue;
+          if ((sel & 0x80u) || w.p >= (sel & 0x7Fu)) return;
         }
         if (srow) {
 #pragma unroll
@@ -319,6 +317,21 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
           dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
           if (col + 32 <= prm.n) dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
         }
+      };
+      // The next chunk's tensor-memory load is in flight while this one is
+      // reduced and stored (tcgen05.wait::ld waits for all of a thread's loads,
+      // so each load is issued right after the previous wait).
+      const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS;
+      uint32_t va[32], vb[32];
+      tmem_ld_32x32b_x32(taddr, va);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c += 2) {
+        tmem_wait_ld(va);
+        tmem_ld_32x32b_x32(taddr + (c + 1) * 32, vb);
+        store_chunk(c, va);
+        tmem_wait_ld(vb);
+        if (c + 2 < BN / 32) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, va);
+        store_chunk(c + 1, vb);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
@@ -575,7 +588,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_wrap64_kernel(const __grid_cons
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS + c * 32, v);
-          tmem_wait_ld();
+          tmem_wait_ld(v);
           const int64_t col = static_cast<int64_t>(w.nt) * BN + c * 32;
           if (!row_ok || col >= prm.n) continue;
 #pragma unroll
