@@ -152,12 +152,13 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.window = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                          "-i", str(self.gpu), "-lms", "20"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -166,7 +167,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark(self, t0: float, t1: float):
+        """The timed region on the host clock (monotonic seconds)."""
+        self.window = (t0, t1)
 
     def stop(self) -> dict:
         if not self.proc:
@@ -179,7 +184,10 @@ class ClockSampler:
             self.proc.kill()
         sm, smax, power, reasons = [], None, [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        lines = self.lines
+        in_window = [l for t, l in lines if self.window and self.window[0] <= t <= self.window[1] + 0.05]
+        use = in_window if in_window else [l for _, l in lines]
+        for line in use:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -193,7 +201,8 @@ class ClockSampler:
                 if flag.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "power_w_max": max(power) if power else None, "samples": len(sm), "reasons": sorted(reasons)}
+                "power_w_max": max(power) if power else None, "samples": len(sm),
+                "samples_in_timed_region": len(in_window), "interval_ms": 20, "reasons": sorted(reasons)}
 
 
 # ------------------------------------------------------------------------- peaks
@@ -705,11 +714,13 @@ def run_sharded(args, cfg: Config) -> None:
     clocks.start()
     time.sleep(0.3)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.monotonic()
     start.record(stream)
     for _ in range(args.steps):
         job.step()
     stop.record(stream)
     torch.cuda.synchronize()
+    clocks.mark(h0, time.monotonic())
     clock_info = clocks.stop()
     status = int(job.status[0].item())
     t = torch.tensor([start.elapsed_time(stop), 0.0 if (ok and status == 0) else 1.0], dtype=torch.float64,
@@ -803,6 +814,7 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if pipe.fits_l2 else None
     step_events = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.monotonic()
     start.record(stream)
     for i in range(args.steps):
         if flush is not None:
@@ -815,6 +827,7 @@ def main():
         step_events[i][1].record(stream)
     stop.record(stream)
     torch.cuda.synchronize()
+    clocks.mark(h0, time.monotonic())
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
