@@ -70,8 +70,15 @@ extern "C" rns8_status rns8_cuda_gemm_rns_device_no_alloc(int device_id, const i
   for (uint32_t p = 0; p < prefix; ++p) prob.moduli[p] = rns8ladder::kLadder[p];
   prob.task_count = 1;
   prob.tasks = &task;
-  const uint64_t need = rns8cuda::plane_gemm_scratch_bytes(prob, sms);
-  if (need > kNoAllocScratchBytes) return RNS8_WORKSPACE_TOO_SMALL;  // split-K sums would not fit the array
+  uint64_t need = rns8cuda::plane_gemm_scratch_bytes(prob, sms);
+  if (need > kNoAllocScratchBytes) {
+    // Tensor-core shapes whose split-K sums do not fit are refused. Shapes
+    // the tensor cores cannot address directly offer the whole array: the
+    // GEMM pads them onto the tensor cores when the padded copies fit, and
+    // otherwise runs the CUDA-core kernels, which need no more.
+    if (rns8cuda::tensor_core_path_supported(prob)) return RNS8_WORKSPACE_TOO_SMALL;
+    need = kNoAllocScratchBytes;
+  }
 
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint32_t* status = reinterpret_cast<uint32_t*>(base);

@@ -834,8 +834,241 @@ bool tensor_core_path_supported(const PlaneGemmProblem& prob) {
   return encode_fn() != nullptr;
 }
 
+// ---- unaligned shapes on the tensor cores ---------------------------------------
+// TMA needs every row pitch to be a multiple of 16 bytes. When K or N is not
+// (or a plane pointer is not 16-byte aligned), the planes are copied into
+// zero-padded ones (K and N rounded up to 16) in scratch, the padded problem
+// runs on the tensor cores, and C's first n columns are copied out. Zero
+// columns of A and zero rows of B add nothing to any sum, so the residues are
+// those of the unpadded product.
+namespace {
+
+int64_t round16(int64_t v) { return (v + 15) / 16 * 16; }
+uint64_t round256_u(uint64_t v) { return (v + 255) / 256 * 256; }
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// dst (planes x drows x dcols, dcols % 16 == 0, 16-byte aligned) = src
+// (planes x rows x cols, any pitch and alignment) inside, zero outside. One
+// 16-byte dst chunk per thread step: when the chunk's 20-byte aligned source
+// window lies inside the source row, five aligned word loads and funnel
+// shifts assemble it; otherwise (row ends, misaligned row starts) bytes.
+__global__ void __launch_bounds__(256) pad_planes_kernel(const int8_t* __restrict__ src, int64_t rows, int64_t cols,
+                                                         uint32_t planes, int8_t* __restrict__ dst, int64_t drows,
+                                                         int64_t dcols) {
+  const int64_t chunks = dcols / 16;
+  const int64_t total_rows = static_cast<int64_t>(planes) * drows;
+  for (int64_t pr = blockIdx.y; pr < total_rows; pr += gridDim.y) {
+    const int64_t p = pr / drows, r = pr - p * drows;
+    uint4* out = reinterpret_cast<uint4*>(dst + pr * dcols);
+    const uint8_t* row = reinterpret_cast<const uint8_t*>(src) + (p * rows + r) * cols;
+    for (int64_t ch = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; ch < chunks;
+         ch += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int64_t c0 = ch * 16;
+      uint32_t w[4] = {0, 0, 0, 0};
+      if (r < rows && c0 < cols) {
+        const uintptr_t addr = reinterpret_cast<uintptr_t>(row + c0);
+        const uintptr_t base = addr & ~uintptr_t(3);
+        if (base >= reinterpret_cast<uintptr_t>(row) && base + 20 <= reinterpret_cast<uintptr_t>(row + cols)) {
+          const uint32_t* wp = reinterpret_cast<const uint32_t*>(base);
+          const uint32_t sh = static_cast<uint32_t>(addr - base) * 8;
+          uint32_t v[5];
+#pragma unroll
+          for (int j = 0; j < 5; ++j) v[j] = wp[j];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) w[j] = __funnelshift_r(v[j], v[j + 1], sh);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < cols) w[j / 4] |= static_cast<uint32_t>(row[c0 + j]) << (8 * (j % 4));
+        }
+      }
+      out[ch] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// dst (planes x rows x cols, compact, 16-byte aligned) = the first cols
+// columns of src (planes x rows x scols, scols % 16 == 0, 16-byte aligned).
+// One aligned 16-byte chunk of the flattened dst per thread step; a chunk
+// inside one row reads its 16 source bytes as five aligned words (when they
+// lie inside the source row) shifted into place, a chunk that crosses rows
+// gathers bytes.
+__global__ void __launch_bounds__(256) crop_planes_kernel(const int8_t* __restrict__ src, int64_t rows, int64_t scols,
+                                                          uint32_t planes, int8_t* __restrict__ dst, int64_t cols) {
+  const int64_t total = static_cast<int64_t>(planes) * rows * cols;
+  const int64_t chunks = (total + 15) / 16;
+  const uint8_t* s8 = reinterpret_cast<const uint8_t*>(src);
+  for (int64_t ch = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; ch < chunks;
+       ch += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i0 = ch * 16;
+    const int64_t pr = i0 / cols, c0 = i0 - pr * cols;
+    uint32_t w[4] = {0, 0, 0, 0};
+    const uintptr_t row = reinterpret_cast<uintptr_t>(s8 + pr * scols);
+    const uintptr_t addr = row + static_cast<uintptr_t>(c0);
+    const uintptr_t base = addr & ~uintptr_t(3);
+    if (c0 + 16 <= cols && i0 + 16 <= total && base + 20 <= row + static_cast<uintptr_t>(scols)) {
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(base);
+      const uint32_t sh = static_cast<uint32_t>(addr - base) * 8;
+      uint32_t v[5];
+#pragma unroll
+      for (int j = 0; j < 5; ++j) v[j] = wp[j];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) w[j] = __funnelshift_r(v[j], v[j + 1], sh);
+      reinterpret_cast<uint4*>(dst)[ch] = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int j = 0; j < 16 && i0 + j < total; ++j) {
+        const int64_t i = i0 + j;
+        const int64_t r = i / cols;
+        dst[i] = static_cast<int8_t>(s8[r * scols + (i - r * cols)]);
+      }
+    }
+  }
+}
+
+// The same for a destination that is not 16-byte aligned: one byte per step.
+__global__ void __launch_bounds__(256) crop_planes_bytes_kernel(const int8_t* __restrict__ src, int64_t rows,
+                                                                int64_t scols, uint32_t planes,
+                                                                int8_t* __restrict__ dst, int64_t cols) {
+  const int64_t total = static_cast<int64_t>(planes) * rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols;
+    dst[i] = src[r * scols + (i - r * cols)];
+  }
+}
+
+unsigned flat_grid(int64_t work, int sm_count) {
+  const int64_t blocks = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count) * 16;
+  return static_cast<unsigned>(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
+}
+
+dim3 row_grid(int64_t chunks_per_row, int64_t total_rows, int sm_count) {
+  const int64_t bx = (chunks_per_row + 255) / 256;
+  int64_t by = total_rows < 65535 ? total_rows : 65535;
+  const int64_t want = static_cast<int64_t>(sm_count) * 16;  // blocks in flight
+  if (bx * by > want) by = std::max<int64_t>(1, want / bx);
+  return dim3(static_cast<unsigned>(bx < 1 ? 1 : bx), static_cast<unsigned>(by < 1 ? 1 : by));
+}
+
+
+struct PadPlan {
+  int64_t kp, np;
+  bool pad_a, pad_b, pad_c;
+  uint64_t a_bytes, b_bytes, c_bytes;  // per task, 256-rounded (0 when not padded)
+  uint64_t per_task() const { return a_bytes + b_bytes + c_bytes; }
+};
+
+PadPlan pad_plan(const PlaneGemmProblem& prob, const PlaneGemmTask* tasks, uint32_t count) {
+  PadPlan pp{};
+  pp.kp = round16(prob.k);
+  pp.np = round16(prob.n);
+  bool a_mis = false, b_mis = false, c_mis = false;
+  for (uint32_t t = 0; t < count; ++t) {
+    a_mis |= !aligned16(tasks[t].a);
+    b_mis |= !aligned16(tasks[t].b);
+    c_mis |= !aligned16(tasks[t].c);
+  }
+  pp.pad_a = pp.kp != prob.k || a_mis;
+  pp.pad_b = pp.kp != prob.k || pp.np != prob.n || b_mis;
+  pp.pad_c = pp.np != prob.n || c_mis;
+  const uint64_t P = prob.planes;
+  pp.a_bytes = pp.pad_a ? round256_u(P * prob.m * pp.kp) : 0;
+  pp.b_bytes = pp.pad_b ? round256_u(P * pp.kp * pp.np) : 0;
+  pp.c_bytes = pp.pad_c ? round256_u(P * prob.m * pp.np) : 0;
+  return pp;
+}
+
+uint64_t tc_split_bytes(const PlaneGemmProblem& prob, int sm_count);
+
+bool padded_path_possible(const PlaneGemmProblem& prob) {
+  return prob.m > 0 && prob.n >= 16 && prob.k > 0 && prob.task_count > 0 && prob.planes > 0 && prob.planes <= 20 &&
+         round16(prob.m) <= (int64_t(1) << 31) && round16(prob.n) <= (int64_t(1) << 31) &&
+         round16(prob.k) <= (int64_t(1) << 31) && encode_fn() != nullptr;
+}
+
+// Scratch of the padded run: padded planes for one chunk of tasks and the
+// split-K sums of the padded chunk.
+uint64_t padded_scratch_bytes(const PlaneGemmProblem& prob, int sm_count) {
+  const uint32_t chunk = prob.task_count < kMaxGroupTasks ? prob.task_count : kMaxGroupTasks;
+  const PadPlan pp = pad_plan(prob, prob.tasks, chunk);
+  PlaneGemmProblem padded = prob;
+  padded.k = pp.kp;
+  padded.n = pp.np;
+  padded.task_count = chunk;
+  return chunk * pp.per_task() + tc_split_bytes(padded, sm_count);
+}
+
+}  // namespace
+
+namespace {
+uint64_t tc_split_bytes(const PlaneGemmProblem& prob, int sm_count) {
+  const uint32_t chunk = prob.task_count < kMaxGroupTasks ? prob.task_count : kMaxGroupTasks;
+  PlaneGemmProblem one = prob;
+  one.task_count = chunk;
+  const TcSchedule s = tc_schedule(one, sm_count);
+  if (s.splits <= 1) return 0;
+  return static_cast<uint64_t>(prob.m) * prob.n * prob.planes * chunk * sizeof(int32_t);
+}
+
+cudaError_t padded_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scratch, uint64_t scratch_bytes,
+                              uint32_t* dev_status, cudaStream_t stream) {
+  for (uint32_t t0 = 0; t0 < prob.task_count; t0 += kMaxGroupTasks) {
+    const uint32_t count = prob.task_count - t0 < static_cast<uint32_t>(kMaxGroupTasks)
+                               ? prob.task_count - t0
+                               : static_cast<uint32_t>(kMaxGroupTasks);
+    const PlaneGemmTask* tasks = prob.tasks + t0;
+    const PadPlan pp = pad_plan(prob, tasks, count);
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    const uint64_t pads = count * pp.per_task();
+    if (pads > scratch_bytes) return cudaErrorInvalidValue;
+    PlaneGemmTask padded_tasks[kMaxGroupTasks];
+    for (uint32_t t = 0; t < count; ++t) {
+      uint8_t* slot = base + t * pp.per_task();
+      int8_t* a = pp.pad_a ? reinterpret_cast<int8_t*>(slot) : const_cast<int8_t*>(tasks[t].a);
+      int8_t* b = pp.pad_b ? reinterpret_cast<int8_t*>(slot + pp.a_bytes) : const_cast<int8_t*>(tasks[t].b);
+      int8_t* c = pp.pad_c ? reinterpret_cast<int8_t*>(slot + pp.a_bytes + pp.b_bytes) : tasks[t].c;
+      if (pp.pad_a)
+        pad_planes_kernel<<<row_grid(pp.kp / 16, prob.planes * prob.m, sm_count), 256, 0, stream>>>(
+            tasks[t].a, prob.m, prob.k, prob.planes, a, prob.m, pp.kp);
+      if (pp.pad_b)
+        pad_planes_kernel<<<row_grid(pp.np / 16, prob.planes * pp.kp, sm_count), 256, 0, stream>>>(
+            tasks[t].b, prob.k, prob.n, prob.planes, b, pp.kp, pp.np);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+      padded_tasks[t] = {a, b, c};
+    }
+    PlaneGemmProblem padded = prob;
+    padded.k = pp.kp;
+    padded.n = pp.np;
+    padded.tasks = padded_tasks;
+    padded.task_count = count;
+    if (!tensor_core_path_supported(padded)) return cudaErrorInvalidValue;
+    cudaError_t e = tc_plane_gemm(padded, sm_count, base + pads, scratch_bytes - pads, dev_status, stream);
+    if (e != cudaSuccess) return e;
+    if (pp.pad_c) {
+      for (uint32_t t = 0; t < count; ++t) {
+        const int64_t total = static_cast<int64_t>(prob.planes) * prob.m * prob.n;
+        if (aligned16(tasks[t].c))
+          crop_planes_kernel<<<flat_grid((total + 15) / 16, sm_count), 256, 0, stream>>>(
+              padded_tasks[t].c, prob.m, pp.np, prob.planes, tasks[t].c, prob.n);
+        else
+          crop_planes_bytes_kernel<<<flat_grid(total, sm_count), 256, 0, stream>>>(padded_tasks[t].c, prob.m, pp.np,
+                                                                                   prob.planes, tasks[t].c, prob.n);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+      }
+    }
+  }
+  return cudaSuccess;
+}
+}  // namespace
+
 uint64_t plane_gemm_scratch_bytes(const PlaneGemmProblem& prob, int sm_count) {
-  if (!tensor_core_path_supported(prob)) return skinny_scratch_bytes(prob);  // 0 unless n < 16
+  if (!tensor_core_path_supported(prob)) {
+    if (skinny_path_supported(prob)) return skinny_scratch_bytes(prob);
+    return padded_path_possible(prob) ? padded_scratch_bytes(prob, sm_count) : 0;
+  }
   const uint32_t chunk = prob.task_count < kMaxGroupTasks ? prob.task_count : kMaxGroupTasks;
   PlaneGemmProblem one = prob;
   one.task_count = chunk;
@@ -852,6 +1085,11 @@ cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count
       scratch_bytes >= skinny_scratch_bytes(prob)) {
     if (used) *used = GemmPath::Simt;  // the narrow-output kernel (CUDA cores)
     return skinny_plane_gemm(prob, scratch, scratch_bytes, stream);
+  }
+  if (path == GemmPath::Auto && !tc_ok && padded_path_possible(prob) && scratch &&
+      scratch_bytes >= padded_scratch_bytes(prob, sm_count)) {
+    if (used) *used = GemmPath::TensorCore;  // zero-padded copies on the tensor cores
+    return padded_plane_gemm(prob, sm_count, scratch, scratch_bytes, dev_status, stream);
   }
   if (path == GemmPath::Simt || !tc_ok) {
     if (used) *used = GemmPath::Simt;

@@ -156,6 +156,77 @@ def test_plane_gemm_unaligned_shapes_use_simt(lib, oracle):
             assert st == 1  # the tensor-core path refuses rows TMA cannot address
 
 
+@pytest.mark.parametrize("m,n,k", [
+    (1000, 1000, 1000),   # K and N not multiples of 16: zero-padded onto the tensor cores
+    (300, 4090, 512),     # N ragged, several N tiles, C cropped back
+    (200, 256, 4100),     # K ragged, few tiles: split-K on the padded problem
+    (129, 17, 77),        # smallest N for the padded path
+])
+def test_unaligned_shapes_padded_onto_tensor_cores(lib, oracle, m, n, k):
+    """Auto path with the advertised scratch: K or N not multiples of 16 run
+    the tensor-core kernel on zero-padded copies; the residues must equal the
+    oracle's and the CUDA-core kernel's byte for byte."""
+    rng = np.random.default_rng(m + 3 * n + 7 * k)
+    P = 9
+    a = random_residues(rng, P, m, k)
+    b = random_residues(rng, P, k, n)
+    a[:, 0, :] = -128
+    b[:, :, 0] = -128
+    st, got, word = run_gemm(lib, a, b, P, 0)
+    assert st == OK and word == 0
+    st, simt, _ = run_gemm(lib, a, b, P, 2)
+    assert st == OK
+    np.testing.assert_array_equal(got, simt)
+    if m * n * k <= 300 * 4090 * 512:
+        np.testing.assert_array_equal(got, oracle.gemm_rns(a, b, P))
+
+
+def test_misaligned_plane_pointers_padded(lib, oracle):
+    """Plane pointers off a 16-byte boundary (aligned shapes) take the padded
+    copies too."""
+    rng = np.random.default_rng(12)
+    P, m, n, k = 3, 64, 32, 48
+    a = random_residues(rng, P, m, k)
+    b = random_residues(rng, P, k, n)
+    raw_a = torch.zeros(a.size + 16, dtype=torch.int8, device="cuda")
+    raw_b = torch.zeros(b.size + 16, dtype=torch.int8, device="cuda")
+    raw_c = torch.zeros(P * m * n + 16, dtype=torch.int8, device="cuda")
+    raw_a[3:3 + a.size] = dev(a).reshape(-1)
+    raw_b[5:5 + b.size] = dev(b).reshape(-1)
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    sb = lib.rns8_cuda_gemm_rns_scratch_bytes(0, m, n, k, P) + (1 << 20)  # room for the padded copies
+    scratch = torch.empty(sb, dtype=torch.uint8, device="cuda")
+    st = lib.rns8_cuda_gemm_rns_device(0, raw_a.data_ptr() + 3, raw_b.data_ptr() + 5, raw_c.data_ptr() + 7, m, n, k, P,
+                                       0, scratch.data_ptr(), sb, status.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert st == OK and int(status[0].item()) == 0
+    got = raw_c[7:7 + P * m * n].cpu().numpy().reshape(P, m, n)
+    np.testing.assert_array_equal(got, oracle.gemm_rns(a, b, P))
+
+
+def test_finite_grouped_unaligned_k(lib, oracle):
+    rng = np.random.default_rng(13)
+    tasks, m, n, k, mod = 40, 96, 48, 100, 251  # two launches of padded tasks
+    a = rng.integers(-125, 126, (tasks, m, k)).astype(np.int8)
+    b = rng.integers(-125, 126, (tasks, k, n)).astype(np.int8)
+    d_a, d_b = dev(a), dev(b)
+    d_c = torch.empty((tasks, m, n), dtype=torch.int8, device="cuda")
+    pa = (C.c_void_p * tasks)(*[d_a[t].data_ptr() for t in range(tasks)])
+    pb = (C.c_void_p * tasks)(*[d_b[t].data_ptr() for t in range(tasks)])
+    pc = (C.c_void_p * tasks)(*[d_c[t].data_ptr() for t in range(tasks)])
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    sb = lib.rns8_cuda_gemm_finite_u8_scratch_bytes(0, m, n, k, tasks)
+    assert sb > 0
+    scratch = torch.empty(sb, dtype=torch.uint8, device="cuda")
+    assert lib.rns8_cuda_gemm_finite_u8_grouped_device(0, pa, pb, pc, tasks, m, n, k, mod, 0, scratch.data_ptr(), sb,
+                                                       status.data_ptr(), stream()) == OK
+    torch.cuda.synchronize()
+    assert int(status[0].item()) == 0
+    got = host(d_c)
+    for t in range(0, tasks, 7):
+        np.testing.assert_array_equal(got[t], oracle.ring_gemm(a[t], b[t], mod))
+
+
 @pytest.mark.parametrize("k", [65536, 65536 + 128, 2 * 65536 + 256])
 def test_plane_gemm_k_longer_than_safe_block(lib, oracle, k):
     # Worst-case magnitudes: every product is (-128)(-128) on the 256 plane.
