@@ -127,6 +127,11 @@ __global__ void __launch_bounds__(256) pack_scalar_kernel(const T* __restrict__ 
 
 template <int P, typename T>
 cudaError_t launch_pack(const T* src, int64_t rows, int64_t cols, int64_t ld, int8_t* planes, cudaStream_t stream) {
+  if (ld == cols) {  // compact source: one long row, so any column count can take the vector path
+    cols *= rows;
+    ld = cols;
+    rows = 1;
+  }
   const bool vec = (cols % 8 == 0) && (ld % 2 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(planes) % 8 == 0);
   const int64_t work = vec ? rows * (cols / 8) : rows * cols;
@@ -251,6 +256,11 @@ cudaError_t launch_subset(const T* src, int64_t rows, int64_t cols, int64_t ld, 
                           uint32_t count, int8_t* planes, cudaStream_t stream) {
   constexpr bool kSigned = static_cast<T>(-1) < 0;
   const SubsetConsts c = subset_consts<kSigned>(plane_index, count);
+  if (ld == cols) {  // compact source: one long row
+    cols *= rows;
+    ld = cols;
+    rows = 1;
+  }
   const bool vec = (cols % 8 == 0) && (ld % 2 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(planes) % 8 == 0);
   const int64_t work = vec ? rows * (cols / 8) : rows * cols;
