@@ -50,7 +50,10 @@ RNS8_API rns8_status rns8_cuda_pack_u64_device(int device_id, const uint64_t* d_
 RNS8_API rns8_status rns8_cuda_pack_finite_u8_device(int device_id, const uint8_t* d_src, int64_t rows, int64_t cols,
                                                      int64_t ld, uint16_t modulus, int8_t* d_residues, void* stream);
 
-/* Scratch bytes the plane GEMM needs for split-K on this shape (0 = none). */
+/* Scratch bytes the plane GEMM needs on this shape (0 = none): split-K sums,
+ * and, when K or N is not a multiple of 16, the zero-padded plane copies that
+ * let such shapes run on the tensor cores (given less, they run on the CUDA
+ * cores). */
 RNS8_API uint64_t rns8_cuda_gemm_rns_scratch_bytes(int device_id, int64_t m, int64_t n, int64_t k, uint32_t prefix);
 
 /* Per plane p < prefix: C_p = (A_p x B_p) mod m_p, centered. A is m x k, B is
