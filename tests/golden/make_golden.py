@@ -129,6 +129,33 @@ def reference_kats() -> dict:
         "m": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "A": [str(v) for v in wa], "B": [str(v) for v in wb],
         "expected": [[str(sum(wa[r * lda + q] * wb[q * ldb + c] for q in range(k)) % 2**64) for c in range(n)]
                      for r in range(m)]}
+    # Exact-wide fixed-width limb boundaries: (prefix, signed, value, limbs) ->
+    # "range" or the little-endian limbs (two's complement when signed).
+    def limbs_of(v: int, count: int) -> list[str]:
+        u = v % (1 << (64 * count))
+        return [str((u >> (64 * l)) & (2**64 - 1)) for l in range(count)]
+
+    half3, half20 = prod[3] // 2, prod[20] // 2
+    cases = [
+        [3, True, str(half3), 1, limbs_of(-half3, 1)],           # centered half-open: M/2 -> -M/2
+        [20, True, str(half20), 2, "range"],
+        [20, True, str(half20), 3, limbs_of(-half20, 3)],
+        [20, True, str(2**63 - 1), 1, limbs_of(2**63 - 1, 1)],
+        [20, True, str(-(2**63)), 1, limbs_of(-(2**63), 1)],
+        [20, True, "-1", 1, limbs_of(-1, 1)],
+        [20, True, str(2**63), 1, "range"],
+        [20, True, str(-(2**63) - 1), 1, "range"],
+        [20, True, "-1", 32, limbs_of(-1, 32)],
+        [20, False, str(2**64 - 1), 1, limbs_of(2**64 - 1, 1)],
+        [20, False, str(2**64), 1, "range"],
+        [20, False, str(2**64), 2, limbs_of(2**64, 2)],
+        [20, False, "1", 32, limbs_of(1, 32)],
+        [20, False, str(2**127), 1, "range"],
+        [20, False, str(2**127), 2, limbs_of(2**127, 2)],
+        [20, False, str(2**127), 32, limbs_of(2**127, 32)],
+    ]
+    kats["exact_wide_limb_boundaries"] = {"source": "tests/unit/test_exact_wide_limb_boundary_cases.inc:1-127",
+                                          "cases": cases}
     # Expected values for the 2x3x4 ring GEMM KAT.
     A = np.array(kats["ring_gemm_2x3x4"]["A"]).reshape(2, 4)
     B = np.array(kats["ring_gemm_2x3x4"]["B"]).reshape(4, 3)

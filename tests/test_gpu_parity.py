@@ -9,6 +9,8 @@ products recomputed with limb-split fp64 GEMMs).
 """
 
 import ctypes as C
+import json
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -18,6 +20,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 OK, RANGE = 0, 5
+KATS = json.loads((Path(__file__).resolve().parent / "golden" / "reference_kats.json").read_text())
 LADDER = [256, 255, 253, 251, 247, 239, 233, 229, 227, 223, 217, 211, 199, 197, 193, 191, 181, 179, 173, 167]
 
 
@@ -512,6 +515,33 @@ def test_export_limbs_near_half_range(lib, oracle, prefix, limbs):
         assert (RANGE if int(status[0].item()) else OK) == ost, (signed, prefix, limbs)
         if ost == OK:
             np.testing.assert_array_equal(host(d_out, np.uint64), owant)
+
+
+@pytest.mark.parametrize("case", KATS["exact_wide_limb_boundaries"]["cases"])
+@pytest.mark.parametrize("cells", [4, 1])  # the 4-cell vector kernel and the one-cell kernel
+def test_export_limbs_reference_boundaries(lib, case, cells):
+    """The reference's exact-wide limb boundary answers on the GPU export; on a
+    range error the destination keeps its bytes."""
+    prefix, signed, value, limbs, want = case
+
+    def centered(v, m):
+        r = v % m
+        return r - m if r >= (m + 1) // 2 else r
+    planes = np.array([[[centered(int(value), m)] * cells] for m in LADDER[:prefix]], np.int8)
+    d_p = dev(planes)
+    sentinel = -0x5A5A5A5A5A5A5A5B
+    d_out = torch.full((1, cells, limbs), sentinel, dtype=torch.int64, device="cuda")
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    assert lib.rns8_cuda_export_limbs_device(0, d_p.data_ptr(), 1, cells, prefix, 1 if signed else 0, limbs,
+                                             d_out.data_ptr(), cells, status.data_ptr(), stream()) == OK
+    torch.cuda.synchronize()
+    got = host(d_out, np.uint64)
+    if want == "range":
+        assert int(status[0].item()) == RANGE
+    else:
+        assert int(status[0].item()) == 0
+        for c in range(cells):
+            assert [int(v) for v in got[0, c]] == [int(v) for v in want]
 
 
 # ---- public C ABI: the whole path ----------------------------------------------------

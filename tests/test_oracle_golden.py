@@ -282,6 +282,30 @@ def test_exact_wide_limbs_round_trip(oracle):
     assert st == RANGE  # products of full-range int64 need more than 64 bits
 
 
+def limb_boundary_planes(prefix: int, value: int, cells: int) -> np.ndarray:
+    """Centered residue planes (prefix x 1 x cells) of one value in every cell."""
+    def centered(v, m):
+        r = v % m
+        return r - m if r >= (m + 1) // 2 else r
+    return np.array([[[centered(value, m)] * cells] for m in LADDER_ALL[:prefix]], np.int8)
+
+
+LADDER_ALL = KATS["ladder"]["moduli"]
+
+
+@pytest.mark.parametrize("case", KATS["exact_wide_limb_boundaries"]["cases"])
+def test_exact_wide_limb_boundaries(oracle, case):
+    """test_exact_wide_limb_boundary_cases.inc:1-127: centered half-open
+    representative, one-limb edges, overflow and 32-limb widths."""
+    prefix, signed, value, limbs, want = case
+    st, got = oracle.export_limbs(limb_boundary_planes(prefix, int(value), 1), prefix, limbs, signed)
+    if want == "range":
+        assert st == RANGE
+    else:
+        assert st == OK
+        assert [int(v) for v in got[0, 0]] == [int(v) for v in want]
+
+
 # ---- WRAP_U64_MOD_2_64 -------------------------------------------------------------
 def test_wrap64_public_kat(oracle):
     """Inputs of the reference's public wrap64 differential test (padded lda/ldb)."""
