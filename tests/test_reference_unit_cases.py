@@ -1,0 +1,96 @@
+"""The reference's bounded-GEMM unit cases
+(tests/unit/test_bounded_gemm_basic_cases.inc:170-358) through this library's
+public C ABI: input-range descriptors (bound = K * lhs_bound * rhs_bound),
+their validation, too-small bounds leaving padded outputs untouched, and plan
+ranges. Descriptor validation runs on the host (rns8_cuda_plan_probe, no GPU);
+the products run on the GPU."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+OK, INVALID, RANGE = 0, 1, 5
+
+
+@pytest.fixture(scope="module")
+def r8():
+    import rns8_b200
+
+    rns8_b200.lib()
+    return rns8_b200
+
+
+def desc(r8, semantics, m, n, k, bound=0, bound_kind=None, lhs=0, rhs=0, max_prefix=0, finite_modulus=0):
+    S, BK = r8.Semantics, r8.BoundKind
+    if bound_kind is None:
+        bound_kind = BK.GLOBAL_MAX_ABS if semantics == S.BOUNDED_I64 else BK.GLOBAL_MAX_UNSIGNED
+    return r8.gemm_desc(semantics, bound_kind, m, n, k, bound=bound, lhs_bound=lhs, rhs_bound=rhs,
+                        max_prefix=max_prefix, finite_modulus=finite_modulus)
+
+
+def test_input_range_descriptor_validation(r8):
+    S, BK = r8.Semantics, r8.BoundKind
+    st, sel, req, eb = r8.api.plan_probe(desc(r8, S.BOUNDED_I64, 2, 2, 3, bound_kind=BK.INPUT_RANGE_AND_K, lhs=7,
+                                              rhs=11))
+    assert st == OK and eb == 3 * 7 * 11 and sel == req
+    assert r8.api.plan_probe(desc(r8, S.BOUNDED_U64, 1, 1, 4, bound=1, bound_kind=BK.INPUT_RANGE_AND_K, lhs=1,
+                                  rhs=1))[0] == INVALID  # a stale global bound
+    assert r8.api.plan_probe(desc(r8, S.BOUNDED_U64, 1, 1, 4, bound_kind=BK.INPUT_RANGE_AND_K, lhs=2**64 - 1,
+                                  rhs=2))[0] == RANGE  # K * lhs * rhs overflows the u64 contract
+    assert r8.api.plan_probe(desc(r8, S.BOUNDED_I64, 1, 1, 4, bound_kind=BK.INPUT_RANGE_AND_K, lhs=2**63,
+                                  rhs=2))[0] == RANGE
+    assert r8.api.plan_probe(desc(r8, S.BOUNDED_U64, 1, 1, 1, bound=1, lhs=1))[0] == INVALID  # stale lhs field
+    assert r8.api.plan_probe(desc(r8, S.FINITE_RING_U8, 1, 1, 1, bound_kind=BK.NONE, lhs=1,
+                                  finite_modulus=255))[0] == INVALID
+    # bounded plan creation rejects insufficient prefix range (:350-358)
+    assert r8.api.plan_probe(desc(r8, S.BOUNDED_I64, 1, 1, 1, bound=2**63 - 1, max_prefix=8))[0] == RANGE
+
+
+@pytest.mark.gpu
+def test_input_range_persistent_and_oneshot(r8):
+    S, BK = r8.Semantics, r8.BoundKind
+    with r8.Context(0) as ctx:
+        d = desc(r8, S.BOUNDED_I64, 2, 2, 3, bound_kind=BK.INPUT_RANGE_AND_K, lhs=7, rhs=11)
+        plan = r8.Plan(ctx, d)
+        info = plan.schedule_info()
+        assert info.bound_kind == BK.INPUT_RANGE_AND_K and info.effective_bound == 3 * 7 * 11
+        assert info.lhs_bound == 7 and info.rhs_bound == 11
+        assert info.bound_contract.decode() == "input_range_and_k_derived_output_bound"
+        assert info.max_selected_prefix == info.min_required_prefix
+        a, b, c = (r8.Matrix.for_plan(ctx, plan, role) for role in "abc")
+        ws = r8.Workspace(ctx, plan)
+        a.pack_i64(np.array([[7, -2, 3], [-1, 4, -5]], np.int64), source_version=10)
+        b.pack_i64(np.array([[2, -3], [6, 1], [-4, 5]], np.int64), source_version=11)
+        r8.gemm_rns(ctx, plan, a, b, c, ws)
+        assert r8.export_i64(ctx, plan, c).ravel().tolist() == [-10, -8, 42, -18]
+        for h in (a, b, c, ws, plan):
+            h.close()
+        one = r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 1, 2, 2, bound_kind=BK.INPUT_RANGE_AND_K, lhs=5, rhs=6),
+                                  np.array([[5, -4]], np.int64), np.array([[6, -3], [2, 1]], np.int64))
+        assert one.ravel().tolist() == [22, -19]
+        one = r8.gemm_u64_oneshot(ctx, desc(r8, S.BOUNDED_U64, 2, 1, 2, bound_kind=BK.INPUT_RANGE_AND_K, lhs=9, rhs=8),
+                                  np.array([[9, 1], [2, 3]], np.uint64), np.array([[8], [7]], np.uint64))
+        assert one.ravel().tolist() == [79, 37]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("signed", [True, False])
+def test_too_small_bound_keeps_padded_output(r8, signed):
+    """:317-348 — a valid but too small global bound: RANGE_ERROR and every
+    element of the padded output (ldc = 4 for n = 2) keeps its sentinel."""
+    S = r8.Semantics
+    with r8.Context(0) as ctx:
+        if signed:
+            A = np.array([[6], [-6]], np.int64)
+            B = np.array([[7, -7, 999]], np.int64)[:, :2]
+            sentinel, dtype, fn = -0x123456789, np.int64, r8.gemm_i64_oneshot
+        else:
+            A = np.array([[6], [8]], np.uint64)
+            B = np.array([[7, 1, 999]], np.uint64)[:, :2]
+            sentinel, dtype, fn = 0xBADC0FFEE0DDF00D, np.uint64, r8.gemm_u64_oneshot
+        C = np.full((2, 4), sentinel, dtype)
+        with pytest.raises(r8.Error) as err:
+            fn(ctx, desc(r8, S.BOUNDED_I64 if signed else S.BOUNDED_U64, 2, 2, 1, bound=41), A, B, out=C[:, :2])
+        assert err.value.status == r8.Status.RANGE_ERROR
+        assert (C == dtype(sentinel)).all()
