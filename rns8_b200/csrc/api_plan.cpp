@@ -449,16 +449,18 @@ uint64_t next_matrix_id() {
   return next.fetch_add(1, std::memory_order_relaxed);
 }
 
+// The schedule info's bound-contract name (api_plan_contract_names.inc:39-52):
+// how the plan's output bound was obtained, not the bound kind's own name.
 static const char* bound_contract_name(const rns8_plan& plan) {
   switch (plan.desc.bound_kind) {
-    case RNS8_BOUND_NONE: return "none";
-    case RNS8_BOUND_GLOBAL_MAX_ABS: return "global_max_abs";
-    case RNS8_BOUND_GLOBAL_MAX_UNSIGNED: return "global_max_unsigned";
-    case RNS8_BOUND_PER_TILE_MAX_ABS: return "per_tile_max_abs";
-    case RNS8_BOUND_PER_TILE_MAX_UNSIGNED: return "per_tile_max_unsigned";
-    case RNS8_BOUND_INPUT_RANGE_AND_K: return "input_range_and_k";
+    case RNS8_BOUND_INPUT_RANGE_AND_K: return "input_range_and_k_derived_output_bound";
+    case RNS8_BOUND_PER_TILE_MAX_ABS:
+    case RNS8_BOUND_PER_TILE_MAX_UNSIGNED: return "per_tile_output_bounds";
+    case RNS8_BOUND_GLOBAL_MAX_ABS:
+    case RNS8_BOUND_GLOBAL_MAX_UNSIGNED: return "global_output_bound";
+    case RNS8_BOUND_NONE: break;
   }
-  return "unknown";
+  return "not_applicable";
 }
 
 }  // namespace rns8host
@@ -637,12 +639,15 @@ extern "C" rns8_status rns8_get_plan_backend_info(const rns8_plan* plan, rns8_pl
     out->accumulator_max_product = 16384;
     out->accumulator_uses_int32_inner_product = 1;
     out->accumulator_safe_for_k_block = 1;
-    set_text(out->accumulator_input_domain, sizeof(out->accumulator_input_domain), "centered_int8_residue");
-    set_text(out->accumulator_signedness, sizeof(out->accumulator_signedness), "signed");
+    // Contract vocabulary of the accumulator fields (api_plan_contract_names.inc:462-530).
+    const bool finite_plan = uses_finite_storage(plan->desc.semantics);
+    set_text(out->accumulator_input_domain, sizeof(out->accumulator_input_domain),
+             finite_plan ? "centered_i8_finite_u8_residues" : "centered_i8_rns_residue_planes");
+    set_text(out->accumulator_signedness, sizeof(out->accumulator_signedness), "signed_i8x_signed_i8");
     set_text(out->accumulator_type, sizeof(out->accumulator_type), "int32");
     set_text(out->accumulator_modulus_policy, sizeof(out->accumulator_modulus_policy),
-             "reduce_modulo_plane_modulus_every_65536_products");
-    set_text(out->accumulator_safety_status, sizeof(out->accumulator_safety_status), "proven_int32_safe");
+             finite_plan ? "finite_u8_modulus" : "selected_rns_modulus_ladder");
+    set_text(out->accumulator_safety_status, sizeof(out->accumulator_safety_status), "safe_int32_k_block_split");
     if (plan->desc.semantics == RNS8_WRAP_U64_MOD_2_64) {
       // 36 unsigned byte-pair products on the low 8 diagonals; a 16384-product
       // K block keeps diagonals 0..3 exact in 32 bits, diagonals 4..7 only
@@ -656,12 +661,13 @@ extern "C" rns8_status rns8_get_plan_backend_info(const rns8_plan* plan, rns8_pl
       out->accumulator_max_lhs_abs = 255;
       out->accumulator_max_rhs_abs = 255;
       out->accumulator_max_product = 65025;
-      set_text(out->accumulator_input_domain, sizeof(out->accumulator_input_domain), "unsigned_byte_limb");
-      set_text(out->accumulator_signedness, sizeof(out->accumulator_signedness), "unsigned");
-      set_text(out->accumulator_type, sizeof(out->accumulator_type), "uint32");
+      set_text(out->accumulator_input_domain, sizeof(out->accumulator_input_domain), "uint8_byte_limb_pairs");
+      set_text(out->accumulator_signedness, sizeof(out->accumulator_signedness), "unsigned_byte_limb");
+      set_text(out->accumulator_type, sizeof(out->accumulator_type), "uint32_low_diagonal_then_uint64_carry");
       set_text(out->accumulator_modulus_policy, sizeof(out->accumulator_modulus_policy),
-               "low_64_bits_of_36_byte_pair_diagonals");
-      set_text(out->accumulator_safety_status, sizeof(out->accumulator_safety_status), "proven_uint32_safe");
+               "mod_2_64_wraparound_byte_limb");
+      set_text(out->accumulator_safety_status, sizeof(out->accumulator_safety_status),
+               "safe_uint32_byte_limb_gemm36_k_block");
     }
     return RNS8_SUCCESS;
   });
@@ -682,8 +688,9 @@ extern "C" rns8_status rns8_get_plan_packing_info(const rns8_plan* plan, rns8_pl
     out->uses_matrix_engine_pack_layout = 0;
     out->flags = RNS8_PLAN_PACKING_SOURCE_VERSIONED_INPUTS | RNS8_PLAN_PACKING_SAME_SOURCE_VERSION_PACK_ELISION;
     const bool finite = uses_finite_storage(plan->desc.semantics);
-    out->input_domain = RNS8_OUTPUT_DOMAIN_RNS_RESIDUE;
-    out->output_domain = finite ? RNS8_OUTPUT_DOMAIN_FINITE_U8 : RNS8_OUTPUT_DOMAIN_RNS_RESIDUE;
+    // Inputs and output live in the plan's storage domain (api_plan_contract_names.inc:277-302).
+    out->input_domain = finite ? RNS8_OUTPUT_DOMAIN_FINITE_U8 : RNS8_OUTPUT_DOMAIN_RNS_RESIDUE;
+    out->output_domain = out->input_domain;
     out->output_device_current = 1;
     out->next_op_flags = RNS8_NEXT_OP_FINAL_EXPORT | (finite ? 0u : static_cast<uint32_t>(RNS8_NEXT_OP_RNS_GEMM));
     rns8cuda::PlaneGemmTask task{reinterpret_cast<const int8_t*>(256), reinterpret_cast<const int8_t*>(256),
@@ -703,8 +710,8 @@ extern "C" rns8_status rns8_get_plan_packing_info(const rns8_plan* plan, rns8_pl
       out->next_op_flags = RNS8_NEXT_OP_FINAL_EXPORT;
       out->accumulator_workspace_bytes = static_cast<uint64_t>(plan->desc.m) * plan->desc.n * 8;
       out->total_transient_workspace_bytes = out->accumulator_workspace_bytes;
-      set_text(out->input_domain_name, sizeof(out->input_domain_name), "wrap64_byte_limb");
-      set_text(out->output_domain_name, sizeof(out->output_domain_name), "wrap64_byte_limb");
+      set_text(out->input_domain_name, sizeof(out->input_domain_name), "wrap64_byte_limb_current");
+      set_text(out->output_domain_name, sizeof(out->output_domain_name), "wrap64_byte_limb_current");
       set_text(out->next_op_hint, sizeof(out->next_op_hint), "export_wrap_u64 or chain wrap gemm");
       set_text(out->a_layout_version, sizeof(out->a_layout_version), "limb_major_compact_row_major_u8_v1");
       set_text(out->b_layout_version, sizeof(out->b_layout_version), "limb_major_compact_row_major_u8_v1");
@@ -712,8 +719,10 @@ extern "C" rns8_status rns8_get_plan_packing_info(const rns8_plan* plan, rns8_pl
       set_text(out->detail, sizeof(out->detail), "eight unsigned byte planes in HBM; 36 byte-pair tensor-core products");
       return RNS8_SUCCESS;
     }
-    set_text(out->input_domain_name, sizeof(out->input_domain_name), "rns_residue");
-    set_text(out->output_domain_name, sizeof(out->output_domain_name), finite ? "finite_u8" : "rns_residue");
+    set_text(out->input_domain_name, sizeof(out->input_domain_name),
+             finite ? "finite_u8_current" : "rns_residue_current");
+    set_text(out->output_domain_name, sizeof(out->output_domain_name),
+             finite ? "finite_u8_current" : "rns_residue_current");
     set_text(out->next_op_hint, sizeof(out->next_op_hint), finite ? "export_finite_u8" : "export or chain rns gemm");
     set_text(out->a_layout_version, sizeof(out->a_layout_version), "modulus_major_compact_row_major_i8_v1");
     set_text(out->b_layout_version, sizeof(out->b_layout_version), "modulus_major_compact_row_major_i8_v1");

@@ -58,6 +58,13 @@ def test_input_range_persistent_and_oneshot(r8):
         assert info.lhs_bound == 7 and info.rhs_bound == 11
         assert info.bound_contract.decode() == "input_range_and_k_derived_output_bound"
         assert info.max_selected_prefix == info.min_required_prefix
+        # Contract vocabulary of the info queries (api_plan_contract_names.inc:39-52, 462-530).
+        bi = plan.backend_info()
+        assert bi.accumulator_input_domain.decode() == "centered_i8_rns_residue_planes"
+        assert bi.accumulator_signedness.decode() == "signed_i8x_signed_i8"
+        assert bi.accumulator_type.decode() == "int32"
+        assert bi.accumulator_modulus_policy.decode() == "selected_rns_modulus_ladder"
+        assert bi.accumulator_safety_status.decode() == "safe_int32_k_block_split"
         a, b, c = (r8.Matrix.for_plan(ctx, plan, role) for role in "abc")
         ws = r8.Workspace(ctx, plan)
         a.pack_i64(np.array([[7, -2, 3], [-1, 4, -5]], np.int64), source_version=10)
