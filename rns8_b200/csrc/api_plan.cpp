@@ -419,6 +419,8 @@ rns8_status build_plan(const rns8_gemm_desc& desc, rns8_plan& plan) {
   plan.prefix = prefix;
   plan.tile_rows = (static_cast<uint64_t>(plan.desc.m) + plan.desc.tile_m - 1) / plan.desc.tile_m;
   plan.tile_cols = (static_cast<uint64_t>(plan.desc.n) + plan.desc.tile_n - 1) / plan.desc.tile_n;
+  // A schedule whose tile count overflows is a range error (api_plan_schedule.inc:113-118).
+  if (plan.tile_cols != 0 && plan.tile_rows > UINT64_MAX / plan.tile_cols) return RNS8_RANGE_ERROR;
   plan.tile_count = plan.tile_rows * plan.tile_cols;
   const i256 required_range = schedule_required_range(plan.desc);
   plan.range_bit_length = bit_length(required_range);

@@ -47,6 +47,19 @@ def test_input_range_descriptor_validation(r8):
     assert r8.api.plan_probe(desc(r8, S.BOUNDED_I64, 1, 1, 1, bound=2**63 - 1, max_prefix=8))[0] == RANGE
 
 
+def test_per_tile_plan_with_overflowing_tile_count(r8):
+    """test_api_validation_cases.inc:59-71: a per-tile plan over INT64_MAX^2
+    cells is a range error, before any tile bound is read."""
+    import ctypes as C
+
+    S, BK = r8.Semantics, r8.BoundKind
+    d = r8.gemm_desc(S.BOUNDED_I64, BK.PER_TILE_MAX_ABS, 2**63 - 1, 2**63 - 1, 1, tile_m=64, tile_n=64)
+    tb = (C.c_uint64 * 1)(1)
+    d.tile_bounds = C.cast(tb, C.POINTER(C.c_uint64))
+    d.tile_bounds_count = 2**64 - 1
+    assert r8.api.plan_probe(d)[0] == RANGE
+
+
 @pytest.mark.gpu
 def test_input_range_persistent_and_oneshot(r8):
     S, BK = r8.Semantics, r8.BoundKind
