@@ -149,11 +149,12 @@ class Plan(_Handle):
 class Matrix(_Handle):
     _destroy = "rns8_destroy_matrix"
 
-    def __init__(self, ctx: Context, rows: int, cols: int, semantics, bound_kind, max_prefix: int = 0):
+    def __init__(self, ctx: Context, rows: int, cols: int, semantics, bound_kind, max_prefix: int = 0,
+                 tile_m: int = 0, tile_n: int = 0):
         super().__init__()
         desc = abi.MatrixDesc(rows=rows, cols=cols, logical_ld=cols, semantics=int(semantics),
                               logical_layout=int(abi.Layout.ROW_MAJOR), bound_kind=int(bound_kind),
-                              max_prefix=max_prefix)
+                              max_prefix=max_prefix, tile_m=tile_m, tile_n=tile_n)
         self.ctx = ctx
         self.rows, self.cols = rows, cols
         check(lib().rns8_create_matrix(ctx.handle, C.byref(desc), C.byref(self.handle)), "rns8_create_matrix")
@@ -168,7 +169,11 @@ class Matrix(_Handle):
         bk = BoundKind(d.bound_kind)
         if bk == BoundKind.INPUT_RANGE_AND_K:
             bk = BoundKind.GLOBAL_MAX_ABS if sem == Semantics.BOUNDED_I64 else BoundKind.GLOBAL_MAX_UNSIGNED
-        return cls(ctx, rows, cols, sem, bk, plan.prefix)
+        # Wrap64 and per-tile matrices carry the plan's tile dimensions.
+        tiled = sem == Semantics.WRAP_U64_MOD_2_64 or bk in (BoundKind.PER_TILE_MAX_ABS,
+                                                             BoundKind.PER_TILE_MAX_UNSIGNED)
+        tm, tn = (plan.desc.tile_m, plan.desc.tile_n) if tiled else (0, 0)
+        return cls(ctx, rows, cols, sem, bk, plan.prefix, tm, tn)
 
     def pack_i64(self, src: np.ndarray, source_version: int = 0) -> None:
         src = np.asarray(src)

@@ -70,7 +70,7 @@ bool plan_context_ok(const rns8_context& ctx, const rns8_plan& plan) {
 // validate_plan_context_workspace (api_workspace_contracts_resources.inc:222-247).
 rns8_status validate_workspace(const rns8_context& ctx, const rns8_plan& plan, const rns8_workspace& ws) {
   if (!plan_context_ok(ctx, plan) || ws.backend != plan.backend) return RNS8_INVALID_ARGUMENT;
-  if (ws.semantics != plan.desc.semantics) return RNS8_INVALID_ARGUMENT;
+  if (ws.semantics != plan.desc.semantics || ws.bound_kind != plan.desc.bound_kind) return RNS8_INVALID_ARGUMENT;
   if (ws.m != plan.desc.m || ws.n != plan.desc.n || ws.k != plan.desc.k || ws.prefix != plan.prefix)
     return RNS8_WORKSPACE_TOO_SMALL;
   if (ws.plan_fingerprint != plan.fingerprint || ws.device_id != ctx.device_id) return RNS8_INVALID_ARGUMENT;
@@ -78,12 +78,17 @@ rns8_status validate_workspace(const rns8_context& ctx, const rns8_plan& plan, c
 }
 
 // matrix_descriptor_matches (api_matrix_currentness_storage.inc:1-23).
+// Wrap64 and per-tile matrices also carry the plan's tile dimensions.
 bool descriptor_matches(const rns8_matrix& mtx, rns8_semantics s, rns8_bound_kind bk, int64_t rows, int64_t cols,
-                        uint32_t prefix) {
+                        uint32_t prefix, const rns8_plan& plan) {
   if (mtx.desc.semantics != s || mtx.desc.bound_kind != bk || mtx.desc.rows != rows || mtx.desc.cols != cols ||
-      mtx.desc.logical_layout != RNS8_LAYOUT_ROW_MAJOR || mtx.prefix < prefix || mtx.desc.max_prefix < prefix)
+      mtx.desc.logical_layout != RNS8_LAYOUT_ROW_MAJOR || mtx.desc.logical_ld < mtx.desc.cols ||
+      mtx.desc.flags != 0 || mtx.prefix < prefix || mtx.desc.max_prefix < prefix)
     return false;
   if (prefix == 0 && (mtx.prefix != 0 || mtx.desc.max_prefix != 0)) return false;
+  if ((s == RNS8_WRAP_U64_MOD_2_64 || bk == RNS8_BOUND_PER_TILE_MAX_ABS || bk == RNS8_BOUND_PER_TILE_MAX_UNSIGNED) &&
+      (mtx.desc.tile_m != plan.desc.tile_m || mtx.desc.tile_n != plan.desc.tile_n))
+    return false;
   return mtx.residues != nullptr;
 }
 
@@ -95,8 +100,8 @@ rns8_status validate_rns_operands(const rns8_context& ctx, const rns8_plan& plan
   const rns8_bound_kind bk = storage_bound_kind(plan);
   const auto& d = plan.desc;
   const uint32_t sp = plan.storage_prefix();
-  if (!descriptor_matches(A, d.semantics, bk, d.m, d.k, sp) || !descriptor_matches(B, d.semantics, bk, d.k, d.n, sp) ||
-      !descriptor_matches(C, d.semantics, bk, d.m, d.n, sp))
+  if (!descriptor_matches(A, d.semantics, bk, d.m, d.k, sp, plan) ||
+      !descriptor_matches(B, d.semantics, bk, d.k, d.n, sp, plan) || !descriptor_matches(C, d.semantics, bk, d.m, d.n, sp, plan))
     return RNS8_INVALID_ARGUMENT;
   if (!A.device_current || !B.device_current) return RNS8_INVALID_ARGUMENT;
   if (exact_wide(d.semantics) && (&A == &C || &B == &C)) return RNS8_INVALID_ARGUMENT;
@@ -111,9 +116,9 @@ rns8_status validate_finite_operands(const rns8_context& ctx, const rns8_plan& p
   if (A.device_id != ctx.device_id || B.device_id != ctx.device_id || C.device_id != ctx.device_id)
     return RNS8_INVALID_ARGUMENT;
   const auto& d = plan.desc;
-  if (!descriptor_matches(A, d.semantics, RNS8_BOUND_NONE, d.m, d.k, 0) ||
-      !descriptor_matches(B, d.semantics, RNS8_BOUND_NONE, d.k, d.n, 0) ||
-      !descriptor_matches(C, d.semantics, RNS8_BOUND_NONE, d.m, d.n, 0))
+  if (!descriptor_matches(A, d.semantics, RNS8_BOUND_NONE, d.m, d.k, 0, plan) ||
+      !descriptor_matches(B, d.semantics, RNS8_BOUND_NONE, d.k, d.n, 0, plan) ||
+      !descriptor_matches(C, d.semantics, RNS8_BOUND_NONE, d.m, d.n, 0, plan))
     return RNS8_INVALID_ARGUMENT;
   if (!A.device_current || !B.device_current || A.finite_modulus != modulus || B.finite_modulus != modulus)
     return RNS8_INVALID_ARGUMENT;
@@ -237,6 +242,8 @@ rns8_status validate_wrap_operands(const rns8_context& ctx, const rns8_plan& pla
   const auto& d = plan.desc;
   if (!wrap_storage_ok(A, d.m, d.k) || !wrap_storage_ok(B, d.k, d.n) || !wrap_storage_ok(C, d.m, d.n))
     return RNS8_INVALID_ARGUMENT;
+  for (const rns8_matrix* mtx : {&A, &B, &C})  // wrap64 matrices carry the plan's tile dimensions
+    if (mtx->desc.tile_m != d.tile_m || mtx->desc.tile_n != d.tile_n) return RNS8_INVALID_ARGUMENT;
   if (!A.device_current || !B.device_current) return RNS8_INVALID_ARGUMENT;
   return RNS8_SUCCESS;
 }
@@ -320,7 +327,7 @@ rns8_status validate_rns_export(const rns8_context& ctx, const rns8_plan& plan, 
                                 rns8_semantics semantics) {
   if (!plan_context_ok(ctx, plan) || plan.desc.semantics != semantics) return RNS8_INVALID_ARGUMENT;
   if (C.device_id != ctx.device_id || C.backend != plan.backend) return RNS8_INVALID_ARGUMENT;
-  if (!descriptor_matches(C, semantics, storage_bound_kind(plan), plan.desc.m, plan.desc.n, plan.storage_prefix()))
+  if (!descriptor_matches(C, semantics, storage_bound_kind(plan), plan.desc.m, plan.desc.n, plan.storage_prefix(), plan))
     return RNS8_INVALID_ARGUMENT;
   if (!C.device_current) return RNS8_INVALID_ARGUMENT;
   if (exact_wide(semantics) && C.exact_range_prefix != 0 &&
@@ -914,7 +921,7 @@ extern "C" rns8_status rns8_export_finite_u8(rns8_context* ctx, const rns8_plan*
         !valid_finite_modulus_for_semantics(plan->desc.semantics, modulus) || plan->desc.finite_modulus != modulus)
       return RNS8_INVALID_ARGUMENT;
     if (!plan_context_ok(*ctx, *plan) || Cc->device_id != ctx->device_id) return RNS8_INVALID_ARGUMENT;
-    if (!descriptor_matches(*Cc, plan->desc.semantics, RNS8_BOUND_NONE, plan->desc.m, plan->desc.n, 0) ||
+    if (!descriptor_matches(*Cc, plan->desc.semantics, RNS8_BOUND_NONE, plan->desc.m, plan->desc.n, 0, *plan) ||
         !Cc->device_current || Cc->finite_modulus != modulus)
       return RNS8_INVALID_ARGUMENT;
     rns8_matrix& C = const_cast<rns8_matrix&>(*Cc);

@@ -127,6 +127,7 @@ struct rns8_workspace {
   int device_id = 0;
   uint64_t plan_fingerprint = 0;
   rns8_semantics semantics = RNS8_BOUNDED_I64;
+  rns8_bound_kind bound_kind = RNS8_BOUND_NONE;
   int64_t m = 0, n = 0, k = 0;
   uint32_t prefix = 0;
   rns8host::DevBuf scratch;  // split-K partial sums

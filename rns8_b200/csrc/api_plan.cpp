@@ -268,9 +268,36 @@ uint64_t plan_fingerprint(const rns8_plan& p) {
   mix(p.desc.bound);
   mix(p.prefix);
   mix(p.desc.finite_modulus);
+  mix(p.desc.lhs_bound);
+  mix(p.desc.rhs_bound);
+  mix(p.desc.flags);
   mix(p.desc.tile_m);
   mix(p.desc.tile_n);
   mix(static_cast<uint64_t>(p.device_id));
+  // The schedule a workspace was sized for (plan_workspace_fingerprint,
+  // api_plan_workspace_fingerprint.inc:29-90): same-shape plans with other
+  // tile bounds, zero masks or selected prefixes do not share workspaces.
+  for (uint64_t v : {p.tile_rows, p.tile_cols, p.tile_count}) mix(v);
+  for (uint32_t v : {p.min_required, p.max_required, p.min_selected, p.max_selected, p.group_count,
+                     p.range_bit_length, p.adaptive_prefix, p.adaptive_skip, p.schedule_flags})
+    mix(v);
+  mix(p.zero_a_row_count);
+  mix(p.zero_b_col_count);
+  mix(p.zero_row_col_product_count);
+  mix(p.tile_bounds.size());
+  for (uint64_t b : p.tile_bounds) mix(b);
+  mix(p.zero_a_rows.size());
+  for (uint8_t z : p.zero_a_rows) mix(z);
+  mix(p.zero_b_cols.size());
+  for (uint8_t z : p.zero_b_cols) mix(z);
+  mix(p.tile_schedule.size());
+  for (const rns8_plan_tile_schedule_entry& e : p.tile_schedule) {
+    mix(e.required_prefix);
+    mix(e.selected_prefix);
+    mix(e.group_index);
+    mix(e.range_bit_length);
+    mix(e.flags);
+  }
   return h;
 }
 

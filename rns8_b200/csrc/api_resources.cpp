@@ -330,6 +330,7 @@ extern "C" rns8_status rns8_create_workspace(rns8_context* ctx, const rns8_plan*
     ws->device_id = ctx->device_id;
     ws->plan_fingerprint = plan->fingerprint;
     ws->semantics = plan->desc.semantics;
+    ws->bound_kind = plan->desc.bound_kind;
     ws->m = plan->desc.m;
     ws->n = plan->desc.n;
     ws->k = plan->desc.k;
