@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 
-OK, INVALID, RANGE = 0, 1, 2
+OK, INVALID, RANGE = 0, 1, 5
 I64_MAX = 2**63 - 1
 
 
@@ -87,13 +87,21 @@ def test_export_rejects_outputs_outside_the_plan_contract(r8):
         plan = r8.Plan(ctx, r8.gemm_desc(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 2, 2, 1, bound=100000))
         dst = np.full(4, 5, np.uint64)
         ptr = dst.ctypes.data_as(C.POINTER(C.c_uint64))
+        vals = np.array([[1, 2], [3, 4]], np.uint64)
         c = r8.Matrix(ctx, 2, 2, S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 0)
+        # A fresh matrix is not device-current: this backend's export refuses
+        # it, as the reference's device-resident backends do.
+        assert lib.rns8_export_u64(ctx.handle, plan.handle, c.handle, ptr, 2) == INVALID
+        c.pack_u64(vals)
         assert lib.rns8_export_u64(ctx.handle, plan.handle, c.handle, ptr, 2) == OK
-        assert not dst.any()  # a fresh matrix holds zero residues
+        assert dst.tolist() == [1, 2, 3, 4]
         dst[:] = 5
+        # Device-current matrices outside the plan's contract.
         wrong_prefix = r8.Matrix(ctx, 2, 2, S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 1)
+        wrong_prefix.pack_u64(vals)
         assert lib.rns8_export_u64(ctx.handle, plan.handle, wrong_prefix.handle, ptr, 2) == INVALID
         wrong_kind = r8.Matrix(ctx, 2, 2, S.BOUNDED_U64, BK.PER_TILE_MAX_UNSIGNED, 0)
+        wrong_kind.pack_u64(vals)
         assert lib.rns8_export_u64(ctx.handle, plan.handle, wrong_kind.handle, ptr, 2) == INVALID
         assert (dst == 5).all()
         for h in (wrong_kind, wrong_prefix, c, plan):

@@ -49,6 +49,41 @@ def test_plan_descriptor_cases(r8):
     assert probe(r8, gdesc(r8, S.FINITE_RING_U8, BK.GLOBAL_MAX_UNSIGNED, B.ROCWMMA)) == INVALID
 
 
+def BOUNDED_KINDS(BK):
+    return (BK.GLOBAL_MAX_ABS, BK.GLOBAL_MAX_UNSIGNED, BK.PER_TILE_MAX_ABS, BK.PER_TILE_MAX_UNSIGNED,
+            BK.INPUT_RANGE_AND_K)
+
+
+def test_contract_selection_descriptors(r8):
+    """test_semantics_contract_selection_cases.inc:1-111: exact-wide plans
+    take BOUND_NONE with no bound, no stray tile bounds (pointer or count),
+    and no bounded-looking CRT metadata; wrap64 plans accept none of the
+    bounded descriptors either, whichever backend is requested."""
+    S, BK, B = r8.Semantics, r8.BoundKind, r8.Backend
+    for sem in (S.EXACT_WIDE_SIGNED, S.EXACT_WIDE_UNSIGNED):
+        d = r8.gemm_desc(sem, BK.NONE, 1, 1, 1, max_prefix=20)
+        assert probe(r8, d) == OK
+        d.bound = 1
+        assert probe(r8, d) == INVALID
+        for bk in BOUNDED_KINDS(BK):
+            d = r8.gemm_desc(sem, bk, 1, 1, 1, bound=2**64 - 1, max_prefix=9, requested_backend=B.CPU_REFERENCE)
+            assert probe(r8, d) == INVALID
+    d = r8.gemm_desc(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 1, 1, 1, bound=1)
+    stale = (C.c_uint64 * 1)(100)
+    d.tile_bounds = C.cast(stale, C.POINTER(C.c_uint64))
+    d.tile_bounds_count = 1
+    assert probe(r8, d) == INVALID
+    d = r8.gemm_desc(S.EXACT_WIDE_UNSIGNED, BK.NONE, 1, 1, 1, max_prefix=20)
+    d.tile_bounds_count = 1
+    assert probe(r8, d) == INVALID
+    for bk in (BK.NONE, BK.GLOBAL_MAX_UNSIGNED, BK.PER_TILE_MAX_ABS, BK.PER_TILE_MAX_UNSIGNED,
+               BK.INPUT_RANGE_AND_K):
+        for backend in (B.CPU_REFERENCE, B.WRAP64_BYTE_LIMB):
+            d = r8.gemm_desc(S.WRAP_U64_MOD_2_64, bk, 1, 1, 1, bound=2**64 - 1, max_prefix=9,
+                             requested_backend=backend)
+            assert probe(r8, d) == INVALID
+
+
 def test_tile_sizes_are_powers_of_two_64_to_512(r8):
     S, BK = r8.Semantics, r8.BoundKind
     assert probe(r8, gdesc(r8, S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, tile_m=256, tile_n=512)) == OK
@@ -90,3 +125,12 @@ def test_matrix_descriptor_cases(r8):
         for bad in (32, 96, 513):
             assert create(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, tile_n=bad) == (INVALID, False)
         assert create(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED)[0] == OK
+        # test_semantics_contract_selection_cases.inc:1-111: exact-wide storage
+        # is unbounded only; bounded-looking exact-wide or wrap64 storage is
+        # refused with no handle.
+        for sem in (S.EXACT_WIDE_SIGNED, S.EXACT_WIDE_UNSIGNED):
+            assert create(sem, BK.NONE, max_prefix=20)[0] == OK
+            for bk in BOUNDED_KINDS(BK):
+                assert create(sem, bk, max_prefix=9) == (INVALID, False)
+        for bk in (BK.NONE, *BOUNDED_KINDS(BK)[1:]):
+            assert create(S.WRAP_U64_MOD_2_64, bk, max_prefix=9) == (INVALID, False)

@@ -114,3 +114,89 @@ def test_too_small_bound_keeps_padded_output(r8, signed):
             fn(ctx, desc(r8, S.BOUNDED_I64 if signed else S.BOUNDED_U64, 2, 2, 1, bound=41), A, B, out=C[:, :2])
         assert err.value.status == r8.Status.RANGE_ERROR
         assert (C == dtype(sentinel)).all()
+
+
+def test_per_tile_contracts_reject_missing_or_inconsistent_bounds(r8):
+    """test_bounded_gemm_per_tile_cases.inc (per-tile bound contracts): no
+    tile bounds, too few, a global bound beside them, and a signed tile bound
+    beyond 2^63 are INVALID_ARGUMENT; a global signed bound of 2^63 + 1
+    likewise (test_bounded_gemm_schedule_cases.inc, int64 min)."""
+    S, BK = r8.Semantics, r8.BoundKind
+    probe = lambda d: r8.api.plan_probe(d)[0]
+    d = r8.gemm_desc(S.BOUNDED_U64, BK.PER_TILE_MAX_UNSIGNED, 65, 65, 1, tile_m=64, tile_n=64)
+    assert probe(d) == INVALID
+    r8.api.set_tile_bounds(d, [7, 1000, 7000000])
+    assert probe(d) == INVALID
+    r8.api.set_tile_bounds(d, [7, 1000, 7000000, 1000000000])
+    d.bound = 1
+    assert probe(d) == INVALID
+    d.bound = 0
+    assert probe(d) == OK
+    s = r8.gemm_desc(S.BOUNDED_I64, BK.PER_TILE_MAX_ABS, 1, 1, 1)
+    r8.api.set_tile_bounds(s, [2**64 - 1])
+    assert probe(s) == INVALID
+    assert probe(desc(r8, S.BOUNDED_I64, 1, 1, 1, bound=2**63 + 1)) == INVALID
+    assert probe(desc(r8, S.BOUNDED_I64, 1, 1, 1, bound=2**63)) == OK
+
+
+def test_per_tile_schedule_collapses_to_fixed_prefix(r8):
+    """test_bounded_gemm_schedule_cases.inc (collapse case): when every tile
+    needs the full nine moduli the schedule is one group at prefix 9, each
+    entry keeps its own range bit length and the grid geometry of a 65 x 65
+    output in 64 x 64 tiles."""
+    import math
+
+    S, BK = r8.Semantics, r8.BoundKind
+    first_full = math.prod(r8.LADDER[:8]) // 2
+    top = 2**63
+    d = r8.gemm_desc(S.BOUNDED_I64, BK.PER_TILE_MAX_ABS, 65, 65, 7, tile_m=64, tile_n=64)
+    r8.api.set_tile_bounds(d, [top, first_full, top, first_full])
+    entries, info = r8.api.plan_tile_schedule_probe(d)
+    assert (info.tile_m, info.tile_n, info.tile_rows, info.tile_cols, info.tile_count) == (64, 64, 2, 2, 4)
+    assert (info.min_required_prefix, info.max_required_prefix) == (9, 9)
+    assert (info.min_selected_prefix, info.max_selected_prefix) == (9, 9)
+    assert (info.prefix_group_count, info.adaptive_prefix_active, info.adaptive_skip_active) == (1, 0, 0)
+    assert info.range_bit_length == (2 * top).bit_length()
+    assert len(entries) == 4
+    for e in entries:
+        assert (e.required_prefix, e.selected_prefix, e.group_index) == (9, 9, 0)
+    assert entries[0].range_bit_length == (2 * top).bit_length()
+    assert entries[1].range_bit_length == math.prod(r8.LADDER[:8]).bit_length()
+    e0, e3 = entries[0], entries[3]
+    assert (e0.row_offset, e0.col_offset, e0.row_extent, e0.col_extent) == (0, 0, 64, 64)
+    assert (e3.tile_row, e3.tile_col, e3.row_offset, e3.col_offset, e3.row_extent, e3.col_extent) == (
+        1, 1, 64, 64, 1, 1)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dk", [-1, 0, 1])
+def test_k_split_edges_keep_padding_and_cancel_exactly(r8, dk):
+    """test_bounded_gemm_schedule_cases.inc (K-split edge cases): K one below,
+    at and one above the 65536-product int32-safe block, with padded lda,
+    ldb and ldc: alternating +-127 rows cancel exactly, and the padding
+    columns of C keep their sentinels."""
+    S = r8.Semantics
+    k = 65536 + dk
+    with r8.Context(0) as ctx:
+        product = 127 * 127
+        A = np.full((2, k + 1), 0x5A5A5A5A, np.int64)
+        B = np.full((k, 3), -0x1234567, np.int64)
+        A[0, :k] = np.where(np.arange(k) % 2 == 0, 127, -127)
+        A[1, :k] = 127
+        B[:, 0], B[:, 1] = 127, -127
+        sentinel = -0x51F15E5
+        Cm = np.full((2, 4), sentinel, np.int64)
+        r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 2, 2, k, bound=k * product), A[:, :k], B[:, :2],
+                            out=Cm[:, :2])
+        alt = 0 if k % 2 == 0 else product
+        assert Cm.tolist() == [[alt, -alt, sentinel, sentinel], [k * product, -k * product, sentinel, sentinel]]
+
+        Au = np.full((2, k + 1), 0xFEEDFACEFEEDFACE, np.uint64)
+        Bu = np.full((k, 3), 0xDEADBEEFDEADBEEF, np.uint64)
+        Au[0, :k], Au[1, :k] = 255, 1
+        Bu[:, 0], Bu[:, 1] = 1, 255
+        su = 0xC001D00DCAFEF00D
+        Cu = np.full((2, 4), su, np.uint64)
+        r8.gemm_u64_oneshot(ctx, desc(r8, S.BOUNDED_U64, 2, 2, k, bound=k * 255 * 255), Au[:, :k], Bu[:, :2],
+                            out=Cu[:, :2])
+        assert Cu.tolist() == [[k * 255, k * 255 * 255, su, su], [k, k * 255, su, su]]
