@@ -11,8 +11,11 @@
 //   src/core/api_oneshot.cpp:61-677   one-shot contracts and orchestration
 // Host buffers are copied with cudaMemcpy2DAsync so caller leading dimensions
 // never reach the kernels, and every call ends with a stream synchronisation.
+#include <algorithm>
 #include <cstring>
+#include <future>
 #include <limits>
+#include <thread>
 #include <vector>
 
 #include "api_internal.hpp"
@@ -427,6 +430,42 @@ rns8_status validate_typed_oneshot(const rns8_gemm_desc& d, rns8_semantics expec
 // are enqueued interleaved, so pageable host memory (whose copies return only
 // when done) overlaps too. The result goes down only after every slab passed
 // the range check, so a RANGE_ERROR leaves C untouched.
+// Largest |x| of a row-major host matrix (x itself for uint64), over up to
+// 16 host threads.
+template <typename T>
+uint64_t host_max_magnitude(const T* src, int64_t rows, int64_t cols, int64_t ld) {
+  auto scan = [=](int64_t r0, int64_t r1) {
+    uint64_t mx = 0;
+    for (int64_t r = r0; r < r1; ++r) {
+      const T* row = src + r * ld;
+      for (int64_t c = 0; c < cols; ++c) {
+        uint64_t v;
+        if constexpr (std::numeric_limits<T>::is_signed)
+          v = row[c] < 0 ? uint64_t{0} - static_cast<uint64_t>(row[c]) : static_cast<uint64_t>(row[c]);
+        else
+          v = static_cast<uint64_t>(row[c]);
+        mx = v > mx ? v : mx;
+      }
+    }
+    return mx;
+  };
+  const int64_t hw = std::max<int64_t>(1, std::thread::hardware_concurrency());
+  const int64_t parts = std::min<int64_t>({hw, 16, rows});
+  std::vector<std::future<uint64_t>> futures;
+  const int64_t per = (rows + parts - 1) / parts;
+  for (int64_t r0 = per; r0 < rows; r0 += per)
+    futures.push_back(std::async(std::launch::async, scan, r0, std::min(rows, r0 + per)));
+  uint64_t mx = scan(0, std::min(rows, per));
+  for (auto& f : futures) mx = std::max(mx, f.get());
+  return mx;
+}
+
+// True when no cell of A x B can exceed the bound: |C_ij| <= K max|A| max|B|.
+bool bound_proven(uint64_t max_a, uint64_t max_b, int64_t k, uint64_t bound) {
+  const unsigned __int128 prod = static_cast<unsigned __int128>(max_a) * max_b;
+  return prod <= static_cast<unsigned __int128>(bound / static_cast<uint64_t>(k));
+}
+
 template <typename T>
 rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, const T* A, int64_t lda, const T* B,
                                       int64_t ldb, T* C, int64_t ldc, int slabs) {
@@ -449,7 +488,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   const uint64_t a_res = static_cast<uint64_t>(P) * prob.m * k, b_res = static_cast<uint64_t>(P) * k * n;
   const uint64_t c_res = static_cast<uint64_t>(P) * prob.m * n, c_nat = static_cast<uint64_t>(m) * n * sizeof(T);
   const uint64_t total = round256(a_nat) + round256(b_nat) + round256(a_res) + round256(b_res) + round256(c_res) +
-                         round256(c_nat) + round256(scratch);
+                         round256(c_nat) + round256(scratch) + 256;
   std::unique_lock<std::mutex> lock(ctx->oneshot_mutex, std::try_to_lock);
   DevBuf local;
   DevBuf& arena = lock.owns_lock() ? ctx->oneshot_arena : local;
@@ -463,11 +502,19 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   int8_t* rC = static_cast<int8_t*>(cv.take(c_res));
   T* dC = static_cast<T*>(cv.take(c_nat));
   void* dS = cv.take(scratch);
+  auto* d_max_b = static_cast<uint64_t*>(cv.take(sizeof(uint64_t)));
   auto pack = [&](const T* src, int64_t r, int64_t c, int8_t* planes) {
     return kSigned ? rns8cuda::pack_i64(reinterpret_cast<const int64_t*>(src), r, c, c, P, planes, ctx->stream)
                    : rns8cuda::pack_u64(reinterpret_cast<const uint64_t*>(src), r, c, c, P, planes, ctx->stream);
   };
-  std::vector<cudaEvent_t> events(static_cast<size_t>(slabs) + 1, nullptr);
+  // While the copies and kernels run, check whether the inputs alone prove
+  // the bound (max|A| on host threads, max|B| on the device once B is in). If
+  // they do, no cell can be a RANGE_ERROR, so each slab of C goes back to the
+  // host as soon as it is exported, overlapping the uploads still in flight
+  // (C stays untouched only on a RANGE_ERROR, which is then impossible);
+  // otherwise C is copied after the status check.
+  auto max_a = std::async(std::launch::async, [=] { return host_max_magnitude(A, m, k, lda); });
+  std::vector<cudaEvent_t> events(2 * static_cast<size_t>(slabs) + 1, nullptr);
   auto destroy = [&] {
     for (cudaEvent_t& e : events)
       if (e) cudaEventDestroy(e);
@@ -501,16 +548,38 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
       ok = (kSigned ? rns8cuda::export_i64(rC, r, n, P, plan.desc.bound, reinterpret_cast<int64_t*>(dC) + r0 * n, n,
                                            ctx->dev_status, ctx->stream)
                     : rns8cuda::export_u64(rC, r, n, P, plan.desc.bound, reinterpret_cast<uint64_t*>(dC) + r0 * n, n,
-                                           ctx->dev_status, ctx->stream)) == cudaSuccess;
+                                           ctx->dev_status, ctx->stream)) == cudaSuccess &&
+           cudaEventRecord(events[slabs + 1 + i], ctx->stream) == cudaSuccess;
   }
-  // Both streams finish before the events go and before any result is read.
-  const bool copies_ok = cudaStreamSynchronize(ctx->copy_stream) == cudaSuccess;
+  uint64_t max_b = ~uint64_t{0};
+  bool early_ok = ok && cudaStreamWaitEvent(ctx->out_stream, events[0], 0) == cudaSuccess &&
+                  rns8cuda::max_magnitude(dB, k * n, kSigned, d_max_b, ctx->sm_count, ctx->out_stream) ==
+                      cudaSuccess &&
+                  cudaMemcpyAsync(&max_b, d_max_b, sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->out_stream) ==
+                      cudaSuccess &&
+                  cudaStreamSynchronize(ctx->out_stream) == cudaSuccess;
+  const bool early = bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok;
+  if (ok && early) {
+    for (int i = 0; early_ok && i < slabs; ++i) {
+      const int64_t r0 = i * slab_rows;
+      if (r0 >= m) break;
+      const int64_t r = std::min<int64_t>(slab_rows, m - r0);
+      early_ok = cudaStreamWaitEvent(ctx->out_stream, events[slabs + 1 + i], 0) == cudaSuccess &&
+                 cudaMemcpy2DAsync(C + r0 * ldc, static_cast<size_t>(ldc) * sizeof(T), dC + r0 * n,
+                                   static_cast<size_t>(n) * sizeof(T), static_cast<size_t>(n) * sizeof(T),
+                                   static_cast<size_t>(r), cudaMemcpyDeviceToHost, ctx->out_stream) == cudaSuccess;
+    }
+  }
+  // Every stream finishes before the events go and before any result is read.
+  const bool copies_ok = cudaStreamSynchronize(ctx->copy_stream) == cudaSuccess &&
+                         cudaStreamSynchronize(ctx->out_stream) == cudaSuccess;
   uint32_t word = 0;
   st = read_status(*ctx, &word);
   destroy();
-  if (!ok || !copies_ok) return RNS8_BACKEND_FAILURE;
+  if (!ok || !copies_ok || (early && !early_ok)) return RNS8_BACKEND_FAILURE;
   if (st != RNS8_SUCCESS) return st;
   if ((st = status_from_device(word)) != RNS8_SUCCESS) return st;
+  if (early) return RNS8_SUCCESS;
   if ((st = copy_out_2d(*ctx, C, ldc, dC, m, n, sizeof(T))) != RNS8_SUCCESS) return st;
   return sync(*ctx);
 }
@@ -596,7 +665,7 @@ rns8_status bounded_oneshot(rns8_context* ctx, const rns8_gemm_desc* desc, const
   if (!plan.tile_bounds.empty()) return bounded_oneshot_per_tile<T>(ctx, plan, A, lda, B, ldb, C, ldc);
   // Large calls overlap the upload with pack, GEMM and export, slab by slab.
   if (plan.desc.m >= 1024 && static_cast<uint64_t>(plan.desc.m) * plan.desc.k * 8 >= (uint64_t{64} << 20)) {
-    const int slabs = static_cast<int>(std::min<int64_t>(8, plan.desc.m / 512));
+    const int slabs = static_cast<int>(std::min<int64_t>(16, plan.desc.m / 512));
     return bounded_oneshot_pipelined<T>(ctx, plan, A, lda, B, ldb, C, ldc, slabs);
   }
   const int64_t m = plan.desc.m, n = plan.desc.n, k = plan.desc.k;

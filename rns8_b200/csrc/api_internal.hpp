@@ -66,6 +66,7 @@ struct rns8_context {
   int sm_count = 148;
   cudaStream_t stream = nullptr;
   cudaStream_t copy_stream = nullptr;  // host-to-device uploads overlapped with `stream`
+  cudaStream_t out_stream = nullptr;   // device-to-host results overlapped with both
   rns8_device_info info{};
   uint32_t* dev_status = nullptr;  // 4 status words
   // Device arena reused by the one-shot entry points (serialised by the mutex).

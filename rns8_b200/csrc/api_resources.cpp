@@ -75,9 +75,11 @@ extern "C" rns8_status rns8_create_context(int device_id, const rns8_context_opt
     ctx->sm_count = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->out_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(reinterpret_cast<void**>(&ctx->dev_status), 4 * sizeof(uint32_t)) != cudaSuccess) {
       if (ctx->stream) cudaStreamDestroy(ctx->stream);
       if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
+      if (ctx->out_stream) cudaStreamDestroy(ctx->out_stream);
       delete ctx;
       return RNS8_BACKEND_FAILURE;
     }
@@ -107,11 +109,13 @@ extern "C" rns8_status rns8_destroy_context(rns8_context* ctx) {
   cudaSetDevice(ctx->device_id);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
+  if (ctx->out_stream) cudaStreamSynchronize(ctx->out_stream);
   ctx->oneshot_arena.release();
   ctx->admission.release();
   if (ctx->dev_status) cudaFree(ctx->dev_status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
+  if (ctx->out_stream) cudaStreamDestroy(ctx->out_stream);
   delete ctx;
   return RNS8_SUCCESS;
 }

@@ -19,6 +19,10 @@ constexpr uint32_t kDevRangeError = 5;       // == RNS8_RANGE_ERROR
 constexpr uint32_t kDevWaitTimeout = 0x100;  // a bounded device wait ran out
 
 // ---- pack (native -> centered int8 residue planes) ------------------------
+// *out = the largest |x| over count contiguous int64 (is_signed) or uint64
+// values; *out must be 8-byte aligned device memory.
+cudaError_t max_magnitude(const void* src, int64_t count, bool is_signed, uint64_t* out, int sm_count,
+                          cudaStream_t stream);
 cudaError_t pack_i64(const int64_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t prefix, int8_t* planes,
                      cudaStream_t stream);
 cudaError_t pack_u64(const uint64_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t prefix, int8_t* planes,

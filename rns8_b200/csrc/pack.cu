@@ -367,7 +367,37 @@ __global__ void __launch_bounds__(256) pack_u8_scalar_kernel(const uint8_t* __re
   }
 }
 
+// Largest |x| (x for unsigned) of count contiguous 64-bit values into *out
+// (zeroed first), by a grid-stride sweep and one atomicMax per warp.
+__global__ void __launch_bounds__(256) max_magnitude_kernel(const uint64_t* __restrict__ src, int64_t count,
+                                                            bool is_signed, unsigned long long* out) {
+  unsigned long long mx = 0;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += step) {
+    const uint64_t v = __ldcs(src + i);
+    const uint64_t mag = (is_signed && (v >> 63)) ? 0 - v : v;
+    mx = mag > mx ? mag : mx;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+    mx = other > mx ? other : mx;
+  }
+  if ((threadIdx.x & 31) == 0 && mx != 0) atomicMax(out, mx);
+}
+
 }  // namespace
+
+cudaError_t max_magnitude(const void* src, int64_t count, bool is_signed, uint64_t* out, int sm_count,
+                          cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(out, 0, sizeof(uint64_t), stream);
+  if (e != cudaSuccess || count <= 0) return e;
+  int64_t blocks = (count + 255) / 256;
+  if (blocks > static_cast<int64_t>(sm_count) * 8) blocks = static_cast<int64_t>(sm_count) * 8;
+  max_magnitude_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      static_cast<const uint64_t*>(src), count, is_signed, reinterpret_cast<unsigned long long*>(out));
+  return cudaGetLastError();
+}
 
 cudaError_t pack_i64(const int64_t* src, int64_t rows, int64_t cols, int64_t ld, uint32_t prefix, int8_t* planes,
                      cudaStream_t stream) {

@@ -814,3 +814,26 @@ def test_pipelined_oneshot_matches_exact(rns8, ctx, signed):
         fn(ctx, rns8.gemm_desc(sem, bk, m, n, k, bound=bound // 4), A[:, :k], B[:, :n], out=untouched)
     assert err.value.status == rns8.Status.RANGE_ERROR
     assert (untouched == 9).all()
+
+
+@pytest.mark.parametrize("signed", [True, False])
+def test_pipelined_oneshot_with_input_proven_bound(rns8, ctx, signed):
+    """When K * max|A| * max|B| <= bound (checked on host threads while the
+    copies run), no cell can be a range error, and each row slab of C is
+    copied back as soon as it is exported; the result and the padding of a
+    strided C are the same as on the checked path."""
+    rng = np.random.default_rng(2200 + signed)
+    m, n, k = 1100, 64, 8192
+    lo = -(2**20) if signed else 0
+    dt = np.int64 if signed else np.uint64
+    A = rng.integers(lo, 2**20, (m, k + 1), dtype=dt, endpoint=True)
+    B = rng.integers(lo, 2**20, (k, n + 3), dtype=dt, endpoint=True)
+    want = A[:, :k] @ B[:, :n]
+    bound = k * 2**40  # = K * max|A| * max|B| for these ranges
+    sem = rns8.Semantics.BOUNDED_I64 if signed else rns8.Semantics.BOUNDED_U64
+    bk = rns8.BoundKind.GLOBAL_MAX_ABS if signed else rns8.BoundKind.GLOBAL_MAX_UNSIGNED
+    fn = rns8.gemm_i64_oneshot if signed else rns8.gemm_u64_oneshot
+    out = np.full((m, n + 2), 5, dt)
+    fn(ctx, rns8.gemm_desc(sem, bk, m, n, k, bound=bound), A[:, :k], B[:, :n], out=out[:, :n])
+    np.testing.assert_array_equal(out[:, :n], want)
+    assert (out[:, n:] == 5).all()
