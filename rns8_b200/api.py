@@ -150,9 +150,9 @@ class Matrix(_Handle):
     _destroy = "rns8_destroy_matrix"
 
     def __init__(self, ctx: Context, rows: int, cols: int, semantics, bound_kind, max_prefix: int = 0,
-                 tile_m: int = 0, tile_n: int = 0):
+                 tile_m: int = 0, tile_n: int = 0, logical_ld: int = 0):
         super().__init__()
-        desc = abi.MatrixDesc(rows=rows, cols=cols, logical_ld=cols, semantics=int(semantics),
+        desc = abi.MatrixDesc(rows=rows, cols=cols, logical_ld=logical_ld or cols, semantics=int(semantics),
                               logical_layout=int(abi.Layout.ROW_MAJOR), bound_kind=int(bound_kind),
                               max_prefix=max_prefix, tile_m=tile_m, tile_n=tile_n)
         self.ctx = ctx
