@@ -200,3 +200,78 @@ def test_k_split_edges_keep_padding_and_cancel_exactly(r8, dk):
         r8.gemm_u64_oneshot(ctx, desc(r8, S.BOUNDED_U64, 2, 2, k, bound=k * 255 * 255), Au[:, :k], Bu[:, :2],
                             out=Cu[:, :2])
         assert Cu.tolist() == [[k * 255, k * 255 * 255, su, su], [k, k * 255, su, su]]
+
+
+def test_schedule_tile_grid_and_prefix_groups(r8):
+    """test_bounded_gemm_schedule_cases.inc (tile grid case): a global bound
+    of 1000 over 130 x 129 in 64 x 64 tiles is one group at prefix 2 (10
+    range bits, adaptive skip below the default 9), a 3 x 3 grid whose last
+    tile is 2 x 1; a schedule buffer of 8 is WORKSPACE_TOO_SMALL with the
+    count still written."""
+    import ctypes as C
+
+    S, BK = r8.Semantics, r8.BoundKind
+    d = r8.gemm_desc(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 130, 129, 7, bound=1000, tile_m=64, tile_n=64)
+    entries, info = r8.api.plan_tile_schedule_probe(d)
+    assert (info.tile_m, info.tile_n, info.tile_rows, info.tile_cols, info.tile_count) == (64, 64, 3, 3, 9)
+    assert (info.min_required_prefix, info.max_required_prefix, info.min_selected_prefix,
+            info.max_selected_prefix) == (2, 2, 2, 2)
+    assert (info.prefix_group_count, info.adaptive_prefix_active, info.adaptive_skip_active) == (1, 0, 1)
+    assert info.range_bit_length == 10
+    e0, e8 = entries[0], entries[-1]
+    assert (e0.tile_row, e0.tile_col, e0.row_offset, e0.col_offset, e0.row_extent, e0.col_extent) == (0, 0, 0, 0, 64,
+                                                                                                    64)
+    assert (e0.required_prefix, e0.selected_prefix, e0.group_index, e0.range_bit_length) == (2, 2, 0, 10)
+    assert (e8.tile_row, e8.tile_col, e8.row_offset, e8.col_offset, e8.row_extent, e8.col_extent) == (2, 2, 128, 128,
+                                                                                                    2, 1)
+    small = (r8.abi.PlanTileScheduleEntry * 8)()
+    for e in small:
+        e.struct_size, e.abi_version = C.sizeof(e), 1
+    written = C.c_uint64()
+    st = r8.lib().rns8_cuda_plan_tile_schedule_probe(C.byref(d), small, 8, C.byref(written), None)
+    assert st == 7 and written.value == 9  # RNS8_WORKSPACE_TOO_SMALL
+
+
+def test_schedule_from_copied_per_tile_bounds(r8):
+    """test_bounded_gemm_schedule_cases.inc (copied per-tile bounds): nine
+    tile bounds from 1 to 2^40 give prefixes 1..6 in five groups (group
+    index ordered by prefix), 41 range bits."""
+    S, BK = r8.Semantics, r8.BoundKind
+    bounds = [1, 1000, 1000000, 2**40, 5, 2000, 70000, 2**20, 2**32]
+    d = r8.gemm_desc(S.BOUNDED_U64, BK.PER_TILE_MAX_UNSIGNED, 130, 129, 7, tile_m=64, tile_n=64)
+    r8.api.set_tile_bounds(d, bounds)
+    entries, info = r8.api.plan_tile_schedule_probe(d)
+    assert (info.tile_rows, info.tile_cols, info.tile_count) == (3, 3, 9)
+    assert (info.min_required_prefix, info.max_required_prefix, info.min_selected_prefix,
+            info.max_selected_prefix) == (1, 6, 1, 6)
+    assert (info.prefix_group_count, info.adaptive_prefix_active, info.adaptive_skip_active) == (5, 1, 1)
+    assert info.range_bit_length == 41
+    got = [(e.required_prefix, e.selected_prefix, e.group_index) for e in entries]
+    assert got[0] == (1, 1, 0) and got[1] == (2, 2, 1) and got[2] == (3, 3, 2) and got[3] == (6, 6, 4)
+    assert got[8] == (5, 5, 3)
+    e8 = entries[8]
+    assert (e8.row_offset, e8.col_offset, e8.row_extent, e8.col_extent) == (128, 128, 2, 1)
+
+
+def test_zero_output_skips_need_the_opt_in(r8):
+    """test_bounded_gemm_schedule_cases.inc (proven-zero opt-in): zero tile
+    bounds flag ZERO_OUTPUT tiles only with ALLOW_PROVEN_ZERO_TILE_SKIPS;
+    without it they run at prefix 1 with 0 range bits; the flag on a global
+    plan is INVALID_ARGUMENT."""
+    S, BK = r8.Semantics, r8.BoundKind
+    bounds = [0, 1000, 0, 1000000]
+    d = r8.gemm_desc(S.BOUNDED_U64, BK.PER_TILE_MAX_UNSIGNED, 65, 65, 1, tile_m=64, tile_n=64)
+    r8.api.set_tile_bounds(d, bounds)
+    entries, info = r8.api.plan_tile_schedule_probe(d)
+    assert info.flags == 0
+    assert (entries[0].range_bit_length, entries[0].required_prefix, entries[0].selected_prefix,
+            entries[0].flags, entries[2].flags) == (0, 1, 1, 0, 0)
+    d = r8.gemm_desc(S.BOUNDED_U64, BK.PER_TILE_MAX_UNSIGNED, 65, 65, 1, tile_m=64, tile_n=64, flags=2)
+    r8.api.set_tile_bounds(d, bounds)
+    entries, info = r8.api.plan_tile_schedule_probe(d)
+    ZERO = 1  # RNS8_TILE_SCHEDULE_ZERO_OUTPUT
+    assert info.flags == ZERO
+    assert [e.flags for e in entries] == [ZERO, 0, ZERO, 0]
+    assert entries[0].range_bit_length == 0 and entries[2].range_bit_length == 0
+    g = r8.gemm_desc(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 1, 1, 1, bound=1, flags=2)
+    assert r8.api.plan_probe(g)[0] == INVALID
