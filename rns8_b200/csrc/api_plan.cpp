@@ -501,7 +501,7 @@ extern "C" const char* rns8_status_string(rns8_status status) {
   switch (status) {
     case RNS8_SUCCESS: return "success";
     case RNS8_INVALID_ARGUMENT: return "invalid argument";
-    case RNS8_UNSUPPORTED_OS: return "unsupported os";
+    case RNS8_UNSUPPORTED_OS: return "unsupported operating system";
     case RNS8_UNSUPPORTED_ARCH: return "unsupported architecture";
     case RNS8_UNSUPPORTED_BACKEND: return "unsupported backend";
     case RNS8_RANGE_ERROR: return "range error";

@@ -63,6 +63,12 @@ def test_status_and_ladder_queries(rns8, oracle):
     assert lib.rns8_status_string(0) == b"success"
     assert lib.rns8_status_string(5) == b"range error"
     assert lib.rns8_status_string(999) == b"unknown status"
+    # test_api_status_cases.inc:1-24: every ABI status has the reference's text.
+    texts = [b"success", b"invalid argument", b"unsupported operating system", b"unsupported architecture",
+             b"unsupported backend", b"range error", b"accumulation overflow risk", b"workspace too small",
+             b"backend failure", b"verification failed", b"internal error"]
+    assert [lib.rns8_status_string(s) for s in range(len(texts))] == texts
+    assert lib.rns8_status_string(0x7FFF) == b"unknown status"
     assert lib.rns8_default_modulus_count() == 28
     for i in range(28):
         assert lib.rns8_default_modulus(i) == oracle.lib().oracle_modulus(i)
