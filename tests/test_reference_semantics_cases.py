@@ -134,3 +134,27 @@ def test_matrix_descriptor_cases(r8):
                 assert create(sem, bk, max_prefix=9) == (INVALID, False)
         for bk in (BK.NONE, *BOUNDED_KINDS(BK)[1:]):
             assert create(S.WRAP_U64_MOD_2_64, bk, max_prefix=9) == (INVALID, False)
+
+
+def test_accelerator_backends_fail_fast(r8):
+    """test_api_backend_info_cases.inc (context kinds fail fast; malformed
+    descriptors fail before unsupported routing): every backend other than
+    this library's is UNSUPPORTED_BACKEND at context creation with no
+    handle; plan descriptors naming them are INVALID_ARGUMENT when malformed
+    (reserved flag, m = 0) and UNSUPPORTED_BACKEND when well formed."""
+    S, BK, B = r8.Semantics, r8.BoundKind, r8.Backend
+    lib = r8.lib()
+    for b in (B.ROCWMMA, B.CK, B.HIPBLASLT, B.AMDGPU_BUILTINS, B.HIP_DIRECT, B.CPU_REFERENCE,
+              B.WRAP64_BYTE_LIMB, B.HIP_VECTOR_ALU_INT64):
+        opts = r8.abi.ContextOptions(requested_backend=int(b))
+        h = C.c_void_p()
+        assert lib.rns8_create_context(0, C.byref(opts), C.byref(h)) == UNSUPPORTED and not h.value
+    for b in (B.CK, B.ROCWMMA, B.AMDGPU_BUILTINS):
+        def d(**kw):
+            g = r8.gemm_desc(S.BOUNDED_I64, BK.GLOBAL_MAX_ABS, 1, 1, 1, bound=1, max_prefix=9, requested_backend=b)
+            for key, val in kw.items():
+                setattr(g, key, val)
+            return g
+        assert probe(r8, d(flags=0x80000000)) == INVALID
+        assert probe(r8, d(m=0)) == INVALID
+        assert probe(r8, d()) == UNSUPPORTED
