@@ -275,3 +275,116 @@ def test_zero_output_skips_need_the_opt_in(r8):
     assert entries[0].range_bit_length == 0 and entries[2].range_bit_length == 0
     g = r8.gemm_desc(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 1, 1, 1, bound=1, flags=2)
     assert r8.api.plan_probe(g)[0] == INVALID
+
+
+def test_default_and_fixed_prefix_selection(r8):
+    """test_bounded_gemm_basic_cases.inc:127-169, 350-420: bound 1000 selects
+    prefix 2 (adaptive skip) unless FORCE_FIXED_PREFIX keeps the default 9;
+    INT64_MAX at max_prefix 8 is a RANGE_ERROR; 2^63 signed and 2^64 - 1
+    unsigned need exactly prefix 9 (8 is a RANGE_ERROR)."""
+    S, BK = r8.Semantics, r8.BoundKind
+    d = desc(r8, S.BOUNDED_U64, 2, 2, 3, bound=1000)
+    _, info = r8.api.plan_tile_schedule_probe(d)
+    assert (info.min_required_prefix, info.max_required_prefix, info.min_selected_prefix, info.max_selected_prefix,
+            info.adaptive_skip_active) == (2, 2, 2, 2, 1)
+    d.flags = r8.PLAN_FORCE_FIXED_PREFIX
+    _, info = r8.api.plan_tile_schedule_probe(d)
+    assert (info.min_required_prefix, info.max_required_prefix, info.min_selected_prefix, info.max_selected_prefix,
+            info.adaptive_skip_active) == (2, 2, 9, 9, 0)
+    assert r8.api.plan_probe(desc(r8, S.BOUNDED_I64, 1, 1, 1, bound=2**63 - 1, max_prefix=8))[0] == RANGE
+    for sem, bound in ((S.BOUNDED_I64, 2**63), (S.BOUNDED_U64, 2**64 - 1)):
+        assert r8.api.plan_probe(desc(r8, sem, 1, 1, 1, bound=bound, max_prefix=8))[0] == RANGE
+        _, info = r8.api.plan_tile_schedule_probe(desc(r8, sem, 1, 1, 1, bound=bound, max_prefix=9))
+        assert (info.min_required_prefix, info.max_required_prefix, info.min_selected_prefix,
+                info.max_selected_prefix) == (9, 9, 9, 9)
+
+
+@pytest.mark.gpu
+def test_oneshot_signs_cancellation_and_full_boundaries(r8):
+    """test_bounded_gemm_basic_cases.inc:1-126: signs and cancellation
+    (2x3 x 3x2 -> {-188, 51, -268, 881}; 123456789 - 123456789 -> 0 under
+    bound 1); outputs at INT64_MAX, -INT64_MAX, INT64_MIN (bound 2^63) and
+    UINT64_MAX; full-width values with padded lda = ldb = 3 and ldc = 4
+    leaving the padding untouched."""
+    S = r8.Semantics
+    I64MIN, I64MAX, U = -(2**63), 2**63 - 1, 2**64 - 1
+    with r8.Context(0) as ctx:
+        A = np.array([[7, -3, 5], [-11, 13, 17]], np.int64)
+        B = np.array([[2, -5], [19, 23], [-29, 31]], np.int64)
+        assert r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 2, 2, 3, bound=100000), A, B).ravel().tolist() == [
+            -188, 51, -268, 881]
+        out = np.array([[99]], np.int64)
+        r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 1, 1, 2, bound=1), np.array([[123456789, 123456789]],
+                            np.int64), np.array([[1], [-1]], np.int64), out=out)
+        assert out[0, 0] == 0
+        for a, bound, want in ((I64MAX, I64MAX, I64MAX), (-I64MAX, I64MAX, -I64MAX), (I64MIN, 2**63, I64MIN)):
+            got = r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 1, 1, 1, bound=bound), np.array([[a]], np.int64),
+                                      np.array([[1]], np.int64))
+            assert got[0, 0] == want
+        got = r8.gemm_u64_oneshot(ctx, desc(r8, S.BOUNDED_U64, 1, 1, 1, bound=U), np.array([[U]], np.uint64),
+                                  np.array([[1]], np.uint64))
+        assert int(got[0, 0]) == U
+        # Padded full-width: signed
+        s = 0x1020304050607
+        A = np.full((2, 3), s, np.int64)
+        B = np.full((2, 3), -s, np.int64)
+        A[0, :2] = [I64MIN, 0]
+        A[1, :2] = [I64MAX, -I64MAX]
+        B[0, :2] = [1, 0]
+        B[1, :2] = [0, 1]
+        Cm = np.full((2, 4), s, np.int64)
+        r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 2, 2, 2, bound=2**63), A[:, :2], B[:, :2], out=Cm[:, :2])
+        assert Cm.tolist() == [[I64MIN, 0, s, s], [I64MAX, -I64MAX, s, s]]
+        # Padded full-width: unsigned
+        su = 0xAAAAAAAAAAAAAAAA
+        A = np.full((2, 3), su, np.uint64)
+        B = np.full((2, 3), su, np.uint64)
+        A[0, :2] = [U, U - 1]
+        A[1, :2] = [0, 1]
+        B[0, :2] = [1, 0]
+        B[1, :2] = [0, 1]
+        Cm = np.full((2, 4), su, np.uint64)
+        r8.gemm_u64_oneshot(ctx, desc(r8, S.BOUNDED_U64, 2, 2, 2, bound=U), A[:, :2], B[:, :2], out=Cm[:, :2])
+        assert [[int(x) for x in row] for row in Cm] == [[U, U - 1, su, su], [0, 1, su, su]]
+
+
+def per_tile(r8, signed, bounds, flags=0, m=65, n=65, k=1):
+    S, BK = r8.Semantics, r8.BoundKind
+    d = r8.gemm_desc(S.BOUNDED_I64 if signed else S.BOUNDED_U64,
+                     BK.PER_TILE_MAX_ABS if signed else BK.PER_TILE_MAX_UNSIGNED, m, n, k, flags=flags, tile_m=64,
+                     tile_n=64)
+    r8.api.set_tile_bounds(d, bounds)
+    return d
+
+
+@pytest.mark.gpu
+def test_per_tile_oneshots(r8):
+    """test_bounded_gemm_per_tile_cases.inc:1-153: too-small per-tile bounds
+    (2 x 3 = 6 against 5, or against a 0 bound without the proven-zero flag)
+    are RANGE_ERROR with the padded C untouched; with the flag, zero-bound
+    tiles are written as zeros; unsigned and signed per-tile prefixes
+    (bounds 7 .. 1e9) export every cell exactly."""
+    m = n = 65
+    with r8.Context(0) as ctx:
+        for signed, bounds in ((True, [5, 10, 10, 10]), (False, [5, 10, 10, 10]), (False, [0, 10, 10, 10])):
+            dt = np.int64 if signed else np.uint64
+            fn = r8.gemm_i64_oneshot if signed else r8.gemm_u64_oneshot
+            C = np.full((m, 67), -99 if signed else 123, dt)
+            with pytest.raises(r8.Error) as err:
+                fn(ctx, per_tile(r8, signed, bounds), np.full((m, 1), 2, dt), np.full((1, n), 3, dt), out=C[:, :n])
+            assert err.value.status == r8.Status.RANGE_ERROR
+            assert (C == (-99 if signed else 123)).all()
+        A = np.array([[1 if r < 64 else 1000] for r in range(m)], np.uint64)
+        B = np.array([[0 if c < 64 else 7 for c in range(n)]], np.uint64)
+        C = np.full((m, n + 1), 0xDEADBEEFDEADBEEF, np.uint64)
+        r8.gemm_u64_oneshot(ctx, per_tile(r8, False, [0, 7, 0, 7000], flags=2), A, B, out=C[:, :n])
+        np.testing.assert_array_equal(C[:, :n], A @ B)
+        assert (C[:, n] == 0xDEADBEEFDEADBEEF).all()
+        A = np.array([[1 if r < 64 else 1000000] for r in range(m)], np.uint64)
+        B = np.array([[7 if c < 64 else 1000 for c in range(n)]], np.uint64)
+        got = r8.gemm_u64_oneshot(ctx, per_tile(r8, False, [7, 1000, 7000000, 1000000000]), A, B)
+        np.testing.assert_array_equal(got, A @ B)
+        A = np.array([[-2 if r < 64 else -1000000] for r in range(m)], np.int64)
+        B = np.array([[3 if c < 64 else -1000 for c in range(n)]], np.int64)
+        got = r8.gemm_i64_oneshot(ctx, per_tile(r8, True, [6, 2000, 3000000, 1000000000]), A, B)
+        np.testing.assert_array_equal(got, A @ B)
