@@ -1,11 +1,18 @@
-"""The reference's bounded-GEMM unit cases
-(tests/unit/test_bounded_gemm_basic_cases.inc:170-358) through this library's
-public C ABI: input-range descriptors (bound = K * lhs_bound * rhs_bound),
-their validation, too-small bounds leaving padded outputs untouched, and plan
-ranges. Descriptor validation runs on the host (rns8_cuda_plan_probe, no GPU);
-the products run on the GPU."""
+"""The reference's bounded-GEMM unit cases (tests/unit/test_bounded_gemm_basic_cases.inc,
+test_bounded_gemm_per_tile_cases.inc, test_bounded_gemm_schedule_cases.inc)
+and its bounded differential / qualification cases
+(tests/differential/test_hip_direct_bounded_oneshot_cases.inc,
+test_hip_direct_qualification_cases.inc) through this library's public C
+ABI: input-range descriptors (bound = K * lhs_bound * rhs_bound), prefix
+selection, per-tile contracts and schedules, signs, cancellation and
+full-width boundaries, K-split edges, and range errors that leave outputs
+untouched. Descriptor validation and schedules run on the host
+(rns8_cuda_plan_probe, rns8_cuda_plan_tile_schedule_probe; no GPU); the
+products run on the GPU."""
 
 from __future__ import annotations
+
+import ctypes as C
 
 import numpy as np
 import pytest
@@ -50,8 +57,6 @@ def test_input_range_descriptor_validation(r8):
 def test_per_tile_plan_with_overflowing_tile_count(r8):
     """test_api_validation_cases.inc:59-71: a per-tile plan over INT64_MAX^2
     cells is a range error, before any tile bound is read."""
-    import ctypes as C
-
     S, BK = r8.Semantics, r8.BoundKind
     d = r8.gemm_desc(S.BOUNDED_I64, BK.PER_TILE_MAX_ABS, 2**63 - 1, 2**63 - 1, 1, tile_m=64, tile_n=64)
     tb = (C.c_uint64 * 1)(1)
@@ -208,8 +213,6 @@ def test_schedule_tile_grid_and_prefix_groups(r8):
     range bits, adaptive skip below the default 9), a 3 x 3 grid whose last
     tile is 2 x 1; a schedule buffer of 8 is WORKSPACE_TOO_SMALL with the
     count still written."""
-    import ctypes as C
-
     S, BK = r8.Semantics, r8.BoundKind
     d = r8.gemm_desc(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 130, 129, 7, bound=1000, tile_m=64, tile_n=64)
     entries, info = r8.api.plan_tile_schedule_probe(d)
@@ -388,3 +391,89 @@ def test_per_tile_oneshots(r8):
         B = np.array([[3 if c < 64 else -1000 for c in range(n)]], np.int64)
         got = r8.gemm_i64_oneshot(ctx, per_tile(r8, True, [6, 2000, 3000000, 1000000000]), A, B)
         np.testing.assert_array_equal(got, A @ B)
+
+
+@pytest.mark.gpu
+def test_cancellation_and_full_width_stressors(r8):
+    """tests/differential/test_hip_direct_bounded_oneshot_cases.inc:241-337:
+    full-range int64 terms that cancel to results inside a small bound (the
+    residue arithmetic is exact modulo M, so intermediate sums beyond int64
+    do not matter); INT64_MIN / INT64_MAX and UINT64_MAX / UINT64_MAX - 42
+    through an identity with max_prefix 20; and K = 65537 unsigned at the
+    exact bound K * 255 * 2."""
+    S = r8.Semantics
+    I64MIN, I64MAX, U = -(2**63), 2**63 - 1, 2**64 - 1
+    with r8.Context(0) as ctx:
+        A = np.array([[I64MAX, I64MIN + 1, 37, -37], [1000000000, -1000000000, -12345, 12345]], np.int64)
+        B = np.array([[1, 1], [1, 1], [1000000, 1000000], [1000000, -1000000]], np.int64)
+        got = r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 2, 2, 4, bound=30000000000), A, B)
+        assert got.ravel().tolist() == [0, 74000000, 0, -24690000000]
+        eye = np.array([[1, 0], [0, 1]])
+        got = r8.gemm_i64_oneshot(ctx, desc(r8, S.BOUNDED_I64, 1, 2, 2, bound=2**63, max_prefix=20),
+                                  np.array([[I64MIN, I64MAX]], np.int64), eye.astype(np.int64))
+        assert got.ravel().tolist() == [I64MIN, I64MAX]
+        got = r8.gemm_u64_oneshot(ctx, desc(r8, S.BOUNDED_U64, 1, 2, 2, bound=U, max_prefix=20),
+                                  np.array([[U, U - 42]], np.uint64), eye.astype(np.uint64))
+        assert [int(x) for x in got.ravel()] == [U, U - 42]
+        k = 65537
+        Au = np.full((1, k), 255, np.uint64)
+        Bu = np.zeros((k, 2), np.uint64)
+        Bu[:, 0], Bu[:, 1] = 1, 2
+        got = r8.gemm_u64_oneshot(ctx, desc(r8, S.BOUNDED_U64, 1, 2, k, bound=k * 255 * 2), Au, Bu)
+        assert [int(x) for x in got.ravel()] == [k * 255, k * 255 * 2]
+
+
+@pytest.mark.gpu
+def test_bounded_export_every_prefix_and_every_failing_cell(r8):
+    """tests/differential/test_hip_direct_qualification_cases.inc:33-82: a
+    1 x 65 output of 2s (bound 10) at prefixes 1, 7, 8, 9, 20, signed and
+    unsigned, with no failing cell or one out-of-bound cell (-11 / 11) at
+    every position: the export succeeds or is a RANGE_ERROR accordingly, and
+    a failing export leaves all 68 destination elements untouched."""
+    S, BK = r8.Semantics, r8.BoundKind
+    lib = r8.lib()
+    cols = 65
+    with r8.Context(0) as ctx:
+        for prefix in (1, 7, 8, 9, 20):
+            for signed in (False, True):
+                sem = S.BOUNDED_I64 if signed else S.BOUNDED_U64
+                bk = BK.GLOBAL_MAX_ABS if signed else BK.GLOBAL_MAX_UNSIGNED
+                plan = r8.Plan(ctx, r8.gemm_desc(sem, bk, 1, cols, 1, bound=10, max_prefix=prefix,
+                                                 flags=r8.PLAN_FORCE_FIXED_PREFIX))
+                assert plan.prefix == prefix
+                mat = r8.Matrix(ctx, 1, cols, sem, bk, prefix)
+                dt = np.int64 if signed else np.uint64
+                fn = lib.rns8_export_i64 if signed else lib.rns8_export_u64
+                for bad in range(-1, cols):
+                    vals = np.full((1, cols), 2, dt)
+                    if bad >= 0:
+                        vals[0, bad] = -11 if signed else 11
+                    (mat.pack_i64 if signed else mat.pack_u64)(vals)
+                    out = np.full(cols + 3, -777 if signed else 777, dt)
+                    st = fn(ctx.handle, plan.handle, mat.handle, out.ctypes.data_as(C.c_void_p), cols + 3)
+                    if bad < 0:
+                        assert st == OK and out[:cols].tolist() == [2] * cols, prefix
+                        assert (out[cols:] == (-777 if signed else 777)).all()
+                    else:
+                        assert st == RANGE, (prefix, signed, bad)
+                        assert (out == (-777 if signed else 777)).all()
+                mat.close()
+                plan.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k", [65535, 65536, 65537, 131073, 262145])
+def test_persistent_gemm_spans_safe_k_blocks(r8, k):
+    """tests/differential/test_hip_direct_qualification_cases.inc:84-126:
+    (-127) x (-127) summed over K across one to five 65536-product blocks."""
+    S, BK = r8.Semantics, r8.BoundKind
+    with r8.Context(0) as ctx:
+        plan = r8.Plan(ctx, r8.gemm_desc(S.BOUNDED_I64, BK.GLOBAL_MAX_ABS, 1, 1, k, bound=k * 127 * 127))
+        ws = r8.Workspace(ctx, plan)
+        a, b, c = (r8.Matrix.for_plan(ctx, plan, role) for role in "abc")
+        a.pack_i64(np.full((1, k), -127, np.int64))
+        b.pack_i64(np.full((k, 1), -127, np.int64))
+        r8.gemm_rns(ctx, plan, a, b, c, ws)
+        assert r8.export_i64(ctx, plan, c)[0, 0] == k * 127 * 127
+        for h in (a, b, c, ws, plan):
+            h.close()
