@@ -244,3 +244,25 @@ def test_export_refuses_other_interpretations(r8, signed):
         assert dst.tolist() == [0xDDDDDDDDDDDDDDDD, 0xEEEEEEEEEEEEEEEE]
         assert value_of(f.export(2, 2)[0, 0], signed) == (-77 if signed else 77)
         f.close()
+
+
+def test_unsigned_high_bit_fixed_width(r8):
+    """tests/differential/test_hip_direct_exact_wide_export_cases.inc:245-303:
+    C = [2^127, 0] (2 x 2^63 x 2^63) exports in two limbs as [0, 2^63 | 0, 0],
+    is a RANGE_ERROR in one limb (destination untouched), and in 32 limbs
+    has every limb above the second zero."""
+    lib = r8.lib()
+    with r8.Context(0) as ctx:
+        f = Chain(r8, ctx, False, 1, 2, 2)
+        f.pack(0, [[2**63, 2**63]], 1)
+        f.pack(1, [[2**63, 0], [2**63, 0]], 1)
+        assert f.multiply(0, 1, 2) == OK
+        two = f.export(2, 2)
+        assert two.reshape(-1).tolist() == [0, 2**63, 0, 0]
+        one = np.full(2, 0x9D9D9D9D9D9D9D9D, np.uint64)
+        assert lib.rns8_export_exact_wide_unsigned_limbs(ctx.handle, f.plan.handle, f.mats[2].handle,
+                                                         one.ctypes.data_as(C.c_void_p), 2, 1) == RANGE
+        assert (one == 0x9D9D9D9D9D9D9D9D).all()
+        wide = f.export(2, 32)
+        assert wide[0, 0, :2].tolist() == [0, 2**63] and (wide[0, 0, 2:] == 0).all() and (wide[0, 1] == 0).all()
+        f.close()

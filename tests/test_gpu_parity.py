@@ -837,3 +837,43 @@ def test_pipelined_oneshot_with_input_proven_bound(rns8, ctx, signed):
     fn(ctx, rns8.gemm_desc(sem, bk, m, n, k, bound=bound), A[:, :k], B[:, :n], out=out[:, :n])
     np.testing.assert_array_equal(out[:, :n], want)
     assert (out[:, n:] == 5).all()
+
+
+def test_ring_gemm_centered_correction_boundaries(lib, oracle):
+    """tests/differential/test_hip_direct_ring_cases.inc:182-211: modulus 255
+    (plane 1), A = [1, 1], sums 128, 127, 254 and -128 reduce to the centered
+    -127, 127, -1, 127 on the auto (zero-padded tensor-core) and CUDA-core
+    paths."""
+    a = np.zeros((2, 1, 2), np.int8)
+    b = np.zeros((2, 2, 4), np.int8)
+    a[1] = [[1, 1]]
+    b[1] = [[64, 127, 127, -64], [64, 0, 127, -64]]
+    assert oracle.gemm_rns(a, b, 2)[1].ravel().tolist() == [-127, 127, -1, 127]
+    for path in (0, 2):
+        st, got, word = run_gemm(lib, a, b, 2, path)
+        assert st == OK and word == 0 and got[1].ravel().tolist() == [-127, 127, -1, 127], path
+
+
+def test_ring_gemm_reciprocal_reduction_every_modulus(lib, oracle):
+    """tests/differential/test_hip_direct_ring_cases.inc:122-180: the same
+    5 x 7 x 67 patterned operands (with +-127, 126 and -128 entries) in all 20
+    planes; every plane's reduction equals the oracle's ring GEMM for its
+    modulus."""
+    m, n, k = 5, 7, 67
+    A = np.empty((m, k), np.int8)
+    B = np.empty((k, n), np.int8)
+    for r in range(m):
+        for q in range(k):
+            pattern = (r * 37 + q * 19) % 11
+            mixed = (r + 113 - (2 * q) % 113) % 113
+            A[r, q] = 127 if pattern == 0 else -127 if pattern == 1 else mixed - 56
+    for q in range(k):
+        for c in range(n):
+            pattern = (q * 23 + c * 29) % 13
+            B[q, c] = 126 if pattern == 0 else -128 if pattern == 1 else ((3 * q + c) % 127) - 63
+    a = np.repeat(A[None], 20, axis=0)
+    b = np.repeat(B[None], 20, axis=0)
+    st, got, word = run_gemm(lib, a, b, 20, 0)
+    assert st == OK and word == 0
+    for p, modulus in enumerate(oracle.LADDER[:20]):
+        np.testing.assert_array_equal(got[p], oracle.ring_gemm(A, B, modulus), err_msg=f"modulus {modulus}")
