@@ -877,3 +877,29 @@ def test_ring_gemm_reciprocal_reduction_every_modulus(lib, oracle):
     assert st == OK and word == 0
     for p, modulus in enumerate(oracle.LADDER[:20]):
         np.testing.assert_array_equal(got[p], oracle.ring_gemm(A, B, modulus), err_msg=f"modulus {modulus}")
+
+
+@pytest.mark.parametrize("field,modulus", [(False, 255), (False, 256), (True, 251)])
+def test_finite_oneshot_patterned_padded(rns8, oracle, ctx, field, modulus):
+    """tests/differential/test_hip_direct_finite_native_cases.inc:1-85: 17 x 19
+    x 33 patterned bytes with padded lda 40, ldb 23, ldc 29 (pad bytes 0xa5,
+    0x5a in the inputs, 0xcc in C) for ring 255, ring 256 and field 251; C
+    equals the oracle and its padding keeps 0xcc."""
+    m, n, k, lda, ldb, ldc = 17, 19, 33, 40, 23, 29
+    A = np.full((m, lda), 0xA5, np.uint8)
+    B = np.full((k, ldb), 0x5A, np.uint8)
+    for r in range(m):
+        for q in range(k):
+            A[r, q] = (r * 37 + q * 19 + (r ^ q) * 11) & 0xFF
+    for q in range(k):
+        for c in range(n):
+            B[q, c] = (q * 23 + c * 41 + (q + c) * 7) & 0xFF
+    sem = rns8.Semantics.FINITE_FIELD_U8 if field else rns8.Semantics.FINITE_RING_U8
+    desc = rns8.gemm_desc(sem, rns8.BoundKind.NONE, m, n, k, finite_modulus=modulus)
+    out = np.full((m, ldc), 0xCC, np.uint8)
+    rns8.gemm_finite_u8_oneshot(ctx, desc, modulus, A[:, :k], B[:, :n], field, out=out[:, :n])
+    st, want = oracle.gemm_finite_u8_oneshot(np.ascontiguousarray(A[:, :k]), np.ascontiguousarray(B[:, :n]),
+                                             modulus, field)
+    assert st == OK
+    np.testing.assert_array_equal(out[:, :n], want)
+    assert (out[:, n:] == 0xCC).all()

@@ -477,3 +477,56 @@ def test_persistent_gemm_spans_safe_k_blocks(r8, k):
         assert r8.export_i64(ctx, plan, c)[0, 0] == k * 127 * 127
         for h in (a, b, c, ws, plan):
             h.close()
+
+
+@pytest.mark.gpu
+def test_per_tile_k_split_centered_cancellation(r8):
+    """tests/differential/test_hip_direct_per_tile_cases.inc:1-49: one tile
+    bounded by 127^2 over K = 65537 alternating +-127: the tile runs at its
+    required prefix (below the plan's 9), and C = [127^2, -127^2] with the
+    padded column untouched."""
+    k = 65537
+    d = per_tile(r8, True, [127 * 127], m=1, n=2, k=k)
+    entries, info = r8.api.plan_tile_schedule_probe(d)
+    assert len(entries) == 1 and entries[0].selected_prefix == entries[0].required_prefix < 9
+    A = np.full((1, k + 1), -0x55AA55AA, np.int64)
+    B = np.full((k, 3), -0x55AA55AA, np.int64)
+    A[0, :k] = np.where(np.arange(k) % 2 == 0, 127, -127)
+    B[:, 0], B[:, 1] = 127, -127
+    C = np.full((1, 3), -0x55AA55AA, np.int64)
+    with r8.Context(0) as ctx:
+        r8.gemm_i64_oneshot(ctx, d, A[:, :k], B[:, :2], out=C[:, :2])
+    assert C.tolist() == [[127 * 127, -127 * 127, -0x55AA55AA]]
+
+
+@pytest.mark.gpu
+def test_persistent_prefix9_exact_k_block_reused(r8):
+    """tests/differential/test_hip_direct_bounded_schedule_cases.inc:401-520:
+    u64, K = 65536 exactly, prefix 9 forced, padded host layouts; the same
+    resident matrices serve two rounds of new inputs."""
+    S, BK = r8.Semantics, r8.BoundKind
+    k = 65536
+    with r8.Context(0) as ctx:
+        plan = r8.Plan(ctx, r8.gemm_desc(S.BOUNDED_U64, BK.GLOBAL_MAX_UNSIGNED, 2, 2, k, bound=k * 12,
+                                         flags=r8.PLAN_FORCE_FIXED_PREFIX))
+        assert plan.prefix == 9
+        info = plan.schedule_info()
+        assert (info.min_selected_prefix, info.max_selected_prefix, info.adaptive_prefix_active) == (9, 9, 0)
+        ws = r8.Workspace(ctx, plan)
+        a, b, c = (r8.Matrix.for_plan(ctx, plan, role) for role in "abc")
+        s = 0xD1FFD1FFD1FFD1FF
+        for variant, (a0, a1, b0, b1) in enumerate(((1, 2, 3, 5), (2, 3, 1, 4))):
+            A = np.full((2, k + 1), s, np.uint64)
+            B = np.full((k, 3), s, np.uint64)
+            A[0, :k], A[1, :k] = a0, a1
+            B[:, 0], B[:, 1] = b0, b1
+            a.pack_u64(A[:, :k], source_version=10 + variant)
+            b.pack_u64(B[:, :2], source_version=20 + variant)
+            r8.gemm_rns(ctx, plan, a, b, c, ws)
+            out = np.full((2, 3), s, np.uint64)
+            r8.export_u64(ctx, plan, c, out=out[:, :2])
+            want = [[k * a0 * b0, k * a0 * b1], [k * a1 * b0, k * a1 * b1]]
+            assert [[int(x) for x in row[:2]] for row in out] == want
+            assert (out[:, 2] == s).all()
+        for h in (a, b, c, ws, plan):
+            h.close()
