@@ -16,6 +16,7 @@
 #include <future>
 #include <limits>
 #include <thread>
+#include <utility>
 #include <vector>
 
 #include "api_internal.hpp"
@@ -558,7 +559,17 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
                   cudaMemcpyAsync(&max_b, d_max_b, sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->out_stream) ==
                       cudaSuccess &&
                   cudaStreamSynchronize(ctx->out_stream) == cudaSuccess;
-  const bool early = bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok;
+  // C written while A is still uploading must not overlap either input.
+  auto span = [](const void* p, int64_t rows, int64_t cols, int64_t ld) {
+    const auto lo = reinterpret_cast<uintptr_t>(p);
+    return std::make_pair(lo, lo + static_cast<uintptr_t>((rows - 1) * ld + cols) * sizeof(T));
+  };
+  auto overlap = [](std::pair<uintptr_t, uintptr_t> x, std::pair<uintptr_t, uintptr_t> y) {
+    return x.first < y.second && y.first < x.second;
+  };
+  const auto c_span = span(C, m, n, ldc);
+  const bool disjoint = !overlap(c_span, span(A, m, k, lda)) && !overlap(c_span, span(B, k, n, ldb));
+  const bool early = bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok && disjoint;
   if (ok && early) {
     for (int i = 0; early_ok && i < slabs; ++i) {
       const int64_t r0 = i * slab_rows;

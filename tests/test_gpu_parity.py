@@ -903,3 +903,18 @@ def test_finite_oneshot_patterned_padded(rns8, oracle, ctx, field, modulus):
     assert st == OK
     np.testing.assert_array_equal(out[:, :n], want)
     assert (out[:, n:] == 0xCC).all()
+
+
+def test_pipelined_oneshot_output_overlapping_an_input(rns8, ctx):
+    """C's host buffer may overlap A's (here C starts at A's row 1024): the
+    result is that of the original A even though the inputs prove the bound
+    (the overlapping call waits for every upload before writing C)."""
+    m, n, k = 2048, 4096, 4096
+    rng = np.random.default_rng(77)
+    X = np.zeros((m + 1024, k), np.int64)
+    X[:m] = rng.integers(-(2**10), 2**10, (m, k), dtype=np.int64, endpoint=True)
+    B = rng.integers(-(2**10), 2**10, (k, n), dtype=np.int64, endpoint=True)
+    want = (X[:m].astype(np.float64) @ B.astype(np.float64)).astype(np.int64)  # |C| <= 2^32: exact
+    desc = rns8.gemm_desc(rns8.Semantics.BOUNDED_I64, rns8.BoundKind.GLOBAL_MAX_ABS, m, n, k, bound=k * 2**20)
+    rns8.gemm_i64_oneshot(ctx, desc, X[:m], B, out=X[1024:])
+    np.testing.assert_array_equal(X[1024:], want)
