@@ -741,10 +741,12 @@ extern "C" rns8_status rns8_get_plan_packing_info(const rns8_plan* plan, rns8_pl
       out->total_transient_workspace_bytes = out->accumulator_workspace_bytes;
       set_text(out->input_domain_name, sizeof(out->input_domain_name), "wrap64_byte_limb_current");
       set_text(out->output_domain_name, sizeof(out->output_domain_name), "wrap64_byte_limb_current");
-      set_text(out->next_op_hint, sizeof(out->next_op_hint), "export_wrap_u64 or chain wrap gemm");
-      set_text(out->a_layout_version, sizeof(out->a_layout_version), "limb_major_compact_row_major_u8_v1");
-      set_text(out->b_layout_version, sizeof(out->b_layout_version), "limb_major_compact_row_major_u8_v1");
-      set_text(out->output_layout_version, sizeof(out->output_layout_version), "limb_major_compact_row_major_u8_v1");
+      set_text(out->next_op_hint, sizeof(out->next_op_hint),
+               "produces wrap64 byte-limb-current output; export reconstructs low 64-bit words");
+      set_text(out->a_layout_version, sizeof(out->a_layout_version), "wrap64_byte_limb_v1");
+      set_text(out->b_layout_version, sizeof(out->b_layout_version), "wrap64_byte_limb_v1");
+      set_text(out->output_layout_version, sizeof(out->output_layout_version), "wrap64_byte_limb_v1");
+      set_text(out->prepack_cache_scope, sizeof(out->prepack_cache_scope), "device_resident_no_prepack_cache");
       set_text(out->detail, sizeof(out->detail), "eight unsigned byte planes in HBM; 36 byte-pair tensor-core products");
       return RNS8_SUCCESS;
     }
@@ -752,11 +754,18 @@ extern "C" rns8_status rns8_get_plan_packing_info(const rns8_plan* plan, rns8_pl
              finite ? "finite_u8_current" : "rns_residue_current");
     set_text(out->output_domain_name, sizeof(out->output_domain_name),
              finite ? "finite_u8_current" : "rns_residue_current");
-    set_text(out->next_op_hint, sizeof(out->next_op_hint), finite ? "export_finite_u8" : "export or chain rns gemm");
-    set_text(out->a_layout_version, sizeof(out->a_layout_version), "modulus_major_compact_row_major_i8_v1");
-    set_text(out->b_layout_version, sizeof(out->b_layout_version), "modulus_major_compact_row_major_i8_v1");
-    set_text(out->output_layout_version, sizeof(out->output_layout_version), "modulus_major_compact_row_major_i8_v1");
-    set_text(out->prepack_cache_scope, sizeof(out->prepack_cache_scope), "none");
+    // Hint, layout and cache-scope identifiers are the reference's contract
+    // names (api_plan_contract_names.inc:343-357, api_plan_workspace_packing.inc:227-235,
+    // api_plan_public_api.inc:526-531 for device-resident storage).
+    set_text(out->next_op_hint, sizeof(out->next_op_hint),
+             finite ? "produces finite-current centered residues; export converts to canonical uint8 output"
+                    : "produces residue-current RNS output; next same-contract RNS GEMM can consume it without "
+                      "logical export");
+    const char* layout = finite ? "finite_u8_centered_residue_v1" : "rns_centered_residue_planes_v1";
+    set_text(out->a_layout_version, sizeof(out->a_layout_version), layout);
+    set_text(out->b_layout_version, sizeof(out->b_layout_version), layout);
+    set_text(out->output_layout_version, sizeof(out->output_layout_version), layout);
+    set_text(out->prepack_cache_scope, sizeof(out->prepack_cache_scope), "device_resident_no_prepack_cache");
     set_text(out->detail, sizeof(out->detail), "resident planes in HBM; B read N-major by the tensor-core kernel");
     return RNS8_SUCCESS;
   });

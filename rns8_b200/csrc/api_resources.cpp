@@ -248,19 +248,23 @@ extern "C" rns8_status rns8_get_matrix_storage_info(const rns8_matrix* m, rns8_m
     out->source_version = m->source_version;
     out->host_residues_current = 0;
     out->hip_device_id = m->device_id;
-    set_text(out->storage_scope, sizeof(out->storage_scope), "device_resident_hbm");
+    // Storage scope and layout identifiers are the reference's contract names
+    // for device storage of these layouts (api_plan_workspace_packing.inc:227-260).
+    set_text(out->storage_scope, sizeof(out->storage_scope), "device_resident_storage");
     if (m->desc.semantics == RNS8_WRAP_U64_MOD_2_64) {
       out->device_byte_limbs_current = m->device_current ? 1u : 0u;
       out->uses_byte_limb_storage = 1;
       out->device_byte_limb_bytes = m->residue_bytes;
-      set_text(out->layout_version, sizeof(out->layout_version), "limb_major_compact_row_major_u8_v1");
+      set_text(out->storage_scope, sizeof(out->storage_scope), "device_byte_limb_storage");
+      set_text(out->layout_version, sizeof(out->layout_version), "wrap64_byte_limb_v1");
       set_text(out->detail, sizeof(out->detail), "eight unsigned byte planes on device " + std::to_string(m->device_id));
       return RNS8_SUCCESS;
     }
     out->device_residues_current = m->device_current ? 1u : 0u;
     out->uses_residue_storage = 1;
     out->device_residue_bytes = m->residue_bytes;
-    set_text(out->layout_version, sizeof(out->layout_version), "modulus_major_compact_row_major_i8_v1");
+    set_text(out->layout_version, sizeof(out->layout_version),
+             uses_finite_storage(m->desc.semantics) ? "finite_u8_centered_residue_v1" : "rns_centered_residue_planes_v1");
     set_text(out->detail, sizeof(out->detail), "centered int8 residue planes on device " + std::to_string(m->device_id));
     return RNS8_SUCCESS;
   });

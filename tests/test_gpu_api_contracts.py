@@ -168,3 +168,64 @@ def test_finite_oneshot_k_blocks(r8, ctx, oracle, modulus, field, k):
     np.testing.assert_array_equal(got, want)
     exact = (A.astype(object).dot(B.astype(object))) % modulus
     np.testing.assert_array_equal(got.astype(object), exact)
+
+
+class _PackingInfo(C.Structure):
+    _fields_ = [("struct_size", C.c_uint64), ("abi_version", C.c_uint32), ("backend", C.c_int32),
+                ("semantics", C.c_int32), ("uses_resident_matrix_inputs", C.c_uint32),
+                ("uses_transient_pack_workspace", C.c_uint32), ("uses_matrix_engine_pack_layout", C.c_uint32),
+                ("reusable_prepack_cache_available", C.c_uint32), ("production_prepack_cache_available", C.c_uint32),
+                ("flags", C.c_uint32), ("input_domain", C.c_int32), ("output_domain", C.c_int32),
+                ("output_host_current", C.c_uint32), ("output_device_current", C.c_uint32),
+                ("next_op_flags", C.c_uint32), ("reserved0", C.c_uint32), ("a_pack_workspace_bytes", C.c_uint64),
+                ("b_pack_workspace_bytes", C.c_uint64), ("accumulator_workspace_bytes", C.c_uint64),
+                ("library_workspace_bytes", C.c_uint64), ("total_transient_workspace_bytes", C.c_uint64),
+                ("input_domain_name", C.c_char * 64), ("output_domain_name", C.c_char * 64),
+                ("next_op_hint", C.c_char * 160), ("a_layout_version", C.c_char * 96),
+                ("b_layout_version", C.c_char * 96), ("output_layout_version", C.c_char * 96),
+                ("prepack_cache_scope", C.c_char * 96), ("detail", C.c_char * 256)]
+
+
+def test_plan_packing_info_contract_names(r8, ctx):
+    """tests/unit/test_api_plan_packing_cases.inc:1-110 on a device-resident
+    backend: bounded plans read and produce residue-current planes
+    (rns_centered_residue_planes_v1, next op: final export or RNS GEMM
+    "without logical export"), wrap64 plans byte limbs (wrap64_byte_limb_v1,
+    final export only), finite plans finite_u8_centered_residue_v1; output is
+    device-current; a short struct and a null plan are INVALID_ARGUMENT."""
+    S, BK = r8.Semantics, r8.BoundKind
+    lib = r8.lib()
+    RNS, FINITE, WRAP = 1, 3, 4
+    FINAL, RNS_GEMM = 1, 2
+
+    def info_of(plan, size=C.sizeof(_PackingInfo)):
+        info = _PackingInfo(struct_size=size, abi_version=1)
+        return lib.rns8_get_plan_packing_info(plan.handle if plan else None, C.byref(info)), info
+
+    cases = [
+        (r8.gemm_desc(S.BOUNDED_I64, BK.GLOBAL_MAX_ABS, 2, 3, 4, bound=16), RNS, FINAL | RNS_GEMM,
+         b"rns_residue_current", b"rns_centered_residue_planes_v1"),
+        (r8.gemm_desc(S.WRAP_U64_MOD_2_64, BK.NONE, 2, 2, 2), WRAP, FINAL, b"wrap64_byte_limb_current",
+         b"wrap64_byte_limb_v1"),
+        (r8.gemm_desc(S.FINITE_FIELD_U8, BK.NONE, 2, 2, 2, finite_modulus=251), FINITE, FINAL, b"finite_u8_current",
+         b"finite_u8_centered_residue_v1"),
+    ]
+    for desc, domain, next_op, domain_name, layout in cases:
+        plan = r8.Plan(ctx, desc)
+        st, info = info_of(plan)
+        assert st == 0
+        assert (info.semantics, info.uses_resident_matrix_inputs, info.uses_transient_pack_workspace,
+                info.uses_matrix_engine_pack_layout, info.reusable_prepack_cache_available) == (
+                    desc.semantics, 1, 0, 0, 0)
+        assert (info.input_domain, info.output_domain) == (domain, domain)
+        assert (info.output_host_current, info.output_device_current) == (0, 1)
+        assert info.next_op_flags == next_op
+        assert info.input_domain_name == domain_name and info.output_domain_name == domain_name
+        assert info.a_layout_version == layout and info.b_layout_version == layout
+        assert info.output_layout_version == layout
+        assert info.prepack_cache_scope == b"device_resident_no_prepack_cache"
+        if domain == RNS:
+            assert b"without logical export" in info.next_op_hint
+        assert info_of(plan, C.sizeof(_PackingInfo) - 1)[0] == 1
+        plan.close()
+    assert info_of(None)[0] == 1
