@@ -12,6 +12,8 @@
 // Host buffers are copied with cudaMemcpy2DAsync so caller leading dimensions
 // never reach the kernels, and every call ends with a stream synchronisation.
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cstring>
 #include <future>
 #include <limits>
@@ -432,12 +434,14 @@ rns8_status validate_typed_oneshot(const rns8_gemm_desc& d, rns8_semantics expec
 // when done) overlaps too. The result goes down only after every slab passed
 // the range check, so a RANGE_ERROR leaves C untouched.
 // Largest |x| of a row-major host matrix (x itself for uint64), over up to
-// 16 host threads.
+// 16 host threads shared with the other GPUs this process can see; the scan
+// gives up (returns ~0) once *stop is set.
 template <typename T>
-uint64_t host_max_magnitude(const T* src, int64_t rows, int64_t cols, int64_t ld) {
+uint64_t host_max_magnitude(const T* src, int64_t rows, int64_t cols, int64_t ld, const std::atomic<bool>* stop) {
   auto scan = [=](int64_t r0, int64_t r1) {
     uint64_t mx = 0;
     for (int64_t r = r0; r < r1; ++r) {
+      if (stop->load(std::memory_order_relaxed)) return ~uint64_t{0};
       const T* row = src + r * ld;
       for (int64_t c = 0; c < cols; ++c) {
         uint64_t v;
@@ -450,8 +454,10 @@ uint64_t host_max_magnitude(const T* src, int64_t rows, int64_t cols, int64_t ld
     }
     return mx;
   };
-  const int64_t hw = std::max<int64_t>(1, std::thread::hardware_concurrency());
-  const int64_t parts = std::min<int64_t>({hw, 16, rows});
+  int devices = 1;
+  if (cudaGetDeviceCount(&devices) != cudaSuccess || devices < 1) devices = 1;
+  const int64_t hw = std::max<int64_t>(1, std::thread::hardware_concurrency() / devices);
+  const int64_t parts = std::min<int64_t>({std::max<int64_t>(hw, 2), 16, rows});
   std::vector<std::future<uint64_t>> futures;
   const int64_t per = (rows + parts - 1) / parts;
   for (int64_t r0 = per; r0 < rows; r0 += per)
@@ -514,8 +520,12 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   // host as soon as it is exported, overlapping the uploads still in flight
   // (C stays untouched only on a RANGE_ERROR, which is then impossible);
   // otherwise C is copied after the status check.
-  auto max_a = std::async(std::launch::async, [=] { return host_max_magnitude(A, m, k, lda); });
+  std::atomic<bool> stop_scan{false};
+  auto max_a = std::async(std::launch::async, [&stop_scan, A, m, k, lda] {
+    return host_max_magnitude(A, m, k, lda, &stop_scan);
+  });
   std::vector<cudaEvent_t> events(2 * static_cast<size_t>(slabs) + 1, nullptr);
+  int last_slab = -1;  // the last slab whose export was issued
   auto destroy = [&] {
     for (cudaEvent_t& e : events)
       if (e) cudaEventDestroy(e);
@@ -551,6 +561,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
                     : rns8cuda::export_u64(rC, r, n, P, plan.desc.bound, reinterpret_cast<uint64_t*>(dC) + r0 * n, n,
                                            ctx->dev_status, ctx->stream)) == cudaSuccess &&
            cudaEventRecord(events[slabs + 1 + i], ctx->stream) == cudaSuccess;
+    if (ok) last_slab = i;
   }
   uint64_t max_b = ~uint64_t{0};
   bool early_ok = ok && cudaStreamWaitEvent(ctx->out_stream, events[0], 0) == cudaSuccess &&
@@ -559,6 +570,20 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
                   cudaMemcpyAsync(&max_b, d_max_b, sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->out_stream) ==
                       cudaSuccess &&
                   cudaStreamSynchronize(ctx->out_stream) == cudaSuccess;
+  // The proof is only worth waiting for while slabs are still being
+  // computed: once the last slab is exported, the checked path is as fast.
+  if (!early_ok || last_slab < 0) {
+    stop_scan.store(true);
+  } else {
+    const cudaEvent_t last_export = events[static_cast<size_t>(slabs + 1 + last_slab)];
+    while (max_a.wait_for(std::chrono::microseconds(200)) != std::future_status::ready) {
+      if (cudaEventQuery(last_export) != cudaErrorNotReady) {
+        stop_scan.store(true);
+        break;
+      }
+    }
+    (void)cudaGetLastError();  // a not-ready query leaves a non-sticky error behind
+  }
   // C written while A is still uploading must not overlap either input.
   auto span = [](const void* p, int64_t rows, int64_t cols, int64_t ld) {
     const auto lo = reinterpret_cast<uintptr_t>(p);
