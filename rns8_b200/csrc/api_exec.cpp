@@ -532,6 +532,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   };
   for (cudaEvent_t& e : events)
     if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      stop_scan.store(true);  // the scan's future joins on return
       destroy();
       return RNS8_BACKEND_FAILURE;
     }
