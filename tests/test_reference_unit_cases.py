@@ -530,3 +530,33 @@ def test_persistent_prefix9_exact_k_block_reused(r8):
             assert (out[:, 2] == s).all()
         for h in (a, b, c, ws, plan):
             h.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("signed", [True, False])
+def test_export_range_errors_repeat_without_side_effects(r8, signed):
+    """tests/differential/test_hip_direct_bounded_residency_cases.inc:179-306:
+    a prefix-1 plan (bound 10) exporting [-11, 7] (or [11, 3]) is a
+    RANGE_ERROR twice in a row, the destination keeps its fill, and the
+    matrix stays device-current."""
+    S, BK = r8.Semantics, r8.BoundKind
+    lib = r8.lib()
+    sem = S.BOUNDED_I64 if signed else S.BOUNDED_U64
+    bk = BK.GLOBAL_MAX_ABS if signed else BK.GLOBAL_MAX_UNSIGNED
+    with r8.Context(0) as ctx:
+        plan = r8.Plan(ctx, r8.gemm_desc(sem, bk, 1, 2, 1, bound=10))
+        assert plan.prefix == 1
+        c = r8.Matrix(ctx, 1, 2, sem, bk, 0)
+        if signed:
+            c.pack_i64(np.array([[-11, 7]], np.int64))
+            fill, out, fn = 0x1212121212121212, np.full(2, 0x1212121212121212, np.int64), lib.rns8_export_i64
+        else:
+            c.pack_u64(np.array([[11, 3]], np.uint64))
+            fill, out, fn = 0xFEFEFEFEFEFEFEFE, np.full(2, 0xFEFEFEFEFEFEFEFE, np.uint64), lib.rns8_export_u64
+        for _ in range(2):
+            assert fn(ctx.handle, plan.handle, c.handle, out.ctypes.data_as(C.c_void_p), 2) == RANGE
+            assert [int(x) for x in out] == [fill if not signed else 0x1212121212121212] * 2
+            si = c.storage_info()
+            assert (si.host_residues_current, si.device_residues_current) == (0, 1)
+        c.close()
+        plan.close()
