@@ -266,3 +266,19 @@ def test_unsigned_high_bit_fixed_width(r8):
         wide = f.export(2, 32)
         assert wide[0, 0, :2].tolist() == [0, 2**63] and (wide[0, 0, 2:] == 0).all() and (wide[0, 1] == 0).all()
         f.close()
+
+
+@pytest.mark.parametrize("signed", [True, False])
+def test_every_fixed_limb_width(r8, signed):
+    """tests/differential/test_hip_direct_exact_wide_residue_cases.inc:278-353:
+    C = -1 (signed) exports as all-ones limbs and C = 1 (unsigned) as 1
+    followed by zero limbs, at widths 1, 2, 3, 4, 8, 16 and 32."""
+    with r8.Context(0) as ctx:
+        f = Chain(r8, ctx, signed)
+        f.pack(0, [[-1 if signed else 1]], 1)
+        f.pack(1, [[1]], 1)
+        assert f.multiply(0, 1, 2) == OK
+        for width in (1, 2, 3, 4, 8, 16, 32):
+            limbs = f.export(2, width)[0, 0].tolist()
+            assert limbs == ([2**64 - 1] * width if signed else [1] + [0] * (width - 1)), width
+        f.close()
