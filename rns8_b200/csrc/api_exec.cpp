@@ -519,12 +519,8 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   // they do, no cell can be a RANGE_ERROR, so each slab of C goes back to the
   // host as soon as it is exported, overlapping the uploads still in flight
   // (C stays untouched only on a RANGE_ERROR, which is then impossible);
-  // otherwise C is copied after the status check. Only a process that sees
-  // one GPU takes this path: with several GPUs on the host, their uploads
-  // already share host memory, which the scan would read from too.
-  int visible_gpus = 0;
-  if (cudaGetDeviceCount(&visible_gpus) != cudaSuccess) visible_gpus = 0;
-  std::atomic<bool> stop_scan{visible_gpus != 1};
+  // otherwise C is copied after the status check.
+  std::atomic<bool> stop_scan{false};
   auto max_a = std::async(std::launch::async, [&stop_scan, A, m, k, lda] {
     return host_max_magnitude(A, m, k, lda, &stop_scan);
   });
@@ -569,7 +565,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
     if (ok) last_slab = i;
   }
   uint64_t max_b = ~uint64_t{0};
-  bool early_ok = ok && visible_gpus == 1 && cudaStreamWaitEvent(ctx->out_stream, events[0], 0) == cudaSuccess &&
+  bool early_ok = ok && cudaStreamWaitEvent(ctx->out_stream, events[0], 0) == cudaSuccess &&
                   rns8cuda::max_magnitude(dB, k * n, kSigned, d_max_b, ctx->sm_count, ctx->out_stream) ==
                       cudaSuccess &&
                   cudaMemcpyAsync(&max_b, d_max_b, sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->out_stream) ==
@@ -577,7 +573,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
                   cudaStreamSynchronize(ctx->out_stream) == cudaSuccess;
   // The proof is only worth waiting for while slabs are still being
   // computed: once the last slab is exported, the checked path is as fast.
-  if (!early_ok || last_slab < 0 || stop_scan.load()) {
+  if (!early_ok || last_slab < 0) {
     stop_scan.store(true);
   } else {
     const cudaEvent_t last_export = events[static_cast<size_t>(slabs + 1 + last_slab)];
@@ -599,8 +595,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   };
   const auto c_span = span(C, m, n, ldc);
   const bool disjoint = !overlap(c_span, span(A, m, k, lda)) && !overlap(c_span, span(B, k, n, ldb));
-  const bool early =
-      visible_gpus == 1 && bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok && disjoint;
+  const bool early = bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok && disjoint;
   if (ok && early) {
     for (int i = 0; early_ok && i < slabs; ++i) {
       const int64_t r0 = i * slab_rows;
