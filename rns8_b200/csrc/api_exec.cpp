@@ -519,8 +519,15 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   // they do, no cell can be a RANGE_ERROR, so each slab of C goes back to the
   // host as soon as it is exported, overlapping the uploads still in flight
   // (C stays untouched only on a RANGE_ERROR, which is then impossible);
-  // otherwise C is copied after the status check.
-  std::atomic<bool> stop_scan{false};
+  // otherwise C is copied after the status check. A process that sees more
+  // than four GPUs skips this: with that many GPUs uploading at once, host
+  // memory is the shared limit and the scan's extra reads of A cost more than
+  // the overlap gains (8 GPUs: 100.5 ms per rank step against 90.4 ms; 2 GPUs:
+  // 25.8 ms against 37.7 ms).
+  int visible_gpus = 0;
+  if (cudaGetDeviceCount(&visible_gpus) != cudaSuccess) visible_gpus = 0;
+  const bool try_early = visible_gpus >= 1 && visible_gpus <= 4;
+  std::atomic<bool> stop_scan{!try_early};
   auto max_a = std::async(std::launch::async, [&stop_scan, A, m, k, lda] {
     return host_max_magnitude(A, m, k, lda, &stop_scan);
   });
@@ -565,7 +572,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
     if (ok) last_slab = i;
   }
   uint64_t max_b = ~uint64_t{0};
-  bool early_ok = ok && cudaStreamWaitEvent(ctx->out_stream, events[0], 0) == cudaSuccess &&
+  bool early_ok = ok && try_early && cudaStreamWaitEvent(ctx->out_stream, events[0], 0) == cudaSuccess &&
                   rns8cuda::max_magnitude(dB, k * n, kSigned, d_max_b, ctx->sm_count, ctx->out_stream) ==
                       cudaSuccess &&
                   cudaMemcpyAsync(&max_b, d_max_b, sizeof(uint64_t), cudaMemcpyDeviceToHost, ctx->out_stream) ==
@@ -595,7 +602,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   };
   const auto c_span = span(C, m, n, ldc);
   const bool disjoint = !overlap(c_span, span(A, m, k, lda)) && !overlap(c_span, span(B, k, n, ldb));
-  const bool early = bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok && disjoint;
+  const bool early = try_early && bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok && disjoint;
   if (ok && early) {
     for (int i = 0; early_ok && i < slabs; ++i) {
       const int64_t r0 = i * slab_rows;
