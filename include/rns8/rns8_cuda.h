@@ -88,10 +88,14 @@ RNS8_API rns8_status rns8_cuda_gemm_export_bounded_device(int device_id, const i
  * exit; the call allocates nothing. Shapes whose split-K sums need more than
  * 8 MiB (prefix * m * n * 4 bytes when K is split) return
  * RNS8_WORKSPACE_TOO_SMALL. The first call on a device looks up the array's
- * device address (make it before any stream capture). All calls share the
- * array: each clears what must start at zero, and calls that overlap on the
- * GPU race. The call enqueues on `stream`, then synchronises that stream and
- * returns RNS8_BACKEND_FAILURE if a bounded device wait ran out. */
+ * device address (make it before any stream capture) and keeps it for the
+ * life of the process: do not call this across a cudaDeviceReset, which
+ * reloads the array elsewhere. All calls share the array: each clears what
+ * must start at zero, and calls that overlap on the GPU race. A device_id
+ * that is negative or not below the visible device count returns
+ * RNS8_INVALID_ARGUMENT; the caller's current device is unchanged on return.
+ * The call enqueues on `stream`, then synchronises that stream and returns
+ * RNS8_BACKEND_FAILURE if a bounded device wait ran out. */
 RNS8_API rns8_status rns8_cuda_gemm_rns_device_no_alloc(int device_id, const int8_t* d_a, const int8_t* d_b,
                                                         int8_t* d_c, int64_t m, int64_t n, int64_t k,
                                                         uint32_t prefix, void* stream);

@@ -92,7 +92,8 @@ bool exact_range_fits(rns8_semantics s, const i256& bound, const i256& product) 
 
 rns8_status device_exact_ranges(rns8_context& ctx, const void* d_src, bool is_signed, int64_t rows, int64_t cols,
                                 ExactRanges& out, i256& maximum) {
-  if (cudaSetDevice(ctx.device_id) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  DeviceScope scope(ctx.device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   std::lock_guard<std::mutex> lock(ctx.admission_mutex);
   using rns8cuda::AxisSummary;
   const uint64_t row_bytes = static_cast<uint64_t>(rows) * sizeof(AxisSummary);
@@ -142,7 +143,8 @@ rns8_status exact_gemm_bound(rns8_context& ctx, int64_t m, int64_t n, int64_t k,
   const AxisRange fb = uniform_axis(b_max, k);
   for (int64_t r = 0; r < m; ++r) h_in[r] = bound_input(a_rows ? (*a_rows)[r] : fa);
   for (int64_t c = 0; c < n; ++c) h_in[m + c] = bound_input(b_cols ? (*b_cols)[c] : fb);
-  if (cudaSetDevice(ctx.device_id) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  DeviceScope scope(ctx.device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   std::lock_guard<std::mutex> lock(ctx.admission_mutex);
   const uint64_t in_bytes = static_cast<uint64_t>(m + n) * sizeof(AxisBoundInput);
   const uint64_t stat_bytes = static_cast<uint64_t>(m + n) * sizeof(BoundStats);

@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <atomic>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <future>
 #include <limits>
@@ -25,11 +26,6 @@
 
 namespace rns8host {
 namespace {
-
-struct DeviceScope {
-  explicit DeviceScope(int dev) { ok = cudaSetDevice(dev) == cudaSuccess; }
-  bool ok;
-};
 
 rns8_status sync(rns8_context& ctx) { return cuda_status(cudaStreamSynchronize(ctx.stream)); }
 
@@ -433,11 +429,29 @@ rns8_status validate_typed_oneshot(const rns8_gemm_desc& d, rns8_semantics expec
 // are enqueued interleaved, so pageable host memory (whose copies return only
 // when done) overlaps too. The result goes down only after every slab passed
 // the range check, so a RANGE_ERROR leaves C untouched.
+// Processes on this host that run one-shots at the same time, and so share
+// its memory bandwidth: RNS8_CUDA_HOST_RANKS when set, else the launcher's
+// local world size (LOCAL_WORLD_SIZE from torchrun,
+// OMPI_COMM_WORLD_LOCAL_SIZE from Open MPI), else 1. The count of GPUs this
+// process can see says nothing about it: ranks started with one visible GPU
+// each still share the host.
+int host_ranks() {
+  for (const char* name : {"RNS8_CUDA_HOST_RANKS", "LOCAL_WORLD_SIZE", "OMPI_COMM_WORLD_LOCAL_SIZE"}) {
+    const char* v = std::getenv(name);
+    if (!v || !*v) continue;
+    char* end = nullptr;
+    const long n = std::strtol(v, &end, 10);
+    if (end && *end == '\0' && n >= 1 && n <= 4096) return static_cast<int>(n);
+  }
+  return 1;
+}
+
 // Largest |x| of a row-major host matrix (x itself for uint64), over up to
-// 16 host threads shared with the other GPUs this process can see; the scan
-// gives up (returns ~0) once *stop is set.
+// 16 host threads, the host's cores divided among `host_ranks` processes; the
+// scan gives up (returns ~0) once *stop is set.
 template <typename T>
-uint64_t host_max_magnitude(const T* src, int64_t rows, int64_t cols, int64_t ld, const std::atomic<bool>* stop) {
+uint64_t host_max_magnitude(const T* src, int64_t rows, int64_t cols, int64_t ld, int host_ranks,
+                            const std::atomic<bool>* stop) {
   auto scan = [=](int64_t r0, int64_t r1) {
     uint64_t mx = 0;
     for (int64_t r = r0; r < r1; ++r) {
@@ -454,9 +468,7 @@ uint64_t host_max_magnitude(const T* src, int64_t rows, int64_t cols, int64_t ld
     }
     return mx;
   };
-  int devices = 1;
-  if (cudaGetDeviceCount(&devices) != cudaSuccess || devices < 1) devices = 1;
-  const int64_t hw = std::max<int64_t>(1, std::thread::hardware_concurrency() / devices);
+  const int64_t hw = std::max<int64_t>(1, std::thread::hardware_concurrency() / std::max(1, host_ranks));
   const int64_t parts = std::min<int64_t>({std::max<int64_t>(hw, 2), 16, rows});
   std::vector<std::future<uint64_t>> futures;
   const int64_t per = (rows + parts - 1) / parts;
@@ -519,18 +531,19 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   // they do, no cell can be a RANGE_ERROR, so each slab of C goes back to the
   // host as soon as it is exported, overlapping the uploads still in flight
   // (C stays untouched only on a RANGE_ERROR, which is then impossible);
-  // otherwise C is copied after the status check. A process that sees more
-  // than four GPUs skips this: with that many GPUs uploading at once, host
-  // memory is the shared limit and the scan's extra reads of A cost more than
-  // the overlap gains (8 GPUs: 100.5 ms per rank step against 90.4 ms; 2 GPUs:
-  // 25.8 ms against 37.7 ms).
-  int visible_gpus = 0;
-  if (cudaGetDeviceCount(&visible_gpus) != cudaSuccess) visible_gpus = 0;
-  const bool try_early = visible_gpus >= 1 && visible_gpus <= 4;
+  // otherwise C is copied after the status check. When more than four
+  // processes on this host run one-shots at once, this is skipped and the
+  // scan never starts: host memory is then the shared limit and the scan's
+  // extra reads of A cost more than the overlap gains (8 ranks: 100.5 ms per
+  // rank step against 90.4 ms; 2 ranks: 25.8 ms against 37.7 ms).
+  const int ranks = host_ranks();
+  const bool try_early = ranks <= 4;
   std::atomic<bool> stop_scan{!try_early};
-  auto max_a = std::async(std::launch::async, [&stop_scan, A, m, k, lda] {
-    return host_max_magnitude(A, m, k, lda, &stop_scan);
-  });
+  std::future<uint64_t> max_a;
+  if (try_early)
+    max_a = std::async(std::launch::async, [&stop_scan, A, m, k, lda, ranks] {
+      return host_max_magnitude(A, m, k, lda, ranks, &stop_scan);
+    });
   std::vector<cudaEvent_t> events(2 * static_cast<size_t>(slabs) + 1, nullptr);
   int last_slab = -1;  // the last slab whose export was issued
   auto destroy = [&] {
@@ -580,7 +593,9 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
                   cudaStreamSynchronize(ctx->out_stream) == cudaSuccess;
   // The proof is only worth waiting for while slabs are still being
   // computed: once the last slab is exported, the checked path is as fast.
-  if (!early_ok || last_slab < 0) {
+  if (!try_early) {
+    // no scan was started
+  } else if (!early_ok || last_slab < 0) {
     stop_scan.store(true);
   } else {
     const cudaEvent_t last_export = events[static_cast<size_t>(slabs + 1 + last_slab)];
@@ -602,7 +617,7 @@ rns8_status bounded_oneshot_pipelined(rns8_context* ctx, const rns8_plan& plan, 
   };
   const auto c_span = span(C, m, n, ldc);
   const bool disjoint = !overlap(c_span, span(A, m, k, lda)) && !overlap(c_span, span(B, k, n, ldb));
-  const bool early = try_early && bound_proven(max_a.get(), max_b, k, plan.desc.bound) && early_ok && disjoint;
+  const bool early = try_early && early_ok && disjoint && bound_proven(max_a.get(), max_b, k, plan.desc.bound);
   if (ok && early) {
     for (int i = 0; early_ok && i < slabs; ++i) {
       const int64_t r0 = i * slab_rows;

@@ -153,6 +153,41 @@ bool valid_abi(uint64_t struct_size, uint32_t abi_version, size_t expected);
 void set_text(char* dst, size_t cap, const std::string& s);
 rns8_status cuda_status(cudaError_t e);
 
+// Makes `dev` the calling thread's current device for the life of the scope
+// and puts the caller's current device back when it ends, so that no entry
+// point leaves the thread on another device than it found it on. `ok` is
+// false when `dev` is negative or cannot be made current.
+class DeviceScope {
+ public:
+  explicit DeviceScope(int dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) {
+      (void)cudaGetLastError();
+      prev_ = -1;
+    }
+    if (dev < 0) return;
+    if (prev_ == dev) {
+      ok = true;
+      return;
+    }
+    ok = cudaSetDevice(dev) == cudaSuccess;
+    switched_ = ok;
+    if (!ok) (void)cudaGetLastError();
+  }
+  ~DeviceScope() {
+    if (switched_ && prev_ >= 0) (void)cudaSetDevice(prev_);
+  }
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+  bool ok = false;
+
+ private:
+  int prev_ = -1;
+  bool switched_ = false;
+};
+
+// Number of CUDA devices visible to this process (0 when none or on error).
+int visible_device_count();
+
 // Contract arithmetic (reference src/core/moduli.cpp).
 i256 modulus_product(uint32_t prefix);
 uint32_t required_prefix_for_range(const i256& range);

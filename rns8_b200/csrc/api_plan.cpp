@@ -32,6 +32,15 @@ void set_text(char* dst, size_t cap, const std::string& s) {
 
 rns8_status cuda_status(cudaError_t e) { return e == cudaSuccess ? RNS8_SUCCESS : RNS8_BACKEND_FAILURE; }
 
+int visible_device_count() {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return count;
+}
+
 i256 modulus_product(uint32_t prefix) {
   i256 p = i256::from_u64(1);
   for (uint32_t i = 0; i < prefix && i < static_cast<uint32_t>(rns8ladder::kCount); ++i)

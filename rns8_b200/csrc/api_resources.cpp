@@ -17,7 +17,8 @@ rns8_status DevBuf::ensure(int dev, uint64_t need) {
   release();
   if (need == 0) return RNS8_SUCCESS;
   void* p = nullptr;
-  if (cudaSetDevice(dev) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  DeviceScope scope(dev);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   const cudaError_t e = cudaMalloc(&p, need);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
@@ -31,11 +32,8 @@ rns8_status DevBuf::ensure(int dev, uint64_t need) {
 
 void DevBuf::release() {
   if (ptr) {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (device >= 0 && cur != device) cudaSetDevice(device);
+    DeviceScope scope(device);
     cudaFree(ptr);
-    if (cur >= 0 && cur != device) cudaSetDevice(cur);
   }
   ptr = nullptr;
   bytes = 0;
@@ -68,7 +66,8 @@ extern "C" rns8_status rns8_create_context(int device_id, const rns8_context_opt
     cudaDeviceProp prop{};
     if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return RNS8_BACKEND_FAILURE;
     if (prop.major != 10 || prop.minor != 0) return RNS8_UNSUPPORTED_ARCH;  // kernels are built for sm_100a only
-    if (cudaSetDevice(dev) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+    DeviceScope scope(dev);
+    if (!scope.ok) return RNS8_BACKEND_FAILURE;
     auto* ctx = new (std::nothrow) rns8_context();
     if (!ctx) return RNS8_INTERNAL_ERROR;
     ctx->device_id = dev;
@@ -106,7 +105,7 @@ extern "C" rns8_status rns8_create_context(int device_id, const rns8_context_opt
 
 extern "C" rns8_status rns8_destroy_context(rns8_context* ctx) {
   if (!ctx) return RNS8_SUCCESS;
-  cudaSetDevice(ctx->device_id);
+  DeviceScope scope(ctx->device_id);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
   if (ctx->out_stream) cudaStreamSynchronize(ctx->out_stream);
@@ -197,8 +196,8 @@ extern "C" rns8_status rns8_create_matrix(rns8_context* ctx, const rns8_matrix_d
     mtx->prefix = prefix;
     mtx->device_id = ctx->device_id;
     mtx->residue_bytes = cells * planes;
-    if (cudaSetDevice(ctx->device_id) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void**>(&mtx->residues), mtx->residue_bytes) != cudaSuccess) {
+    DeviceScope scope(ctx->device_id);
+    if (!scope.ok || cudaMalloc(reinterpret_cast<void**>(&mtx->residues), mtx->residue_bytes) != cudaSuccess) {
       (void)cudaGetLastError();
       delete mtx;
       return RNS8_BACKEND_FAILURE;
@@ -221,7 +220,7 @@ extern "C" rns8_status rns8_create_matrix(rns8_context* ctx, const rns8_matrix_d
 
 extern "C" rns8_status rns8_destroy_matrix(rns8_matrix* matrix) {
   if (!matrix) return RNS8_SUCCESS;
-  cudaSetDevice(matrix->device_id);
+  DeviceScope scope(matrix->device_id);
   if (matrix->residues) cudaFree(matrix->residues);
   delete matrix;
   return RNS8_SUCCESS;

@@ -10,7 +10,6 @@ using rns8host::cuda_status;
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
-bool set_device(int device_id) { return device_id >= 0 && cudaSetDevice(device_id) == cudaSuccess; }
 
 int sm_count_of(int device_id) {
   int count = 0;
@@ -37,7 +36,8 @@ extern "C" rns8_status rns8_cuda_pack_i64_device(int device_id, const int64_t* d
                                                  int64_t ld, uint32_t prefix, int8_t* d_planes, void* stream) {
   if (!d_src || !d_planes || !rns8host::valid_matrix_access(rows, cols, ld) || !valid_prefix(prefix))
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::pack_i64(d_src, rows, cols, ld, prefix, d_planes, as_stream(stream)));
 }
 
@@ -45,7 +45,8 @@ extern "C" rns8_status rns8_cuda_pack_u64_device(int device_id, const uint64_t* 
                                                  int64_t ld, uint32_t prefix, int8_t* d_planes, void* stream) {
   if (!d_src || !d_planes || !rns8host::valid_matrix_access(rows, cols, ld) || !valid_prefix(prefix))
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::pack_u64(d_src, rows, cols, ld, prefix, d_planes, as_stream(stream)));
 }
 
@@ -53,7 +54,8 @@ extern "C" rns8_status rns8_cuda_pack_finite_u8_device(int device_id, const uint
                                                        int64_t ld, uint16_t modulus, int8_t* d_residues, void* stream) {
   if (!d_src || !d_residues || !rns8host::valid_matrix_access(rows, cols, ld) || modulus < 2 || modulus > 256)
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::pack_finite_u8(d_src, rows, cols, ld, modulus, d_residues, as_stream(stream)));
 }
 
@@ -85,7 +87,8 @@ extern "C" rns8_status rns8_cuda_gemm_rns_device(int device_id, const int8_t* d_
   const rns8cuda::GemmPath path = path_of(gemm_path, &path_ok);
   if (!d_a || !d_b || !d_c || !d_status || m <= 0 || n <= 0 || k <= 0 || !valid_prefix(prefix) || !path_ok)
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   const rns8cuda::PlaneGemmTask task{d_a, d_b, d_c};
   const auto prob = seam_problem(m, n, k, prefix, 0, &task, 1);
   return launch_result(rns8cuda::plane_gemm(prob, path, sm_count_of(device_id), d_scratch, scratch_bytes, d_status,
@@ -113,7 +116,8 @@ extern "C" rns8_status rns8_cuda_gemm_export_bounded_device(int device_id, const
                                   : rns8host::validate_bound_contract(RNS8_BOUNDED_U64,
                                                                       RNS8_BOUND_GLOBAL_MAX_UNSIGNED, bound, prefix);
   if (c != RNS8_SUCCESS) return c;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   const rns8cuda::PlaneGemmTask task{d_a, d_b, nullptr};
   const auto prob = seam_problem(m, n, k, prefix, 0, &task, 1);
   return launch_result(rns8cuda::gemm_export_bounded(prob, is_signed != 0, bound, d_out, ld, sm_count_of(device_id),
@@ -146,7 +150,8 @@ extern "C" rns8_status rns8_cuda_gemm_finite_u8_grouped_device(int device_id, co
     if (!d_a[t] || !d_b[t] || !d_c[t]) return RNS8_INVALID_ARGUMENT;
     tasks[t] = {d_a[t], d_b[t], d_c[t]};
   }
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   const auto prob = seam_problem(m, n, k, 1, modulus, tasks.data(), task_count);
   return launch_result(rns8cuda::plane_gemm(prob, path, sm_count_of(device_id), d_scratch, scratch_bytes, d_status,
                                             as_stream(stream)));
@@ -159,7 +164,8 @@ extern "C" rns8_status rns8_cuda_export_i64_device(int device_id, const int8_t* 
     return RNS8_INVALID_ARGUMENT;
   const rns8_status c = rns8host::validate_bound_contract(RNS8_BOUNDED_I64, RNS8_BOUND_GLOBAL_MAX_ABS, bound, prefix);
   if (c != RNS8_SUCCESS) return c;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::export_i64(d_planes, m, n, prefix, bound, d_dst, ld, d_status, as_stream(stream)));
 }
 
@@ -171,7 +177,8 @@ extern "C" rns8_status rns8_cuda_export_u64_device(int device_id, const int8_t* 
   const rns8_status c =
       rns8host::validate_bound_contract(RNS8_BOUNDED_U64, RNS8_BOUND_GLOBAL_MAX_UNSIGNED, bound, prefix);
   if (c != RNS8_SUCCESS) return c;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::export_u64(d_planes, m, n, prefix, bound, d_dst, ld, d_status, as_stream(stream)));
 }
 
@@ -181,7 +188,8 @@ extern "C" rns8_status rns8_cuda_export_limbs_device(int device_id, const int8_t
   if (!d_planes || !d_dst || !d_status || !rns8host::valid_matrix_access(m, n, ld) || !valid_prefix(prefix) ||
       limb_count == 0 || limb_count > 32)
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::export_limbs(d_planes, m, n, prefix, is_signed != 0, limb_count, d_dst, ld, d_status,
                                               as_stream(stream)));
 }
@@ -190,14 +198,16 @@ extern "C" rns8_status rns8_cuda_export_finite_u8_device(int device_id, const in
                                                          uint16_t modulus, uint8_t* d_dst, int64_t ld, void* stream) {
   if (!d_residues || !d_dst || !rns8host::valid_matrix_access(m, n, ld) || modulus < 2 || modulus > 256)
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::export_finite_u8(d_residues, m, n, modulus, d_dst, ld, as_stream(stream)));
 }
 
 extern "C" rns8_status rns8_cuda_pack_wrap_u64_device(int device_id, const uint64_t* d_src, int64_t rows, int64_t cols,
                                                     int64_t ld, uint8_t* d_limbs, void* stream) {
   if (!d_src || !d_limbs || !rns8host::valid_matrix_access(rows, cols, ld)) return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::wrap_pack_u64(d_src, rows, cols, ld, d_limbs, as_stream(stream)));
 }
 
@@ -209,7 +219,8 @@ extern "C" rns8_status rns8_cuda_gemm_wrap_u64_device(int device_id, const uint8
   if (!ok || !d_a_limbs || !d_b_limbs || !d_c || m <= 0 || n <= 0 || k <= 0) return RNS8_INVALID_ARGUMENT;
   if (!rns8host::valid_matrix_access(m, k, k) || !rns8host::valid_matrix_access(k, n, n)) return RNS8_INVALID_ARGUMENT;
   if (!d_status && path != rns8cuda::GemmPath::Simt) return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::wrap_gemm(d_a_limbs, d_b_limbs, d_c, m, n, k, path, sm_count_of(device_id), d_status,
                                            as_stream(stream)));
 }
@@ -217,6 +228,7 @@ extern "C" rns8_status rns8_cuda_gemm_wrap_u64_device(int device_id, const uint8
 extern "C" rns8_status rns8_cuda_export_wrap_u64_device(int device_id, const uint8_t* d_limbs, int64_t rows,
                                                       int64_t cols, uint64_t* d_dst, int64_t ld, void* stream) {
   if (!d_limbs || !d_dst || !rns8host::valid_matrix_access(rows, cols, ld)) return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::wrap_export_u64(d_limbs, rows, cols, d_dst, ld, as_stream(stream)));
 }

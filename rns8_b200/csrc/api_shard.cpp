@@ -10,7 +10,6 @@ namespace {
 
 using rns8host::cuda_status;
 
-bool set_device(int device_id) { return device_id >= 0 && cudaSetDevice(device_id) == cudaSuccess; }
 
 int sm_count_of(int device_id) {
   int count = 0;
@@ -50,7 +49,8 @@ extern "C" rns8_status rns8_cuda_pack_i64_planes_device(int device_id, const int
                                                         uint32_t plane_count, int8_t* d_planes, void* stream) {
   if (!d_src || !d_planes || !rns8host::valid_matrix_access(rows, cols, ld) || !valid_planes(plane_index, plane_count))
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::pack_planes_i64(d_src, rows, cols, ld, plane_index, plane_count, d_planes,
                                                  static_cast<cudaStream_t>(stream)));
 }
@@ -60,7 +60,8 @@ extern "C" rns8_status rns8_cuda_pack_u64_planes_device(int device_id, const uin
                                                         uint32_t plane_count, int8_t* d_planes, void* stream) {
   if (!d_src || !d_planes || !rns8host::valid_matrix_access(rows, cols, ld) || !valid_planes(plane_index, plane_count))
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return launch_result(rns8cuda::pack_planes_u64(d_src, rows, cols, ld, plane_index, plane_count, d_planes,
                                                  static_cast<cudaStream_t>(stream)));
 }
@@ -88,7 +89,8 @@ extern "C" rns8_status rns8_cuda_gemm_rns_slabs_device(int device_id, const int8
       slab_count == 0 || slab_count > static_cast<uint32_t>(rns8cuda::kMaxSlabs) || slab_rows <= 0 ||
       exchange > RNS8_CUDA_EXCHANGE_COPY)
     return RNS8_INVALID_ARGUMENT;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   const rns8cuda::PlaneGemmTask task{d_a, d_b, nullptr};
   const rns8cuda::PlaneGemmProblem prob = subset_problem(m, n, k, plane_index, plane_count, &task);
   const rns8cuda::SlabScatter sc{slab_dst, slab_rows, slab_count, plane_index};
@@ -103,7 +105,8 @@ extern "C" rns8_status rns8_cuda_gemm_rns_slabs_device(int device_id, const int8
 extern "C" rns8_status rns8_cuda_ipc_alloc(int device_id, uint64_t bytes, void** d_ptr, uint8_t* handle) {
   if (!d_ptr || !handle || bytes == 0) return RNS8_INVALID_ARGUMENT;
   *d_ptr = nullptr;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   void* p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess) return RNS8_INTERNAL_ERROR;
   cudaIpcMemHandle_t h{};
@@ -119,14 +122,16 @@ extern "C" rns8_status rns8_cuda_ipc_alloc(int device_id, uint64_t bytes, void**
 
 extern "C" rns8_status rns8_cuda_ipc_free(int device_id, void* d_ptr) {
   if (!d_ptr) return RNS8_SUCCESS;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return cudaFree(d_ptr) == cudaSuccess ? RNS8_SUCCESS : RNS8_BACKEND_FAILURE;
 }
 
 extern "C" rns8_status rns8_cuda_ipc_open(int device_id, const uint8_t* handle, void** d_ptr) {
   if (!handle || !d_ptr) return RNS8_INVALID_ARGUMENT;
   *d_ptr = nullptr;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   cudaIpcMemHandle_t h{};
   std::memcpy(&h, handle, sizeof(h));
   void* p = nullptr;
@@ -137,6 +142,7 @@ extern "C" rns8_status rns8_cuda_ipc_open(int device_id, const uint8_t* handle, 
 
 extern "C" rns8_status rns8_cuda_ipc_close(int device_id, void* d_ptr) {
   if (!d_ptr) return RNS8_SUCCESS;
-  if (!set_device(device_id)) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   return cudaIpcCloseMemHandle(d_ptr) == cudaSuccess ? RNS8_SUCCESS : RNS8_BACKEND_FAILURE;
 }

@@ -13,10 +13,13 @@
 // The array's name is only a host-side stand-in in host code, so the device
 // address is looked up once per device (with that device current) through
 // cudaGetSymbolAddress and passed to the kernels. The first call on a device
-// performs that look-up; make it before any stream capture. Every call shares
-// the array and it keeps the last call's contents, so each call clears the
-// status word and the split-K sums before use; calls that overlap on the GPU
-// (other streams, other host threads on the same device) race on it.
+// performs that look-up; make it before any stream capture. The address is
+// kept for the life of the process, so the entry point must not be used
+// across a cudaDeviceReset (or a release and re-creation of the primary
+// context), which loads the array at a new address. Every call shares the
+// array and it keeps the last call's contents, so each call clears the status
+// word and the split-K sums before use; calls that overlap on the GPU (other
+// streams, other host threads on the same device) race on it.
 #include <mutex>
 
 #include "api_internal.hpp"
@@ -52,11 +55,16 @@ extern "C" rns8_status rns8_cuda_gemm_rns_device_no_alloc(int device_id, const i
                                                           int8_t* d_c, int64_t m, int64_t n, int64_t k,
                                                           uint32_t prefix, void* stream) {
   if (!d_a || !d_b || !d_c || m <= 0 || n <= 0 || k <= 0 || prefix == 0 || prefix > RNS8_MAX_SUPPORTED_PREFIX ||
-      device_id < 0 || device_id >= kMaxDevices)
+      device_id < 0 || device_id >= kMaxDevices || device_id >= rns8host::visible_device_count())
     return RNS8_INVALID_ARGUMENT;
-  if (cudaSetDevice(device_id) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);  // the caller's current device is restored on return
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned char* base = nullptr;
-  if (scratch_address(device_id, &base) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  if (scratch_address(device_id, &base) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return RNS8_BACKEND_FAILURE;
+  }
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_id) != cudaSuccess || sms <= 0)
     return RNS8_BACKEND_FAILURE;
@@ -80,7 +88,6 @@ extern "C" rns8_status rns8_cuda_gemm_rns_device_no_alloc(int device_id, const i
     need = kNoAllocScratchBytes;
   }
 
-  const cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint32_t* status = reinterpret_cast<uint32_t*>(base);
   void* scratch = need ? base + kStatusAreaBytes : nullptr;
   if (cudaMemsetAsync(status, 0, sizeof(uint32_t), s) != cudaSuccess) return RNS8_BACKEND_FAILURE;

@@ -29,7 +29,8 @@ extern "C" rns8_status rns8_cuda_wait_probe(int device_id, uint32_t arrive, uint
   if (!d_status || arrive > 1 || budget_cycles == 0 ||
       budget_cycles > static_cast<uint64_t>(rns8cuda::kWaitBudgetCycles))
     return RNS8_INVALID_ARGUMENT;
-  if (device_id < 0 || cudaSetDevice(device_id) != cudaSuccess) return RNS8_BACKEND_FAILURE;
+  rns8host::DeviceScope scope(device_id);
+  if (!scope.ok) return RNS8_BACKEND_FAILURE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s) != cudaSuccess) return RNS8_BACKEND_FAILURE;
   wait_probe_kernel<<<1, 32, 0, s>>>(d_status, arrive, static_cast<long long>(budget_cycles));

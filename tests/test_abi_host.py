@@ -58,6 +58,26 @@ def test_struct_layouts_match_c(tmp_path, rns8):
         assert C.sizeof(structs[name]) == int(size), name
 
 
+def test_abi_layout_matches_reference_header():
+    """Every struct size, field offset, enumerator and numeric macro of the
+    reference's public headers (tests/golden/abi_layout.json, generated from
+    doublemover/RNS8 include/rns8 by tests/golden/make_abi_layout.py) is the
+    same in include/rns8, as the C compiler lays them out."""
+    import importlib.util
+    import json
+
+    spec = importlib.util.spec_from_file_location("make_abi_layout", ROOT / "tests" / "golden" / "make_abi_layout.py")
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    want = json.loads((ROOT / "tests" / "golden" / "abi_layout.json").read_text())
+    names = {"structs": {s: list(f) for s, f in want["offsetof"].items()}, "enums": list(want["enums"]),
+             "macros": list(want["macros"])}
+    assert len(names["structs"]) == 20 and sum(len(f) for f in names["structs"].values()) == 443
+    got = gen.probe(INCLUDE, names)
+    for key in ("sizeof", "offsetof", "enums", "macros"):
+        assert got[key] == want[key], key
+
+
 def test_status_and_ladder_queries(rns8, oracle):
     lib = rns8.lib()
     assert lib.rns8_status_string(0) == b"success"

@@ -20,6 +20,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 LADDER = [256, 255, 253, 251, 247, 239, 233, 229, 227, 223, 217, 211, 199, 197, 193, 191, 181, 179, 173, 167]
+INVALID_ARGUMENT = 1
 WORKSPACE_TOO_SMALL = 7
 
 
@@ -47,6 +48,8 @@ def residues(rng, planes, rows, cols):
     (256, 256, 8192, 8),   # few output tiles: K is split, the array holds the int32 sums
     (1024, 1024, 512, 9),  # 288 tiles, no split: only the status word is used
     (130, 272, 2048, 3),   # ragged tails with a split
+    (130, 272, 1000, 3),   # K % 16 != 0: zero-padded plane copies fit in the array
+    (512, 512, 1000, 9),   # K % 16 != 0 and the padded copies exceed 8 MiB: CUDA-core kernels on the array
 ])
 def test_no_alloc_matches_allocating_entry_point(lib, m, n, k, prefix):
     rng = np.random.default_rng(m + n + k + prefix)
@@ -83,3 +86,25 @@ def test_no_alloc_rejects_problems_beyond_the_array(lib):
                                                   stream) == WORKSPACE_TOO_SMALL
     torch.cuda.synchronize()
     assert bool((c == 5).all())
+
+
+def test_no_alloc_device_id_and_current_device(lib):
+    # A device id the process cannot see is the caller's mistake, and the call
+    # leaves the caller's current device as it found it.
+    m = n = k = 64
+    a = torch.zeros((1, m, k), dtype=torch.int8, device="cuda")
+    b = torch.zeros((1, k, n), dtype=torch.int8, device="cuda")
+    c = torch.full((1, m, n), 5, dtype=torch.int8, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    count = torch.cuda.device_count()
+    for bad in (-1, count, count + 7):
+        assert lib.rns8_cuda_gemm_rns_device_no_alloc(bad, a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, 1,
+                                                      stream) == INVALID_ARGUMENT
+    torch.cuda.synchronize()
+    assert bool((c == 5).all())
+    before = torch.cuda.current_device()
+    assert lib.rns8_cuda_gemm_rns_device_no_alloc(0, a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, 1,
+                                                  stream) == 0
+    assert torch.cuda.current_device() == before
+    torch.cuda.synchronize()
+    assert bool((c == 0).all())
