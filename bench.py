@@ -66,7 +66,7 @@ class Config:
     batch: int = 1
     modulus: int = 0
     limbs: int = 0
-    cpu_rows: int = 128  # rows of A in the CPU sample
+    sample: int = 128    # CPU sample: rows of A (whole tasks for the batched finite config)
 
     @property
     def ops(self) -> float:
@@ -77,23 +77,23 @@ class Config:
 CONFIGS = {
     "C1": Config("C1", "i64", 512, 512, 512, -(2**20), 2**20, 7, False,
                  "RNS8_BOUNDED_I64 512^3, U[-2^20,2^20], bound 2^49, prefix 7 default (BASELINE config 1)",
-                 bound=2**49, cpu_rows=512),
+                 bound=2**49, sample=512),
     "C2": Config("C2", "finite", 2048, 2048, 2048, 0, 250, 1, False,
                  "RNS8_FINITE_FIELD_U8 modulus 251, 64 x 2048^3 grouped, U[0,250] (BASELINE config 2)",
-                 batch=64, modulus=251, cpu_rows=256),
+                 batch=64, modulus=251, sample=8),
     "C3": Config("C3", "i64", 8192, 8192, 8192, -(2**24), 2**24, 9, True,
                  "RNS8_BOUNDED_I64 8192^3 prefix-9 forced, U[-2^24,2^24], bound 2^61 (BASELINE config 3)",
-                 bound=2**61, cpu_rows=128),
+                 bound=2**61, sample=1024),
     "C4": Config("C4", "u64", 256, 256, 262144, 0, 2**22 - 1, 8, False,
                  "RNS8_BOUNDED_U64 256x256x262144, U[0,2^22), bound 2^62, prefix 8 default (BASELINE config 4)",
-                 bound=2**62, cpu_rows=16),
+                 bound=2**62, sample=256),
     "C5": Config("C5", "exact", 4096, 4096, 4096, -(2**63), 2**63 - 1, 20, True,
                  "RNS8_EXACT_WIDE_SIGNED 4096^3, U[INT64_MIN,INT64_MAX], 3 limbs, prefix 20 forced "
-                 "(BASELINE config 5)", limbs=3, cpu_rows=16),
+                 "(BASELINE config 5)", limbs=3, sample=512),
     # Not a BASELINE config: the WRAP_U64_MOD_2_64 path at the C3 shape.
     "W": Config("W", "wrap", 8192, 8192, 8192, 0, 2**64 - 1, 8, False,
                 "RNS8_WRAP_U64_MOD_2_64 8192^3, U[0,2^64) (36 byte-pair products on the tensor cores)",
-                cpu_rows=64),
+                sample=1024),
 }
 
 
@@ -104,9 +104,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="C3")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-rows", type=int, default=0, help="rows of A in the CPU baseline sample (0: the config's)")
+    ap.add_argument("--sample", type=int, default=0,
+                    help="CPU sample (rows of A; tasks for C2) for the oracle parity check, the CPU baseline and the "
+                         "reference arm (0: the config's)")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle comparison (and the CPU baseline)")
     ap.add_argument("--size", type=int, default=0,
                     help="C3 only: M = N = K = size (8192 is the benchmark; smaller sizes are for ncu captures)")
     ap.add_argument("--shard", choices=["weak-rows", "rows", "planes"], default="weak-rows",
@@ -125,8 +127,9 @@ def parse():
         if cfg.name != "C3":
             ap.error("--size applies to C3 only")
         cfg = dataclasses.replace(cfg, m=args.size, n=args.size, k=args.size)
-    if args.cpu_rows:
-        cfg = dataclasses.replace(cfg, cpu_rows=args.cpu_rows)
+    if args.sample:
+        cfg = dataclasses.replace(cfg, sample=args.sample)
+    cfg = dataclasses.replace(cfg, sample=min(cfg.sample, cfg.batch if cfg.kind == "finite" else cfg.m))
     return args, cfg
 
 
@@ -253,93 +256,156 @@ def profile_traffic(cfg: Config, kernel: str) -> int | None:
         return None
 
 
-# ----------------------------------------------------------------- CPU baseline
-def host_inputs(cfg: Config, rows: int, seed: int):
-    """Seeded host inputs for the CPU sample: a rows-row slab of A and all of B."""
+# ------------------------------------------------------------- seeded inputs
+# The reference benchmark's generator (rns8_bench_types.hpp:72 seed = 1;
+# rns8_bench_bounded_i64_lane.inc:11-16): one std::mt19937_64 draws all of A,
+# then all of B, row-major, each value from std::uniform_int_distribution over
+# the config's range (uint32_t per byte for the finite lanes,
+# rns8_bench_finite_lanes.inc:28-31). The generator is the CPU checker's
+# (libstdc++ through the oracle library), so the GPU arm, the oracle parity
+# check, the CPU baseline and the reference arm all see the same inputs.
+SEED = 1
+
+
+def seeded_inputs(cfg: Config, rank: int = 0):
+    """Host A and B of this rank. Rank 0's are exactly the reference bench's
+    draws; rank r > 0 (weak scaling) draws its own A slab from seed 1 + r and
+    shares rank 0's B (the engine of seed 1 skips rank 0's A)."""
     import numpy as np
 
-    rng = np.random.default_rng(seed)
-    if cfg.kind == "finite":
-        A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.uint8, endpoint=True)
-        B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.uint8, endpoint=True)
-    elif cfg.kind in ("u64", "wrap"):
-        A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.uint64, endpoint=True)
-        B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.uint64, endpoint=True)
+    from oracle import bridge
+
+    m, n, k, bt = cfg.m, cfg.n, cfg.k, cfg.batch
+    if cfg.kind == "finite":  # batched: A_t then B_t for each task t
+        rng = bridge.Rng(SEED + rank)
+        A = np.empty((bt, m, k), np.uint8)
+        B = np.empty((bt, k, n), np.uint8)
+        for t in range(bt):
+            A[t] = rng.u8(cfg.hi, (m, k))
+            B[t] = rng.u8(cfg.hi, (k, n))
+        return A, B
+    unsigned = cfg.kind in ("u64", "wrap")
+    draw = (lambda r, shape: r.u64(cfg.lo, cfg.hi, shape)) if unsigned else (lambda r, shape: r.i64(cfg.lo, cfg.hi,
+                                                                                                      shape))
+    rng = bridge.Rng(SEED)
+    if rank == 0:
+        A = draw(rng, (m, k))
     else:
-        A = rng.integers(cfg.lo, cfg.hi, (rows, cfg.k), dtype=np.int64, endpoint=True)
-        B = rng.integers(cfg.lo, cfg.hi, (cfg.k, cfg.n), dtype=np.int64, endpoint=True)
+        (rng.skip_u64 if unsigned else rng.skip_i64)(cfg.lo, cfg.hi, m * k)
+        A = draw(bridge.Rng(SEED + rank), (m, k))
+    B = draw(rng, (k, n))
     return A, B
 
 
-def cpu_baseline(cfg: Config, rows: int) -> dict:
-    """The CPU oracle (a restatement of the reference's src/cpu path, OpenMP over
-    all host cores) on a row slab of the workload, scaled to the whole step.
+def fnv_checksum(values) -> int:
+    """The reference benchmark's output checksum (rns8_bench_support.cpp:96-99):
+    h = 1469598103934665603; h ^= v; h *= 1099511628211 over the outputs in
+    memory order, each widened to uint64."""
+    import numpy as np
 
-    B is packed once, as in the full workload; the slab's own stages (pack A,
-    the plane GEMMs, the export) are timed on `rows` rows. The full step is
-    t_pack_B + (M / rows) * t_slab per product (x batch for C2), and value is
-    the workload's effective ops over that time."""
+    from oracle import bridge
+
+    v = np.ascontiguousarray(values)
+    if v.dtype.itemsize == 8:
+        return bridge.checksum(v.reshape(v.shape[0], -1))
+    h = 1469598103934665603
+    flat = v.reshape(-1)
+    step = 1 << 22
+    # FNV is sequential: chain the chunks through the running hash.
+    for i in range(0, flat.size, step):
+        chunk = flat[i:i + step].astype(np.uint64)
+        h = int(bridge.lib().oracle_checksum_u64_from(h, bridge._p(chunk), chunk.size))
+    return h
+
+
+# ----------------------------------------------------------------- CPU sample
+def cpu_sample(cfg: Config, A, B, sample: int):
+    """The CPU oracle (a restatement of the reference's src/cpu path, OpenMP
+    over all host threads) on a bounded sample of the workload: rows [0,
+    sample) of A against all of B (whole tasks for the batched finite config).
+
+    Returns (info, out): out is the oracle's output for the sample, which the
+    GPU's must equal bit for bit. B's pack serves all M rows in the full
+    workload, so a sample step is charged t_slab + (sample / M) * t_pack_B;
+    value = the sample's effective ops over that time. `wall_s` is what the
+    sample actually took."""
+    import numpy as np
+
     from oracle import bridge
 
     lib = bridge.lib()
     threads = lib.oracle_max_threads()
-    A, B = host_inputs(cfg, rows, 123)
-    P = cfg.prefix
-    if cfg.kind == "wrap":  # wrap64_reference.cpp:254-290 on the slab; packing is a byte copy
+    m, n, k, P = cfg.m, cfg.n, cfg.k, cfg.prefix
+    if cfg.kind == "finite":  # whole tasks: pack A_t and B_t, GEMM mod m, export
         t0 = time.perf_counter()
-        out = bridge.wrap64_gemm(A, B)
-        t_slab = time.perf_counter() - t0
-        full = cfg.m / rows * t_slab
-        return {"value": cfg.ops / full / 1e9, "unit": "GOPS", "cores": threads, "kind": "port",
-                "sample": f"oracle wrap64 GEMM (native uint64 multiply-add) on a {rows}-row slab of A in "
-                          f"{t_slab:.2f} s; step = {cfg.m}/{rows} x t_slab = {full:.1f} s; {threads} threads",
-                "seconds": t_slab, "step_seconds": full}
-    t0 = time.perf_counter()
-    if cfg.kind == "finite":
-        b = bridge.pack_finite_u8(B, cfg.modulus)
+        out = np.empty((sample, m, n), np.uint8)
+        for t in range(sample):
+            a = bridge.pack_finite_u8(A[t], cfg.modulus)
+            b = bridge.pack_finite_u8(B[t], cfg.modulus)
+            c = bridge.ring_gemm(a, b, cfg.modulus)
+            out[t] = (c.astype(np.int16) % cfg.modulus).astype(np.uint8)  # centered -> canonical (a15)
+        wall = step = time.perf_counter() - t0
+        ops = sample * 2.0 * m * n * k
+        what = f"oracle pack, GEMM mod {cfg.modulus}, export of {sample} of {cfg.batch} tasks"
+    elif cfg.kind == "wrap":  # wrap64_reference.cpp:254-290 on the slab; packing is a byte copy
+        t0 = time.perf_counter()
+        out = bridge.wrap64_gemm(A[:sample], B)
+        wall = step = time.perf_counter() - t0
+        ops = 2.0 * sample * n * k
+        what = f"oracle wrap64 GEMM (native uint64 multiply-add) on rows [0, {sample}) of A"
     else:
+        t0 = time.perf_counter()
         b = bridge.pack(B, P)
-    t_b = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    if cfg.kind == "finite":
-        c = bridge.ring_gemm(bridge.pack_finite_u8(A, cfg.modulus), b, cfg.modulus)
-        out = (c.astype("int16") % cfg.modulus).astype("uint8")  # centered -> canonical, a1/a15
-        st = 0
-        what = f"oracle pack, GEMM mod {cfg.modulus}, export"
-    else:
-        c = bridge.gemm_rns(bridge.pack(A, P), b, P)
+        t_b = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        c = bridge.gemm_rns(bridge.pack(np.ascontiguousarray(A[:sample]), P), b, P)
         if cfg.kind == "i64":
             st, out = bridge.export_i64(c, P, cfg.bound)
         elif cfg.kind == "u64":
             st, out = bridge.export_u64(c, P, cfg.bound)
         else:
             st, out = bridge.export_limbs(c, P, cfg.limbs, True)
-        what = f"oracle pack, {P} plane GEMMs, " + (f"{cfg.limbs}-limb export" if cfg.kind == "exact" else "export")
-    t_slab = time.perf_counter() - t0
-    assert st == 0 and out.shape[0] == rows
-    full = cfg.batch * (t_b + cfg.m / rows * t_slab)
-    return {"value": cfg.ops / full / 1e9, "unit": "GOPS", "cores": threads, "kind": "port",
-            "sample": f"{what}: B ({cfg.k}x{cfg.n}) packed once in {t_b:.2f} s, a {rows}-row slab of A through "
-                      f"the remaining stages in {t_slab:.2f} s; step = {cfg.batch} x (t_B + {cfg.m}/{rows} x t_slab)"
-                      f" = {full:.1f} s; {threads} threads",
-            "seconds": t_b + t_slab, "step_seconds": full}
+        t_slab = time.perf_counter() - t0
+        if st != 0:
+            raise RuntimeError(f"oracle export status {st} on the sample")
+        wall = t_b + t_slab
+        step = t_slab + sample / m * t_b
+        ops = 2.0 * sample * n * k
+        what = (f"oracle pack, {P} plane GEMMs, " + (f"{cfg.limbs}-limb export" if cfg.kind == "exact" else "export") +
+                f" of rows [0, {sample}) of A against all of B; B packed in {t_b:.2f} s, charged {sample}/{m} of it")
+    info = {"value": ops / step / 1e9, "unit": "GOPS", "cores": threads, "kind": "port",
+            "sample": f"{what}; step {step:.2f} s ({wall:.2f} s wall); {threads} threads",
+            "sample_ops": ops, "step_s": step, "wall_s": wall,
+            "full_step_s_extrapolated": cfg.ops / (ops / step)}
+    return info, out
 
 
 def reference_arm(args, cfg: Config) -> None:
+    """The reference's CPU path (the oracle port: the reference's own src/cpu
+    needs Boost.Multiprecision, absent here) on every host thread, on the same
+    seeded inputs and the same bounded sample as this arm's CPU baseline."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    rows = max(8, cfg.cpu_rows // 4)
+    A, B = seeded_inputs(cfg, 0)
+    wall0 = time.perf_counter()
     for _ in range(args.warmup):
-        cpu_baseline(cfg, rows)
-    vals = [cpu_baseline(cfg, rows) for _ in range(args.steps)]
+        cpu_sample(cfg, A, B, cfg.sample)
+    vals = [cpu_sample(cfg, A, B, cfg.sample)[0] for _ in range(args.steps)]
     v = statistics.median(x["value"] for x in vals)
+    step_ms = 1e3 * statistics.median(x["step_s"] for x in vals)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GOPS", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * statistics.median(x["step_seconds"] for x in vals),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-            "config": {"workload": cfg.workload, "sample_rows": rows, "note": "reference CPU path (oracle port; the "
-                       "reference's own src/cpu needs Boost.Multiprecision, absent here)"},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {"finite": "uint8", "wrap": "uint64"}.get(cfg.kind, "int64"), "data": "synthetic",
+            "config": {"workload": cfg.workload, "name": cfg.name, "m_per_rank": cfg.m, "n": cfg.n, "k": cfg.k,
+                       "batch": cfg.batch, "prefix": cfg.prefix, "seed": SEED,
+                       "sample": (f"{cfg.sample} of {cfg.batch} tasks" if cfg.kind == "finite"
+                                  else f"rows [0, {cfg.sample}) of {cfg.m}"),
+                       "note": "reference CPU path (oracle port; the reference's own src/cpu needs "
+                               "Boost.Multiprecision, absent here); each step is the bounded sample"},
+            "measured_wall_s": time.perf_counter() - wall0,
+            "full_step_s_extrapolated": statistics.median(x["full_step_s_extrapolated"] for x in vals),
             "cpu_baseline": {**{k: vals[0][k] for k in ("unit", "cores", "kind", "sample")}, "value": v},
             "e2e": {"value": v, "unit": "GOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -350,14 +416,14 @@ class DevicePipeline:
     """Device-resident buffers and the three stages of one step (pack, plane
     GEMM, export), launched through the C-ABI device seam on one stream."""
 
-    def __init__(self, torch, lib, cfg: Config, dev: int, rank: int, sptr=None):
+    def __init__(self, torch, lib, cfg: Config, dev: int, hostA, hostB):
         self.torch, self.lib, self.cfg, self.dev = torch, lib, cfg, dev
         m, n, k, P, bt = cfg.m, cfg.n, cfg.k, cfg.prefix, cfg.batch
-        g = torch.Generator(device="cuda").manual_seed(1000 + rank)
-        gb = torch.Generator(device="cuda").manual_seed(999)
+        # The seeded host inputs, uploaded once (uint64 travels as int64 bits).
+        as_t = (lambda a: torch.from_numpy(a.view("int64")) if a.dtype.itemsize == 8 else torch.from_numpy(a))
+        self.A = as_t(hostA).to("cuda")
+        self.B = as_t(hostB).to("cuda")
         if cfg.kind == "finite":
-            self.A = torch.randint(cfg.lo, cfg.hi + 1, (bt, m, k), dtype=torch.uint8, device="cuda", generator=g)
-            self.B = torch.randint(cfg.lo, cfg.hi + 1, (bt, k, n), dtype=torch.uint8, device="cuda", generator=gb)
             self.ra = torch.empty((bt, m, k), dtype=torch.int8, device="cuda")
             self.rb = torch.empty((bt, k, n), dtype=torch.int8, device="cuda")
             self.rc = torch.empty((bt, m, n), dtype=torch.int8, device="cuda")
@@ -368,24 +434,12 @@ class DevicePipeline:
             self.pc = vp(*[self.rc[t].data_ptr() for t in range(bt)])
             self.sbytes = lib.rns8_cuda_gemm_finite_u8_scratch_bytes(dev, m, n, k, bt)
         elif cfg.kind == "wrap":
-            self.A = torch.randint(0, 256, (m, k, 8), dtype=torch.uint8, device="cuda", generator=g).view(
-                torch.int64).reshape(m, k)
-            self.B = torch.randint(0, 256, (k, n, 8), dtype=torch.uint8, device="cuda", generator=gb).view(
-                torch.int64).reshape(k, n)
             self.ra = torch.empty((8, m, k), dtype=torch.uint8, device="cuda")
             self.rb = torch.empty((8, k, n), dtype=torch.uint8, device="cuda")
             self.rc = torch.empty((1,), dtype=torch.uint8, device="cuda")
             self.out = torch.empty((m, n), dtype=torch.int64, device="cuda")
             self.sbytes = 0
         else:
-            if cfg.kind == "exact":  # full int64 range: uniform random bytes
-                self.A = torch.randint(0, 256, (m, k, 8), dtype=torch.uint8, device="cuda", generator=g).view(
-                    torch.int64).reshape(m, k)
-                self.B = torch.randint(0, 256, (k, n, 8), dtype=torch.uint8, device="cuda", generator=gb).view(
-                    torch.int64).reshape(k, n)
-            else:  # u64 values below 2^63 share int64's bit pattern
-                self.A = torch.randint(cfg.lo, cfg.hi + 1, (m, k), dtype=torch.int64, device="cuda", generator=g)
-                self.B = torch.randint(cfg.lo, cfg.hi + 1, (k, n), dtype=torch.int64, device="cuda", generator=gb)
             self.ra = torch.empty((P, m, k), dtype=torch.int8, device="cuda")
             self.rb = torch.empty((P, k, n), dtype=torch.int8, device="cuda")
             self.rc = torch.empty((P, m, n), dtype=torch.int8, device="cuda")
@@ -492,12 +546,13 @@ class DevicePipeline:
 class EndToEnd:
     """The same work through the public C ABI from pinned host buffers."""
 
-    def __init__(self, torch, r8, lib, cfg: Config, dev: int, pipe: DevicePipeline):
+    def __init__(self, torch, r8, lib, cfg: Config, dev: int, pipe: DevicePipeline, hostA, hostB):
         self.cfg, self.lib, self.r8 = cfg, lib, r8
         self.ctx = r8.Context(dev)
         m, n, k = cfg.m, cfg.n, cfg.k
-        self.hA = pipe.A.cpu().pin_memory()
-        self.hB = pipe.B.cpu().pin_memory()
+        as_t = (lambda a: torch.from_numpy(a.view("int64")) if a.dtype.itemsize == 8 else torch.from_numpy(a))
+        self.hA = as_t(hostA).pin_memory()
+        self.hB = as_t(hostB).pin_memory()
         self.hC = torch.empty(tuple(pipe.out.shape), dtype=pipe.out.dtype).pin_memory()
         S = r8.Semantics
         if cfg.kind == "wrap":
@@ -586,15 +641,10 @@ class ShardedProduct:
         self.torch, self.dist, self.lib, self.cfg, self.dev, self.sptr = torch, dist, lib, cfg, dev, sptr
         self.mode, self.world, self.rank = mode, world, rank
         m, n, k, P = cfg.m, cfg.n, cfg.k, cfg.prefix
-        g = torch.Generator(device="cuda").manual_seed(999)
-        if cfg.kind == "exact":
-            self.A = torch.randint(0, 256, (m, k, 8), dtype=torch.uint8, device="cuda", generator=g).view(
-                torch.int64).reshape(m, k)
-            self.B = torch.randint(0, 256, (k, n, 8), dtype=torch.uint8, device="cuda", generator=g).view(
-                torch.int64).reshape(k, n)
-        else:
-            self.A = torch.randint(cfg.lo, cfg.hi + 1, (m, k), dtype=torch.int64, device="cuda", generator=g)
-            self.B = torch.randint(cfg.lo, cfg.hi + 1, (k, n), dtype=torch.int64, device="cuda", generator=g)
+        # One product: every rank draws the same seeded A and B.
+        self.hA, self.hB = seeded_inputs(cfg, 0)
+        self.A = torch.from_numpy(self.hA.view("int64")).to("cuda")
+        self.B = torch.from_numpy(self.hB.view("int64")).to("cuda")
         self.signed = cfg.kind != "u64"
         if mode == "planes":
             self.row0, self.rows = shard.slab_of_rank(rank, m, world)
@@ -674,9 +724,7 @@ class ShardedProduct:
         if not self.rows:
             return True
         sub = dataclasses.replace(cfg, m=self.rows)
-        pipe = DevicePipeline(self.torch, self.lib, sub, self.dev, 0, self.sptr)
-        pipe.A.copy_(self.A[self.row0:self.row0 + self.rows])
-        pipe.B.copy_(self.B)
+        pipe = DevicePipeline(self.torch, self.lib, sub, self.dev, self.hA[self.row0:self.row0 + self.rows], self.hB)
         pipe.step()
         self.torch.cuda.synchronize()
         return bool(self.torch.equal(pipe.out, self.out[: self.rows])) and pipe.device_status() == 0
@@ -760,10 +808,13 @@ def main():
     if args.shard != "weak-rows":
         run_sharded(args, cfg)
         return
+    rank, world, local = dist_env()
+    if world > 1:  # ranks share the host's cores for the oracle check
+        os.environ.setdefault("OMP_NUM_THREADS", str(max(1, (os.cpu_count() or 1) // world)))
+    hostA, hostB = seeded_inputs(cfg, rank)
     import torch
     import torch.distributed as dist
 
-    rank, world, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
@@ -773,8 +824,7 @@ def main():
 
     lib = r8.lib()
     stream = torch.cuda.current_stream()
-    sptr = C.c_void_p(stream.cuda_stream)
-    pipe = DevicePipeline(torch, lib, cfg, local, rank, sptr)
+    pipe = DevicePipeline(torch, lib, cfg, local, hostA, hostB)
 
     for _ in range(max(3, args.warmup)):
         pipe.step()
@@ -859,7 +909,7 @@ def main():
     # ---- e2e through the public C ABI from pinned host buffers -------------------
     e2e = None
     if not args.no_e2e:
-        ee = EndToEnd(torch, r8, lib, cfg, local, pipe)
+        ee = EndToEnd(torch, r8, lib, cfg, local, pipe, hostA, hostB)
         for _ in range(max(3, args.warmup)):
             ee.run()
         torch.cuda.synchronize()
@@ -877,9 +927,36 @@ def main():
                "d2h_bytes_per_step": ee.d2h, "ms_per_step": e2e_ms, "api": ee.api}
         ee.close()
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(cfg, cfg.cpu_rows)
+    # ---- parity: the GPU's output against the CPU oracle on the same inputs --------
+    # Rank 0 of a one-GPU run checks the config's sample (the CPU baseline is
+    # that run's timing); with several ranks each checks 16 rows (one task) of
+    # its own product on its share of the host's cores. The FNV checksum of
+    # the whole GPU output is reported beside it.
+    cpu, parity = None, None
+    if not args.no_parity:
+        sample = cfg.sample if world == 1 else min(cfg.sample, 1 if cfg.kind == "finite" else 16)
+        info, want = cpu_sample(cfg, hostA, hostB, sample)
+        out = pipe.out.cpu().numpy()
+        if cfg.kind in ("u64", "wrap"):
+            out = out.view("uint64")
+        elif cfg.kind == "exact":
+            out = out.view("uint64")
+        got = out[:sample]
+        match = bool(got.shape == want.shape and (got == want.view(got.dtype)).all())
+        flag = torch.tensor([0.0 if match else 1.0], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        parity = {"oracle": "CPU restatement of the reference's src/cpu path, same seeded inputs",
+                  "seed": SEED, "generator": "std::mt19937_64 + std::uniform_int_distribution (libstdc++)",
+                  ("tasks_checked" if cfg.kind == "finite" else "rows_checked"): sample,
+                  "cells_checked": int(want.size if cfg.kind != "exact" else want.size // cfg.limbs),
+                  "match": bool(float(flag.item()) == 0.0),
+                  "checksum_sample_gpu": fnv_checksum(got), "checksum_sample_oracle": fnv_checksum(want),
+                  "checksum_gpu_full": fnv_checksum(out)}
+        if world > 1:
+            parity["note"] = "every rank checked its own first rows; match is the AND over ranks"
+        if rank == 0 and world == 1:
+            cpu = info
 
     # Roofline of the dominant stage (one kernel launch per stage, except that
     # the grouped finite GEMM launches once per 32 tasks).
@@ -918,13 +995,16 @@ def main():
             "roofline": roof,
             "stages_ms": stage_ms,
             "stage_frac_of_peak": stage_frac,
-            "e2e": e2e, "cpu_baseline": cpu, "clocks": clock_info,
+            "e2e": e2e, "cpu_baseline": cpu, "parity": parity, "clocks": clock_info,
             "gpu_launches": pipe.launches_per_step * args.steps,
         }
+        line["config"]["seed"] = SEED
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if parity is not None and not parity["match"]:
+        raise SystemExit("parity FAILED: the GPU output differs from the CPU oracle on the sample")
 
 
 if __name__ == "__main__":

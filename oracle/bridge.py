@@ -59,7 +59,11 @@ _SIGS = {
     "oracle_rng_next": (u64, [C.c_int]),
     "oracle_rng_fill_i64": (None, [C.c_int, i64, i64, vp, i64]),
     "oracle_rng_fill_u64": (None, [C.c_int, u64, u64, vp, i64]),
+    "oracle_rng_fill_u8": (None, [C.c_int, u32, vp, i64]),
+    "oracle_rng_skip_i64": (None, [C.c_int, i64, i64, i64]),
+    "oracle_rng_skip_u64": (None, [C.c_int, u64, u64, i64]),
     "oracle_checksum_u64": (u64, [vp, i64, i64, i64]),
+    "oracle_checksum_u64_from": (u64, [u64, vp, i64]),
 }
 
 _lib = None
@@ -312,6 +316,18 @@ class Rng:
         out = np.empty(shape, np.uint64)
         lib().oracle_rng_fill_u64(self.h, lo, hi, _p(out), out.size)
         return out
+
+    def u8(self, hi: int, shape) -> np.ndarray:
+        """uniform_int_distribution<uint32_t>(0, hi) per byte (the reference's finite lanes)."""
+        out = np.empty(shape, np.uint8)
+        lib().oracle_rng_fill_u8(self.h, hi, _p(out), out.size)
+        return out
+
+    def skip_i64(self, lo: int, hi: int, count: int) -> None:
+        lib().oracle_rng_skip_i64(self.h, lo, hi, count)
+
+    def skip_u64(self, lo: int, hi: int, count: int) -> None:
+        lib().oracle_rng_skip_u64(self.h, lo, hi, count)
 
     def __del__(self):
         try:

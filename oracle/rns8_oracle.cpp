@@ -1025,6 +1025,23 @@ OX void oracle_rng_fill_u64(int h, uint64_t lo, uint64_t hi, uint64_t* out, int6
   for (int64_t i = 0; i < count; ++i) out[i] = dist(*g_rngs[h]);
 }
 
+// Finite-u8 inputs: std::uniform_int_distribution<uint32_t>(0, hi) per byte, as
+// the reference's finite lanes draw them (rns8_bench_finite_lanes.inc:28-31).
+OX void oracle_rng_fill_u8(int h, uint32_t hi, uint8_t* out, int64_t count) {
+  std::uniform_int_distribution<uint32_t> dist(0, hi);
+  for (int64_t i = 0; i < count; ++i) out[i] = static_cast<uint8_t>(dist(*g_rngs[h]));
+}
+// Advances the engine past `count` draws of uniform_int_distribution<T>(lo, hi)
+// (the values another rank's slab would take), storing nothing.
+OX void oracle_rng_skip_i64(int h, int64_t lo, int64_t hi, int64_t count) {
+  std::uniform_int_distribution<int64_t> dist(lo, hi);
+  for (int64_t i = 0; i < count; ++i) (void)dist(*g_rngs[h]);
+}
+OX void oracle_rng_skip_u64(int h, uint64_t lo, uint64_t hi, int64_t count) {
+  std::uniform_int_distribution<uint64_t> dist(lo, hi);
+  for (int64_t i = 0; i < count; ++i) (void)dist(*g_rngs[h]);
+}
+
 // benchmarks/rns8_bench_event_phase_helpers.inc:544-552 + rns8_bench_support.cpp:96-99.
 OX uint64_t oracle_checksum_u64(const uint64_t* v, int64_t rows, int64_t cols, int64_t ld) {
   uint64_t h = 1469598103934665603ull;
@@ -1033,5 +1050,14 @@ OX uint64_t oracle_checksum_u64(const uint64_t* v, int64_t rows, int64_t cols, i
       h ^= v[r * ld + c];
       h *= 1099511628211ull;
     }
+  return h;
+}
+// The same mix continued from a running hash `h` over `count` values (for
+// outputs checksummed in chunks).
+OX uint64_t oracle_checksum_u64_from(uint64_t h, const uint64_t* v, int64_t count) {
+  for (int64_t i = 0; i < count; ++i) {
+    h ^= v[i];
+    h *= 1099511628211ull;
+  }
   return h;
 }
