@@ -276,6 +276,210 @@ __global__ void __launch_bounds__(256) export_bounded_kernel(ExportArgs a) {
   if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(a.status, kDevRangeError);
 }
 
+// ---- bounded export, streamed (contiguous destinations) --------------------------
+// A persistent CTA per SM: one producer warp streams each tile's slice of
+// every plane (4096 cells, so P copies of 4 KiB) into a ring of shared-memory
+// stages with 1-D bulk copies, and 16 consumer warps reconstruct eight cells
+// per lane from shared memory with the two-plane dp2a sums (PairTable). The
+// copies run ahead of the arithmetic by up to kStages tiles whatever the
+// consumers are doing, which is what the register-fed kernel above cannot
+// do: its loads wait behind its own multiply chains. full[s] completes when
+// a stage's copies have landed; empty[s] when all consumer warps have read it.
+constexpr int kWsConsumerWarps = 16;
+constexpr int kWsThreads = 32 * (kWsConsumerWarps + 1);
+constexpr int kWsTileCells = kWsConsumerWarps * 32 * 8;
+
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Eight consecutive cells from their P plane words (signed residues, cells
+// 4j..4j+3 in word j): fractional CRT by the dp2a sums, 16-byte streaming
+// stores, then the exact path for cells the fraction leaves undecided.
+template <int P, bool kSigned>
+__device__ __forceinline__ void pair_reconstruct8(const ExportArgs& a, uint64_t s_init,
+                                                  uint32_t (&w)[2 * PairTable<P>::kPairs][2], int64_t first,
+                                                  bool& bad) {
+  constexpr PairTable<P> K = make_pair_table<P>();
+  constexpr int kPairs = PairTable<P>::kPairs;
+  if constexpr (P % 2 != 0) {
+    w[P][0] = 0;
+    w[P][1] = 0;
+  }
+  uint32_t undecided = 0;
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    int32_t f0[2] = {0, 0}, f1[2] = {0, 0}, g0[2] = {0, 0}, g1[2] = {0, 0}, g2[2] = {0, 0}, g3[2] = {0, 0};
+    constexpr uint32_t kSel[2] = {0x5140u, 0x7362u};  // bytes (j, 4+j, j+1, 5+j) for j = 0, 2
+    const uint32_t sel = kSel[(e & 3) >> 1];
+#pragma unroll
+    for (int q = 0; q < kPairs; ++q) {
+      const int x = static_cast<int>(__byte_perm(w[2 * q][e / 4], w[2 * q + 1][e / 4], sel));
+      f0[0] = __dp2a_lo(static_cast<int>(K.f[q][0]), x, f0[0]);
+      f1[0] = __dp2a_lo(static_cast<int>(K.f[q][1]), x, f1[0]);
+      g0[0] = __dp2a_lo(static_cast<int>(K.g[q][0]), x, g0[0]);
+      g1[0] = __dp2a_lo(static_cast<int>(K.g[q][1]), x, g1[0]);
+      g2[0] = __dp2a_lo(static_cast<int>(K.g[q][2]), x, g2[0]);
+      g3[0] = __dp2a_lo(static_cast<int>(K.g[q][3]), x, g3[0]);
+      f0[1] = __dp2a_hi(static_cast<int>(K.f[q][0]), x, f0[1]);
+      f1[1] = __dp2a_hi(static_cast<int>(K.f[q][1]), x, f1[1]);
+      g0[1] = __dp2a_hi(static_cast<int>(K.g[q][0]), x, g0[1]);
+      g1[1] = __dp2a_hi(static_cast<int>(K.g[q][1]), x, g1[1]);
+      g2[1] = __dp2a_hi(static_cast<int>(K.g[q][2]), x, g2[1]);
+      g3[1] = __dp2a_hi(static_cast<int>(K.g[q][3]), x, g3[1]);
+    }
+    uint64_t v[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint64_t s = s_init + static_cast<uint64_t>(static_cast<int64_t>(f0[h])) +
+                         (static_cast<uint64_t>(static_cast<int64_t>(f1[h])) << 16);
+      const uint32_t s_lo = static_cast<uint32_t>(s);
+      const uint32_t q = __funnelshift_r(s_lo, static_cast<uint32_t>(s >> 32), 31);
+      const int32_t frac = static_cast<int32_t>(s_lo & 0x7FFFFFFFu) - (1 << 30);
+      const uint32_t afrac = static_cast<uint32_t>(frac < 0 ? -frac : frac);
+      bad |= afrac >= a.frac.t_out;
+      undecided |= (afrac > a.frac.t_in && afrac < a.frac.t_out) ? (1u << (e + h)) : 0u;
+      const uint64_t sum = static_cast<uint64_t>(static_cast<int64_t>(g0[h])) +
+                           (static_cast<uint64_t>(static_cast<int64_t>(g1[h])) << 16) +
+                           (static_cast<uint64_t>(static_cast<int64_t>(g2[h])) << 32) +
+                           (static_cast<uint64_t>(static_cast<int64_t>(g3[h])) << 48);
+      v[h] = sum + K.bias_m64 - static_cast<uint64_t>(q) * K.m64;
+    }
+    __stcs(reinterpret_cast<ulonglong2*>(static_cast<uint64_t*>(a.dst) + first + e),
+           make_ulonglong2(static_cast<unsigned long long>(v[0]), static_cast<unsigned long long>(v[1])));
+  }
+  while (undecided != 0) {
+    const int e = __ffs(undecided) - 1;
+    undecided &= undecided - 1;
+    int r[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const uint32_t word = (e >> 2) ? w[p][1] : w[p][0];
+      r[p] = static_cast<int>(static_cast<int8_t>((word >> (8 * (e & 3))) & 0xFFu));
+    }
+    uint64_t v;
+    if (reconstruct_bounded<P, kSigned>(r, a.lim, &v))
+      static_cast<uint64_t*>(a.dst)[first + e] = v;
+    else
+      bad = true;
+  }
+}
+
+template <int P, bool kSigned, int kStages>
+__global__ void __launch_bounds__(kWsThreads, 1) export_bounded_ws_kernel(ExportArgs a) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[kStages], empty[kStages];
+  const int64_t cells = a.m * a.n;
+  const int64_t tiles = cells / kWsTileCells;
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWsConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  int64_t mine = 0;  // tiles b, b + grid, ... of this CTA
+  if (blockIdx.x < tiles) mine = (tiles - 1 - blockIdx.x) / gridDim.x + 1;
+  if (warp == kWsConsumerWarps) {
+    if (lane != 0) return;
+    int64_t issued = 0;
+    for (int64_t j = 0; j < mine; ++j, ++issued) {
+      const int s = static_cast<int>(j % kStages);
+      if (j >= kStages && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((j / kStages) - 1) & 1))) {
+        atomicOr(a.status, kDevWaitTimeout);
+        break;
+      }
+      const int64_t tile = blockIdx.x + j * gridDim.x;
+      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(P * kWsTileCells));
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+        bulk_load_1d(ring + (s * P + p) * kWsTileCells, a.planes + static_cast<int64_t>(p) * cells + tile * kWsTileCells,
+                     kWsTileCells, &full[s]);
+    }
+    // Leave no copy in flight: wait (bounded) for the last stages issued.
+    for (int64_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+      if (!mbar_wait_bounded(&full[j % kStages], static_cast<uint32_t>((j / kStages) & 1)))
+        atomicOr(a.status, kDevWaitTimeout);
+    return;
+  }
+  const uint64_t s_init = a.frac.s_init + make_pair_table<P>().sumF128;  // residues r, not r + 128
+  bool bad = false;
+  const int off = (warp * 32 + lane) * 8;
+  for (int64_t j = 0; j < mine; ++j) {
+    const int s = static_cast<int>(j % kStages);
+    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((j / kStages) & 1))) {
+      if (lane == 0) atomicOr(a.status, kDevWaitTimeout);
+      break;
+    }
+    uint32_t w[2 * PairTable<P>::kPairs][2];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const uint2 v = *reinterpret_cast<const uint2*>(ring + (s * P + p) * kWsTileCells + off);
+      w[p][0] = v.x;
+      w[p][1] = v.y;
+    }
+    // The stage is refilled by bulk copies (the async proxy) once every warp
+    // has arrived on empty[s]: order this thread's generic-proxy reads of it
+    // before those writes.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    pair_reconstruct8<P, kSigned>(a, s_init, w, (blockIdx.x + j * gridDim.x) * kWsTileCells + off, bad);
+  }
+  // The last, partial tile (fewer than 4096 cells): one CTA, exact path.
+  if (blockIdx.x == tiles % gridDim.x) {
+    for (int64_t c = tiles * kWsTileCells + warp * 32 + lane; c < cells; c += kWsConsumerWarps * 32) {
+      int r[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) r[p] = a.planes[static_cast<int64_t>(p) * cells + c];
+      uint64_t v;
+      if (reconstruct_bounded<P, kSigned>(r, a.lim, &v))
+        static_cast<uint64_t*>(a.dst)[c] = v;
+      else
+        bad = true;
+    }
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(a.status, kDevRangeError);
+}
+
+template <int P>
+constexpr int ws_stages() {
+  constexpr int by_smem = (224 * 1024) / (P * kWsTileCells);
+  return by_smem > 4 ? 4 : by_smem;
+}
+
+// The streamed kernel applies to contiguous destinations with the fractional
+// path enabled, 16-byte aligned planes and at least one whole tile.
+template <int P, bool kSigned>
+bool launch_bounded_ws(const ExportArgs& a, cudaStream_t stream, cudaError_t* err) {
+  constexpr int kStages = ws_stages<P>();
+  const int64_t cells = a.m * a.n;
+  if (kStages < 2 || !a.frac.enabled || a.ld != a.n || reinterpret_cast<uintptr_t>(a.dst) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(a.planes) % 16 != 0 || cells % 16 != 0 || cells < kWsTileCells)
+    return false;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                               cudaSuccess || sms <= 0) {
+    *err = cudaGetLastError();
+    return true;
+  }
+  const int smem = kStages * P * kWsTileCells;
+  auto kernel = export_bounded_ws_kernel<P, kSigned, kStages>;
+  *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (*err != cudaSuccess) return true;
+  const int64_t tiles = cells / kWsTileCells;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  kernel<<<grid, kWsThreads, smem, stream>>>(a);
+  *err = cudaGetLastError();
+  return true;
+}
+
 template <int P, bool kSigned, int kCells>
 cudaError_t launch_bounded(const ExportArgs& a, cudaStream_t stream) {
   const int64_t groups = a.m * a.n / kCells;
@@ -299,6 +503,8 @@ cudaError_t launch_export(const ExportArgs& a, cudaStream_t stream) {
   const int64_t cells = a.m * a.n;
   if constexpr (kMode == Mode::I64 || kMode == Mode::U64) {
     constexpr bool kSigned = kMode == Mode::I64;
+    cudaError_t ws_err = cudaSuccess;
+    if (launch_bounded_ws<P, kSigned>(a, stream, &ws_err)) return ws_err;
     const uintptr_t base = reinterpret_cast<uintptr_t>(a.planes);
     constexpr int kWide = RNS8_EXPORT_CELLS;
     if (cells % kWide == 0 && base % kWide == 0) return launch_bounded<P, kSigned, kWide>(a, stream);

@@ -457,6 +457,53 @@ __device__ __forceinline__ int frac_reconstruct(const uint32_t (&u)[P], const Fr
   return 1;
 }
 
+// The same sums taken two planes at a time with dp2a (two 16-bit x 8-bit
+// products plus a 32-bit addend): F_i and G_i mod 2^64 are written as signed
+// 16-bit digits (F_i = d0 + d1 * 2^16, G_i = sum_b d_b * 2^(16b) mod 2^64),
+// the digits of planes 2k and 2k+1 share a word, and one byte permute puts
+// both planes' signed residues for two cells into the dp2a byte operand.
+// Every digit sum stays below P * 128 * 2^15 < 2^27, so
+//   sum_i r_i * F_i = f0 + f1 * 2^16   and   sum_i r_i * G_i = sum_b g_b * 2^(16b)  (mod 2^64)
+// are the multiply-add form's integers exactly, with r_i in place of r_i + 128.
+template <int P>
+struct PairTable {
+  static constexpr int kPairs = (P + 1) / 2;
+  uint32_t f[kPairs][2];
+  uint32_t g[kPairs][4];
+  uint64_t m64;       // M mod 2^64
+  uint64_t bias_m64;  // kQuotientBias * M mod 2^64
+  uint64_t sumF128;   // 128 * sum F_i: turns FracLimits::s_init (for r + 128) into the start for r
+};
+
+__host__ __device__ constexpr uint32_t signed_digit16(uint64_t v, int b) {
+  // digit b of the balanced base-2^16 expansion of v mod 2^64, as a 16-bit pattern
+  for (int i = 0; i < b; ++i) {
+    const uint32_t low = static_cast<uint32_t>(v & 0xFFFFu);
+    v = (v >> 16) + (low >= 0x8000u ? 1u : 0u);
+  }
+  return static_cast<uint32_t>(v & 0xFFFFu);
+}
+
+template <int P>
+__host__ __device__ constexpr PairTable<P> make_pair_table() {
+  constexpr FracTable<P> T = make_frac_table<P>();
+  PairTable<P> t{};
+  for (int k = 0; k < PairTable<P>::kPairs; ++k) {
+    for (int b = 0; b < 2; ++b) t.f[k][b] = 0;
+    for (int b = 0; b < 4; ++b) t.g[k][b] = 0;
+  }
+  for (int i = 0; i < P; ++i) {
+    const uint64_t g = static_cast<uint64_t>(T.Glo[i]) | (static_cast<uint64_t>(T.Ghi[i]) << 32);
+    const int k = i / 2, sh = 16 * (i % 2);
+    for (int b = 0; b < 2; ++b) t.f[k][b] |= signed_digit16(T.F[i], b) << sh;
+    for (int b = 0; b < 4; ++b) t.g[k][b] |= signed_digit16(g, b) << sh;
+  }
+  t.m64 = T.M64;
+  t.bias_m64 = static_cast<uint64_t>(kQuotientBias) * T.M64;
+  t.sumF128 = static_cast<uint64_t>(T.sumF128);
+  return t;
+}
+
 // Host: M_P as 32-bit limbs, and the limits for a bounded export.
 inline void host_product32(uint32_t prefix, uint32_t out[kLimbs32]) {
   uint64_t prod[kLimbs32] = {1, 0, 0, 0, 0};
