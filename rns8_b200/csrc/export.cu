@@ -289,14 +289,6 @@ constexpr int kWsConsumerWarps = 16;
 constexpr int kWsThreads = 32 * (kWsConsumerWarps + 1);
 constexpr int kWsTileCells = kWsConsumerWarps * 32 * 8;
 
-__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Eight consecutive cells from their P plane words (signed residues, cells
 // 4j..4j+3 in word j): fractional CRT by the dp2a sums, 16-byte streaming
 // stores, then the exact path for cells the fraction leaves undecided.
@@ -424,10 +416,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) export_bounded_ws_kernel(Export
       w[p][0] = v.x;
       w[p][1] = v.y;
     }
-    // The stage is refilled by bulk copies (the async proxy) once every warp
-    // has arrived on empty[s]: order this thread's generic-proxy reads of it
-    // before those writes.
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    release_stage_reads();  // the stage is refilled once every warp has arrived on empty[s]
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     pair_reconstruct8<P, kSigned>(a, s_init, w, (blockIdx.x + j * gridDim.x) * kWsTileCells + off, bad);

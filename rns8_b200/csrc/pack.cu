@@ -125,12 +125,159 @@ __global__ void __launch_bounds__(256) pack_scalar_kernel(const T* __restrict__ 
   }
 }
 
+// ---- streamed pack (compact sources) ---------------------------------------------
+// A persistent CTA per SM: one producer warp streams 4096-element tiles of
+// the source (32 KiB) into a ring of shared-memory stages with 1-D bulk
+// copies; 16 consumer warps convert eight elements per lane and store eight
+// bytes to each plane. The copies run up to kStages tiles ahead of the
+// integer arithmetic, which the register-fed kernel above cannot do (its
+// loads wait behind its own multiply chains). A lane's 64 source bytes are
+// read as four 16-byte chunks starting at chunk (lane / 2) mod 4, which puts
+// the 32 lanes of each read on distinct bank groups; the eight output bytes
+// of each plane are rotated back into place with two byte permutes.
+constexpr int kPackWarps = 16;
+constexpr int kPackThreads = 32 * (kPackWarps + 1);
+constexpr int kPackTile = kPackWarps * 32 * 8;
+constexpr int kPackStages = 4;
+
+// The pack has no status word, so a bounded wait that runs out cannot be
+// reported; instead it cannot change the result: the warp that gives up sets
+// a block-wide flag, the producer stops issuing, and every consumer warp
+// reads its remaining tiles straight from global memory. The producer then
+// waits (bounded) for the copies it already issued before the block exits.
+template <int P, typename T>
+__device__ __forceinline__ void pack8_store(const int4 (&v)[4], int8_t* out, int64_t elems, uint32_t sel_lo,
+                                           uint32_t sel_hi) {
+  constexpr bool kSigned = static_cast<T>(-1) < 0;
+  Words d[8];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    d[2 * q] = split_words<T>(static_cast<T>((static_cast<uint64_t>(static_cast<uint32_t>(v[q].y)) << 32) |
+                                             static_cast<uint32_t>(v[q].x)));
+    d[2 * q + 1] = split_words<T>(static_cast<T>((static_cast<uint64_t>(static_cast<uint32_t>(v[q].w)) << 32) |
+                                                 static_cast<uint32_t>(v[q].z)));
+  }
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    const uint32_t lo = pack4(residue_byte<kSigned>(d[0], p), residue_byte<kSigned>(d[1], p),
+                              residue_byte<kSigned>(d[2], p), residue_byte<kSigned>(d[3], p));
+    const uint32_t hi = pack4(residue_byte<kSigned>(d[4], p), residue_byte<kSigned>(d[5], p),
+                              residue_byte<kSigned>(d[6], p), residue_byte<kSigned>(d[7], p));
+    __stcs(reinterpret_cast<uint2*>(out + static_cast<int64_t>(p) * elems),
+           make_uint2(__byte_perm(lo, hi, sel_lo), __byte_perm(lo, hi, sel_hi)));
+  }
+}
+
+template <int P, typename T>
+__global__ void __launch_bounds__(kPackThreads, 1) pack_ws_kernel(const T* __restrict__ src, int64_t elems,
+                                                                  int8_t* __restrict__ planes) {
+  constexpr bool kSigned = static_cast<T>(-1) < 0;
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[kPackStages], empty[kPackStages];
+  __shared__ int gave_up;
+  const int64_t tiles = elems / kPackTile;
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPackStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kPackWarps);
+    }
+    gave_up = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* stop = &gave_up;
+  int64_t mine = 0;  // tiles b, b + grid, ... of this CTA
+  if (blockIdx.x < tiles) mine = (tiles - 1 - blockIdx.x) / gridDim.x + 1;
+  if (warp == kPackWarps) {
+    if (lane != 0) return;
+    int64_t issued = 0;
+    for (int64_t j = 0; j < mine && !*stop; ++j, ++issued) {
+      const int s = static_cast<int>(j % kPackStages);
+      if (j >= kPackStages && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((j / kPackStages) - 1) & 1))) {
+        *stop = 1;
+        break;
+      }
+      const int64_t tile = blockIdx.x + j * gridDim.x;
+      mbar_arrive_expect_tx(&full[s], kPackTile * 8);
+      bulk_load_1d(ring + static_cast<size_t>(s) * kPackTile * 8, src + tile * kPackTile, kPackTile * 8, &full[s]);
+    }
+    for (int64_t j = issued > kPackStages ? issued - kPackStages : 0; j < issued; ++j)
+      (void)mbar_wait_bounded(&full[j % kPackStages], static_cast<uint32_t>((j / kPackStages) & 1));
+    return;
+  }
+  const int rot = (lane >> 1) & 3;
+  uint32_t sel_lo = 0, sel_hi = 0;  // rotate the 8 output bytes left by 2 * rot
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sel_lo |= static_cast<uint32_t>((j - 2 * rot) & 7) << (4 * j);
+    sel_hi |= static_cast<uint32_t>((j + 4 - 2 * rot) & 7) << (4 * j);
+  }
+  const int tid = warp * 32 + lane;
+  for (int64_t j = 0; j < mine; ++j) {
+    const int s = static_cast<int>(j % kPackStages);
+    const int64_t tile = blockIdx.x + j * gridDim.x;
+    bool direct = *stop != 0;
+    if (!direct) direct = !mbar_wait_bounded(&full[s], static_cast<uint32_t>((j / kPackStages) & 1));
+    direct = __any_sync(0xFFFFFFFFu, direct);
+    int4 v[4];
+    if (direct) {  // a wait ran out somewhere in this block: read the tile from global memory
+      *stop = 1;
+      const int4* gp = reinterpret_cast<const int4*>(src + tile * kPackTile) + tid * 4;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = gp[(q + rot) & 3];
+    } else {
+      const int4* sp = reinterpret_cast<const int4*>(ring + static_cast<size_t>(s) * kPackTile * 8) + tid * 4;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = sp[(q + rot) & 3];  // slot q holds chunk (q + rot) mod 4
+      release_stage_reads();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    pack8_store<P, T>(v, planes + tile * kPackTile + tid * 8, elems, sel_lo, sel_hi);
+  }
+  // The last, partial tile: one CTA, one element per thread.
+  if (blockIdx.x == tiles % gridDim.x) {
+    for (int64_t i = tiles * kPackTile + tid; i < elems; i += kPackWarps * 32) {
+      const Words d = split_words<T>(src[i]);
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+        planes[static_cast<int64_t>(p) * elems + i] = static_cast<int8_t>(residue_byte<kSigned>(d, p) & 0xFFu);
+    }
+  }
+}
+
+// Compact sources of at least one tile with a 16-byte aligned start and
+// 8-byte aligned planes take the streamed kernel.
+template <int P, typename T>
+bool launch_pack_ws(const T* src, int64_t elems, int8_t* planes, cudaStream_t stream, cudaError_t* err) {
+  if (elems < kPackTile || elems % 8 != 0 || reinterpret_cast<uintptr_t>(src) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(planes) % 8 != 0)
+    return false;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    *err = cudaGetLastError();
+    return true;
+  }
+  constexpr int smem = kPackStages * kPackTile * 8;
+  auto kernel = pack_ws_kernel<P, T>;
+  *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (*err != cudaSuccess) return true;
+  const int64_t tiles = elems / kPackTile;
+  kernel<<<static_cast<unsigned>(tiles < sms ? tiles : sms), kPackThreads, smem, stream>>>(src, elems, planes);
+  *err = cudaGetLastError();
+  return true;
+}
+
 template <int P, typename T>
 cudaError_t launch_pack(const T* src, int64_t rows, int64_t cols, int64_t ld, int8_t* planes, cudaStream_t stream) {
   if (ld == cols) {  // compact source: one long row, so any column count can take the vector path
     cols *= rows;
     ld = cols;
     rows = 1;
+    cudaError_t err = cudaSuccess;
+    if (launch_pack_ws<P, T>(src, cols, planes, stream, &err)) return err;
   }
   const bool vec = (cols % 8 == 0) && (ld % 2 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(planes) % 8 == 0);
