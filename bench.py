@@ -887,15 +887,39 @@ def main():
         total_ms = sum(e0.elapsed_time(e1) for e0, e1 in step_events)
     if pipe.device_status() != 0:
         raise RuntimeError(f"device status {pipe.device_status():#x} in the timed region")
-    # Per-stage split (for the roofline): the same steps launched from the
-    # host with events between the stages, after the timed region.
+    # Per-stage split (for the roofline): after the timed region, the same
+    # steps with events between the stages. Each stage is replayed from its
+    # own captured graph (host launches with --no-graph), one step's work is
+    # queued ahead so the GPU is busy when the first event is recorded, and
+    # the median over steps is kept, so that no stage time includes the
+    # host's launch latency.
+    stages = (pipe.pack, pipe.gemm, pipe.export)
+    stage_graphs = None
+    if graph is not None:
+        try:
+            stage_graphs = []
+            for fn in stages:
+                sg = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(sg):
+                    fn()
+                stage_graphs.append(sg)
+        except Exception:
+            stage_graphs = None
     records = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    if graph is not None:
+        graph.replay()  # lead-in work
     for i in range(args.steps):
         if flush is not None:
             flush.zero_()
-        pipe.step(records[i])
+        for j in range(3):
+            records[i][j].record(stream)
+            if stage_graphs is not None:
+                stage_graphs[j].replay()
+            else:
+                stages[j]()
+        records[i][3].record(stream)
     torch.cuda.synchronize()
-    stage_ms = {name: statistics.mean(r[i].elapsed_time(r[i + 1]) for r in records)
+    stage_ms = {name: statistics.median(r[i].elapsed_time(r[i + 1]) for r in records)
                 for i, name in enumerate(("pack", "plane_gemm", "export"))}
     if pipe.device_status() != 0:
         raise RuntimeError(f"device status {pipe.device_status():#x} in the stage timing")
@@ -994,6 +1018,8 @@ def main():
                              if pipe.fits_l2 else "inputs larger than L2"},
             "roofline": roof,
             "stages_ms": stage_ms,
+            "stages_timing": ("median over the steps of events between per-stage graph replays"
+                              if stage_graphs is not None else "median over the steps of events between host launches"),
             "stage_frac_of_peak": stage_frac,
             "e2e": e2e, "cpu_baseline": cpu, "parity": parity, "clocks": clock_info,
             "gpu_launches": pipe.launches_per_step * args.steps,

@@ -5,6 +5,7 @@
 // runs out reports failure to its caller instead of hanging the GPU.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -56,6 +57,24 @@ __device__ __forceinline__ int reduce_i32_centered(int32_t v, const ModConst& c)
   uint32_t r = umod_u32(u, c.m, c.magic);
   r = r >= c.off ? r - c.off : r + c.m - c.off;
   return center_residue(r, c.m);
+}
+
+// ---- host: kernel attributes --------------------------------------------------
+// Raises `kernel`'s dynamic shared-memory limit on the current device, once
+// per process and device (`done` holds one bit per device id below 64).
+// cudaFuncSetAttribute can wait for running instances of the kernel, so it is
+// kept off the per-launch path: a second launch of the same kernel queued
+// behind the first would otherwise leave the GPU idle while the host waits.
+template <typename Kernel>
+inline cudaError_t raise_smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }
 
 // ---- PTX wrappers ------------------------------------------------------------

@@ -460,7 +460,8 @@ bool launch_bounded_ws(const ExportArgs& a, cudaStream_t stream, cudaError_t* er
   }
   const int smem = kStages * P * kWsTileCells;
   auto kernel = export_bounded_ws_kernel<P, kSigned, kStages>;
-  *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  static std::atomic<uint64_t> configured{0};
+  *err = raise_smem_limit_once(kernel, smem, configured);
   if (*err != cudaSuccess) return true;
   const int64_t tiles = cells / kWsTileCells;
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);

@@ -683,12 +683,8 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
                           const SlabScatter* scatter) {
   if (prob.task_count == 0 || prob.task_count > kMaxGroupTasks || prob.planes == 0 || prob.planes > 20)
     return cudaErrorInvalidValue;
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(tc_plane_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(SMEM_BYTES));
-  });
+  static std::atomic<uint64_t> configured{0};
+  const cudaError_t attr_err = raise_smem_limit_once(tc_plane_gemm_kernel, static_cast<int>(SMEM_BYTES), configured);
   if (attr_err != cudaSuccess) return attr_err;
 
   const TcSchedule s = tc_schedule(prob, sm_count);
@@ -783,12 +779,8 @@ bool tma_encode_available() { return encode_fn() != nullptr; }
 
 cudaError_t tc_wrap64_gemm(const uint8_t* a_limbs, const uint8_t* b_limbs, uint64_t* c, int64_t m, int64_t n,
                            int64_t k, int sm_count, uint32_t* dev_status, cudaStream_t stream) {
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(tc_wrap64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(SMEM_BYTES));
-  });
+  static std::atomic<uint64_t> configured{0};
+  const cudaError_t attr_err = raise_smem_limit_once(tc_wrap64_kernel, static_cast<int>(SMEM_BYTES), configured);
   if (attr_err != cudaSuccess) return attr_err;
   WrapParams prm;
   std::memset(&prm, 0, sizeof(prm));

@@ -262,7 +262,8 @@ bool launch_pack_ws(const T* src, int64_t elems, int8_t* planes, cudaStream_t st
   }
   constexpr int smem = kPackStages * kPackTile * 8;
   auto kernel = pack_ws_kernel<P, T>;
-  *err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  static std::atomic<uint64_t> configured{0};
+  *err = raise_smem_limit_once(kernel, smem, configured);
   if (*err != cudaSuccess) return true;
   const int64_t tiles = elems / kPackTile;
   kernel<<<static_cast<unsigned>(tiles < sms ? tiles : sms), kPackThreads, smem, stream>>>(src, elems, planes);
