@@ -24,7 +24,14 @@ JSON line; they are measurements for the record, the driver runs C3), and
 
 Multi-GPU (torchrun, one rank per GPU): rows are sharded, each rank owns a
 slab of A and C of the config's size and a full B (weak scaling, no collective
-on the data path); value = all ranks' work / max-over-ranks time.
+on the data path); value = all ranks' work / max-over-ranks time. With several
+ranks the line also carries `strong_scaling`: the config's one product split
+into 2-D output blocks (rank (i, j) packs row slab i of A and column slab j of
+B), its max-over-ranks step time and rank 0's per-stage times.
+
+Inputs are the reference benchmark's: one std::mt19937_64(1) draws A, then B
+(uniform_int_distribution), so the CPU oracle checks the GPU's output on a
+sample of rows (`parity`) and times the same sample (`cpu_baseline`).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config C1..C5|W] [--size S (C3 only: M = N = K = S)]
@@ -109,19 +116,21 @@ def parse():
                     help="CPU sample (rows of A; tasks for C2) for the oracle parity check, the CPU baseline and the "
                          "reference arm (0: the config's)")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle comparison (and the CPU baseline)")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="with several GPUs, skip the strong-scaling measurement attached to the weak line")
     ap.add_argument("--size", type=int, default=0,
                     help="C3 only: M = N = K = size (8192 is the benchmark; smaller sizes are for ncu captures)")
-    ap.add_argument("--shard", choices=["weak-rows", "rows", "planes"], default="weak-rows",
-                    help="weak-rows: each rank owns an M-row slab (the benchmark line); rows / planes: the "
-                         "config's one product split across ranks by row slabs / by residue planes with the "
-                         "fused NVLink exchange (strong scaling, device-resident, for comparing the two)")
+    ap.add_argument("--shard", choices=["weak-rows", "rows", "grid", "planes"], default="weak-rows",
+                    help="weak-rows: each rank owns an M-row slab (the benchmark line); rows / grid / planes: the "
+                         "config's one product split across ranks by row slabs / by 2-D output blocks / by residue "
+                         "planes with the fused NVLink exchange (strong scaling, device-resident)")
     ap.add_argument("--exchange", choices=["fused", "copy"], default="fused",
                     help="--shard planes: epilogue stores into the slab owners' buffers, or local planes + copies")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch every step's kernels from the host instead of replaying a captured CUDA graph")
     args = ap.parse_args()
     if args.shard != "weak-rows" and cfg_kind(args.config) not in ("i64", "u64", "exact"):
-        ap.error("--shard rows|planes applies to the int64/uint64/exact-wide configs")
+        ap.error("--shard rows|grid|planes applies to the int64/uint64/exact-wide configs")
     cfg = CONFIGS[args.config]
     if args.size:
         if cfg.name != "C3":
@@ -627,6 +636,9 @@ class ShardedProduct:
 
     rows:   rank r packs its row slab of A and all of B into every plane,
             multiplies and exports its slab (no exchange).
+    grid:   the output split into row_groups x col_groups blocks
+            (rns8_b200.shard.output_tile): rank (i, j) packs row slab i of A
+            and column slab j of B, so B's pack is divided too; no exchange.
     planes: rank r packs all of A and B into its planes {p : p mod world == r},
             multiplies them for all of C with the row-slab scatter epilogue
             (each output row stored into its owner's receive buffer, over
@@ -646,13 +658,16 @@ class ShardedProduct:
         self.A = torch.from_numpy(self.hA.view("int64")).to("cuda")
         self.B = torch.from_numpy(self.hB.view("int64")).to("cuda")
         self.signed = cfg.kind != "u64"
+        self.col0, self.cols = 0, n
         if mode == "planes":
             self.row0, self.rows = shard.slab_of_rank(rank, m, world)
+        elif mode == "grid":
+            self.row0, self.rows, self.col0, self.cols = shard.output_tile(rank, world, m, n)
         else:
             self.row0, self.rows = shard.row_slab(rank, world, m)
         self.status = torch.zeros(4, dtype=torch.int32, device="cuda")
-        shape = (max(self.rows, 1), n, cfg.limbs) if cfg.kind == "exact" else (max(self.rows, 1), n)
-        self.out = torch.empty(shape, dtype=torch.int64, device="cuda")
+        r, c = max(self.rows, 1), max(self.cols, 1)
+        self.out = torch.empty((r, c, cfg.limbs) if cfg.kind == "exact" else (r, c), dtype=torch.int64, device="cuda")
         self.launches_per_step = 0
         if mode == "planes":
             self.mine = shard.planes_of_rank(rank, world, P)
@@ -669,17 +684,20 @@ class ShardedProduct:
             self.step_index = 0
         else:
             self.ex = None
-            r = max(self.rows, 1)
             self.ra = torch.empty((P, r, k), dtype=torch.int8, device="cuda")
-            self.rb = torch.empty((P, k, n), dtype=torch.int8, device="cuda")
-            self.rc = torch.empty((P, r, n), dtype=torch.int8, device="cuda")
-            self.sbytes = lib.rns8_cuda_gemm_rns_scratch_bytes(dev, r, n, k, P)
+            self.rb = torch.empty((P, k, c), dtype=torch.int8, device="cuda")
+            self.rc = torch.empty((P, r, c), dtype=torch.int8, device="cuda")
+            self.sbytes = lib.rns8_cuda_gemm_rns_scratch_bytes(dev, r, c, k, P)
         self.scratch = torch.empty(max(1, self.sbytes), dtype=torch.uint8, device="cuda")
 
-    def step(self):
+    def step(self, events=None):
+        """One step; with `events` (four CUDA events) the pack, GEMM and export
+        boundaries are recorded (row and grid modes)."""
         cfg, lib, d, s = self.cfg, self.lib, self.dev, self.sptr
         m, n, k, P = cfg.m, cfg.n, cfg.k, cfg.prefix
         chk = DevicePipeline._check
+        stream = self.torch.cuda.current_stream()
+        mark = (lambda i: events[i].record(stream)) if events else (lambda i: None)
         launches = 0
         if self.mode == "planes":
             b = self.step_index % 2
@@ -697,41 +715,109 @@ class ShardedProduct:
             if self.world > 1:
                 self.dist.all_reduce(self.flag)  # every rank's scatter into this rank's buffer has completed
             planes = self.ex.receive_buffer(b)
+            ld_out = n
         else:
-            if self.rows:
+            if self.rows and self.cols:
                 pk = lib.rns8_cuda_pack_i64_device if self.signed else lib.rns8_cuda_pack_u64_device
+                mark(0)
                 chk(pk(d, self.A.data_ptr() + self.row0 * k * 8, self.rows, k, k, P, self.ra.data_ptr(), s), "pack A")
-                chk(pk(d, self.B.data_ptr(), k, n, n, P, self.rb.data_ptr(), s), "pack B")
+                chk(pk(d, self.B.data_ptr() + self.col0 * 8, k, self.cols, n, P, self.rb.data_ptr(), s), "pack B")
+                mark(1)
                 chk(lib.rns8_cuda_gemm_rns_device(d, self.ra.data_ptr(), self.rb.data_ptr(), self.rc.data_ptr(),
-                                                  self.rows, n, k, P, 0, self.scratch.data_ptr(), self.sbytes,
+                                                  self.rows, self.cols, k, P, 0, self.scratch.data_ptr(), self.sbytes,
                                                   self.status.data_ptr(), s), "gemm")
+                mark(2)
                 launches += 3
             planes = self.rc.data_ptr()
-        if self.rows:
+            ld_out = self.cols
+        if self.rows and self.cols:
+            cols = self.cols if self.mode != "planes" else n
             if cfg.kind == "exact":
-                st = lib.rns8_cuda_export_limbs_device(d, planes, self.rows, n, P, 1, cfg.limbs, self.out.data_ptr(),
-                                                       n, self.status.data_ptr(), s)
+                st = lib.rns8_cuda_export_limbs_device(d, planes, self.rows, cols, P, 1, cfg.limbs,
+                                                       self.out.data_ptr(), ld_out, self.status.data_ptr(), s)
             else:
                 fn = lib.rns8_cuda_export_i64_device if self.signed else lib.rns8_cuda_export_u64_device
-                st = fn(d, planes, self.rows, n, P, cfg.bound, self.out.data_ptr(), n, self.status.data_ptr(), s)
+                st = fn(d, planes, self.rows, cols, P, cfg.bound, self.out.data_ptr(), ld_out,
+                        self.status.data_ptr(), s)
             chk(st, "export")
             launches += 1
+            if self.mode != "planes":
+                mark(3)
         self.launches_per_step = launches
 
-    def check_against_rows(self):
-        """This rank's slab against the unsharded pipeline on this GPU."""
+    def check_against_unsharded(self):
+        """This rank's block against the unsharded pipeline on this GPU, and
+        its first rows against the CPU oracle."""
+        import numpy as np
+
         cfg = self.cfg
-        if not self.rows:
+        if not self.rows or not self.cols:
             return True
-        sub = dataclasses.replace(cfg, m=self.rows)
-        pipe = DevicePipeline(self.torch, self.lib, sub, self.dev, self.hA[self.row0:self.row0 + self.rows], self.hB)
+        sub = dataclasses.replace(cfg, m=self.rows, n=self.cols)
+        hb = np.ascontiguousarray(self.hB[:, self.col0:self.col0 + self.cols])
+        pipe = DevicePipeline(self.torch, self.lib, sub, self.dev, self.hA[self.row0:self.row0 + self.rows], hb)
         pipe.step()
         self.torch.cuda.synchronize()
-        return bool(self.torch.equal(pipe.out, self.out[: self.rows])) and pipe.device_status() == 0
+        same = bool(self.torch.equal(pipe.out, self.out[: self.rows, : self.cols])) and pipe.device_status() == 0
+        _, want = cpu_sample(sub, self.hA[self.row0:self.row0 + self.rows], hb, min(8, self.rows))
+        got = self.out[:8].cpu().numpy().view("uint64" if cfg.kind in ("u64", "exact") else "int64")
+        return same and bool((got[: want.shape[0]] == want.view(got.dtype)).all())
 
     def close(self):
         if self.ex is not None:
             self.ex.close()
+
+
+def measure_sharded(args, cfg: Config, torch, dist, lib, rank: int, world: int, local: int, mode: str,
+                    exchange: str) -> dict:
+    """One strong-scaling measurement: max-over-ranks device time of K steps
+    of the sharded product, per-stage times (rank 0's, row and grid modes),
+    and the AND over ranks of every block's check."""
+    stream = torch.cuda.current_stream()
+    sptr = C.c_void_p(stream.cuda_stream)
+    job = ShardedProduct(torch, dist, lib, cfg, local, rank, world, mode, exchange, sptr)
+    for _ in range(max(3, args.warmup)):
+        job.step()
+    torch.cuda.synchronize()
+    ok = job.check_against_unsharded()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        job.step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    stages = None
+    if mode != "planes":
+        recs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        job.step()  # lead-in work
+        for i in range(args.steps):
+            job.step(recs[i])
+        torch.cuda.synchronize()
+        stages = {name: statistics.median(r[i].elapsed_time(r[i + 1]) for r in recs)
+                  for i, name in enumerate(("pack", "plane_gemm", "export"))}
+    status = int(job.status[0].item())
+    t = torch.tensor([start.elapsed_time(stop), 0.0 if (ok and status == 0) else 1.0], dtype=torch.float64,
+                     device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if float(t[1].item()) != 0.0:
+        raise RuntimeError("sharded result differs from the unsharded pipeline or the oracle (or a device status was set)")
+    ms_per_step = float(t[0].item()) / args.steps
+    from rns8_b200.shard import grid_shape
+
+    groups = (world, 1) if mode != "grid" else grid_shape(world)
+    res = {"mode": mode, "n_gpus": world, "ms_per_step": ms_per_step, "value": cfg.ops / (ms_per_step * 1e-3) / 1e9,
+           "unit": "GOPS", "scaling": "strong", "block": {"rows": job.rows, "cols": job.cols},
+           "grid": list(groups) if mode != "planes" else None, "stages_ms_rank0": stages,
+           "exchange": (("fused epilogue scatter" if job.fused.value else "local planes + copies")
+                        if mode == "planes" else "none"),
+           "checked": "every rank's block equals the unsharded pipeline's and its first rows the oracle's",
+           "gpu_launches": job.launches_per_step * args.steps}
+    job.close()
+    return res
 
 
 def run_sharded(args, cfg: Config) -> None:
@@ -748,53 +834,26 @@ def run_sharded(args, cfg: Config) -> None:
     import rns8_b200 as r8
 
     lib = r8.lib()
-    stream = torch.cuda.current_stream()
-    sptr = C.c_void_p(stream.cuda_stream)
-    job = ShardedProduct(torch, dist, lib, cfg, local, rank, world, args.shard, args.exchange, sptr)
-    for _ in range(max(3, args.warmup)):
-        job.step()
-    torch.cuda.synchronize()
-    ok = job.check_against_rows()
-    if world > 1:
-        dist.barrier()
     clocks = ClockSampler(local)
-    torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     h0 = time.monotonic()
-    start.record(stream)
-    for _ in range(args.steps):
-        job.step()
-    stop.record(stream)
-    torch.cuda.synchronize()
+    res = measure_sharded(args, cfg, torch, dist, lib, rank, world, local, args.shard, args.exchange)
     clocks.mark(h0, time.monotonic())
     clock_info = clocks.stop()
-    status = int(job.status[0].item())
-    t = torch.tensor([start.elapsed_time(stop), 0.0 if (ok and status == 0) else 1.0], dtype=torch.float64,
-                     device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    if float(t[1].item()) != 0.0:
-        raise RuntimeError("sharded result differs from the unsharded pipeline (or a device status was set)")
-    ms_per_step = float(t[0].item()) / args.steps
     if rank == 0:
         line = {
-            "metric": METRIC, "value": cfg.ops / (ms_per_step * 1e-3) / 1e9, "unit": "GOPS", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int64",
-            "data": "synthetic",
+            "metric": METRIC, "value": res["value"], "unit": "GOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
             "config": {"workload": cfg.workload, "name": cfg.name, "m": cfg.m, "n": cfg.n, "k": cfg.k,
-                       "prefix": cfg.prefix, "parallelism": f"{args.shard} x{world}",
-                       "exchange": (("fused epilogue scatter" if job.fused.value else "local planes + copies")
-                                    if args.shard == "planes" else "none"),
-                       "l2": "inputs larger than L2"},
+                       "prefix": cfg.prefix, "parallelism": f"{args.shard} x{world}", "exchange": res["exchange"],
+                       "grid": res["grid"], "block": res["block"], "seed": SEED, "l2": "inputs larger than L2"},
+            "stages_ms_rank0": res["stages_ms_rank0"],
             "e2e": None, "note": "strong-scaling variant (device-resident); the benchmark line is --shard weak-rows",
-            "checked": "every rank's slab equals the unsharded pipeline's", "clocks": clock_info,
-            "gpu_launches": job.launches_per_step * args.steps,
+            "checked": res["checked"], "clocks": clock_info, "gpu_launches": res["gpu_launches"],
         }
         print(json.dumps(line), flush=True)
-    job.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -982,6 +1041,12 @@ def main():
         if rank == 0 and world == 1:
             cpu = info
 
+    # ---- strong scaling beside the weak line: the config's one product split
+    # into 2-D output blocks over the ranks (no exchange) --------------------------
+    strong = None
+    if world > 1 and not args.no_strong and cfg.kind in ("i64", "u64", "exact"):
+        strong = measure_sharded(args, cfg, torch, dist, lib, rank, world, local, "grid", "fused")
+
     # Roofline of the dominant stage (one kernel launch per stage, except that
     # the grouped finite GEMM launches once per 32 tasks).
     work = pipe.stage_work()
@@ -1021,7 +1086,7 @@ def main():
             "stages_timing": ("median over the steps of events between per-stage graph replays"
                               if stage_graphs is not None else "median over the steps of events between host launches"),
             "stage_frac_of_peak": stage_frac,
-            "e2e": e2e, "cpu_baseline": cpu, "parity": parity, "clocks": clock_info,
+            "e2e": e2e, "cpu_baseline": cpu, "parity": parity, "strong_scaling": strong, "clocks": clock_info,
             "gpu_launches": pipe.launches_per_step * args.steps,
         }
         line["config"]["seed"] = SEED

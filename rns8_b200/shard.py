@@ -1,9 +1,11 @@
-"""Row-slab sharding of the RNS8 GEMM across GPUs (one process per GPU).
+"""Sharding of the RNS8 GEMM across GPUs (one process per GPU).
 
 Output rows are independent: rank r of `world` computes rows
 [row0, row0 + rows) of C from the same rows of A and all of B, with no
 exchange between ranks: output row slabs are independent units.
 The split is as even as possible; earlier ranks take the remainder rows.
+The 2-D partition (output_tile) also splits the columns, so that each rank
+packs a column slab of B instead of all of it.
 """
 
 from __future__ import annotations
@@ -17,6 +19,29 @@ def row_slab(rank: int, world: int, m: int) -> tuple[int, int]:
     rows = base + (1 if rank < extra else 0)
     row0 = rank * base + min(rank, extra)
     return row0, rows
+
+
+def grid_shape(world: int) -> tuple[int, int]:
+    """(row_groups, col_groups) of the 2-D output partition: the factor pair of
+    world closest to square, with at least as many row groups as column
+    groups (1 -> 1x1, 2 -> 2x1, 4 -> 2x2, 8 -> 4x2)."""
+    if world <= 0:
+        raise ValueError("need world >= 1")
+    cols = max(c for c in range(1, int(world**0.5) + 1) if world % c == 0)
+    return world // cols, cols
+
+
+def output_tile(rank: int, world: int, m: int, n: int) -> tuple[int, int, int, int]:
+    """(row0, rows, col0, cols) of rank's block of an m x n output under the
+    2-D partition: rank = i * col_groups + j owns row slab i of A and C and
+    column slab j of B and C, so it packs only its own slabs and no rank
+    exchanges anything."""
+    r, c = grid_shape(world)
+    if not 0 <= rank < world:
+        raise ValueError("need 0 <= rank < world")
+    row0, rows = row_slab(rank // c, r, m)
+    col0, cols = row_slab(rank % c, c, n)
+    return row0, rows, col0, cols
 
 
 def gemm_i64_row_sharded(ctx, desc, A, B, rank: int, world: int, out=None):

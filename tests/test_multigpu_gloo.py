@@ -11,7 +11,7 @@ import pytest
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from rns8_b200.shard import row_slab
+from rns8_b200.shard import grid_shape, output_tile, row_slab
 
 
 def test_row_slab_partitions_rows():
@@ -26,6 +26,59 @@ def test_row_slab_partitions_rows():
             assert max(r for _, r in spans) - min(r for _, r in spans) <= 1
     with pytest.raises(ValueError):
         row_slab(2, 2, 10)
+
+
+def test_output_tile_partitions_the_output():
+    assert [grid_shape(w) for w in (1, 2, 3, 4, 6, 8)] == [(1, 1), (2, 1), (3, 1), (2, 2), (3, 2), (4, 2)]
+    for m, n in ((8192, 8192), (4700, 4080), (7, 3), (1, 1)):
+        for world in (1, 2, 3, 4, 8):
+            cover = np.zeros((m, n), np.int32)
+            for r in range(world):
+                row0, rows, col0, cols = output_tile(r, world, m, n)
+                cover[row0:row0 + rows, col0:col0 + cols] += 1
+            assert (cover == 1).all()
+    with pytest.raises(ValueError):
+        output_tile(4, 4, 10, 10)
+
+
+def _grid_worker(rank, world, port, m, n, k, q):
+    from oracle import bridge
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    rng = np.random.default_rng(43)
+    A = rng.integers(-(2**20), 2**20, (m, k), dtype=np.int64, endpoint=True)
+    B = rng.integers(-(2**20), 2**20, (k, n), dtype=np.int64, endpoint=True)
+    row0, rows, col0, cols = output_tile(rank, world, m, n)
+    # Each rank touches only its row slab of A and column slab of B.
+    st, C, _ = bridge.gemm_bounded_oneshot(np.ascontiguousarray(A[row0:row0 + rows]),
+                                           np.ascontiguousarray(B[:, col0:col0 + cols]), k * 2**40)
+    assert st == 0
+    parts = [None] * world
+    dist.all_gather_object(parts, (row0, col0, C))
+    if rank == 0:
+        full = np.zeros((m, n), np.int64)
+        for r0, c0, c in parts:
+            full[r0:r0 + c.shape[0], c0:c0 + c.shape[1]] = c
+        st, want, _ = bridge.gemm_bounded_oneshot(A, B, k * 2**40)
+        q.put(bool(np.array_equal(full, want)))
+    dist.destroy_process_group()
+
+
+def test_output_tile_gemm_four_gloo_ranks():
+    """2 x 2 output blocks on four gloo ranks, each from its own A row slab and
+    B column slab, gathered into the unsharded product."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_grid_worker, args=(r, 4, port, 67, 45, 33, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    ok = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert ok
 
 
 def _free_port():
