@@ -437,6 +437,179 @@ __global__ void __launch_bounds__(kWsThreads, 1) export_bounded_ws_kernel(Export
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(a.status, kDevRangeError);
 }
 
+// ---- exact-wide limb export, streamed ---------------------------------------------
+// The same producer / consumer ring as the bounded export, with tiles of 2048
+// cells (each lane takes four consecutive cells, one 32-bit word per plane)
+// and the wide fractional CRT of export_limbs_frac_kernel per cell. With
+// three limbs and a contiguous, 16-byte aligned destination, a lane's four
+// cells are twelve consecutive limbs, written as six 16-byte stores.
+constexpr int kLimbTileCells = kWsConsumerWarps * 32 * 4;
+
+template <int P, Mode kMode>
+__device__ __forceinline__ void limbs_from_words(const ExportArgs& a, uint32_t (&w)[4 * ((P + 3) / 4)], int64_t first,
+                                                 bool vec3, bool& bad) {
+  constexpr int kG = (P + 3) / 4;
+  constexpr GarnerTable<P> GT = make_table<P>();
+#pragma unroll
+  for (int p = 0; p < 4 * kG; ++p) w[p] = p < P ? (w[p] ^ 0x80808080u) : 0u;
+  uint32_t cw[4][kG];
+#pragma unroll
+  for (int q = 0; q < kG; ++q) {  // 4 x 4 byte transpose: plane words -> cell words
+    const uint32_t t0 = __byte_perm(w[4 * q], w[4 * q + 1], 0x5140);
+    const uint32_t t1 = __byte_perm(w[4 * q + 2], w[4 * q + 3], 0x5140);
+    const uint32_t t2 = __byte_perm(w[4 * q], w[4 * q + 1], 0x7362);
+    const uint32_t t3 = __byte_perm(w[4 * q + 2], w[4 * q + 3], 0x7362);
+    cw[0][q] = __byte_perm(t0, t1, 0x5410);
+    cw[1][q] = __byte_perm(t0, t1, 0x7632);
+    cw[2][q] = __byte_perm(t2, t3, 0x5410);
+    cw[3][q] = __byte_perm(t2, t3, 0x7632);
+  }
+  uint32_t undecided = 0;
+  uint64_t limbs[4][3];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v[6];
+    if (!wide_frac_reconstruct<P>(cw[c], v)) {
+      undecided |= 1u << c;
+      limbs[c][0] = limbs[c][1] = limbs[c][2] = 0;
+      continue;
+    }
+    if constexpr (kMode == Mode::LimbsUnsigned) {
+      if (v[5] >> 31) {  // centered value below zero: the canonical value is v + M
+        uint64_t carry = 0;
+#pragma unroll
+        for (int l = 0; l < 6; ++l) {
+          const uint64_t t = static_cast<uint64_t>(v[l]) + (l < kLimbs32 ? GT.product[l] : 0u) + carry;
+          v[l] = static_cast<uint32_t>(t);
+          carry = t >> 32;
+        }
+      }
+    }
+    if (vec3) {
+#pragma unroll
+      for (int l = 0; l < 3; ++l)
+        limbs[c][l] = static_cast<uint64_t>(v[2 * l]) | (static_cast<uint64_t>(v[2 * l + 1]) << 32);
+    } else {
+      bad |= !store_limbs<kMode>(a, first + c, v);
+    }
+  }
+  if (vec3) {  // 12 limbs of 4 cells, 96 contiguous bytes
+    ulonglong2* out = reinterpret_cast<ulonglong2*>(static_cast<uint64_t*>(a.dst) + first * 3);
+#pragma unroll
+    for (int j = 0; j < 6; ++j) {
+      const int i0 = 2 * j, i1 = 2 * j + 1;
+      __stcs(out + j, make_ulonglong2(static_cast<unsigned long long>(limbs[i0 / 3][i0 % 3]),
+                                      static_cast<unsigned long long>(limbs[i1 / 3][i1 % 3])));
+    }
+  }
+  while (undecided != 0) {  // rewrites the placeholder limbs of undecided cells
+    const int c = __ffs(undecided) - 1;
+    undecided &= undecided - 1;
+    int r[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p) r[p] = static_cast<int>((w[p] >> (8 * c)) & 0xFFu) - 128;
+    bad |= !export_cell<P, kMode>(a, first + c, r);
+  }
+}
+
+template <int P, Mode kMode, int kStages>
+__global__ void __launch_bounds__(kWsThreads, 1) export_limbs_ws_kernel(ExportArgs a) {
+  constexpr int kG = (P + 3) / 4;
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[kStages], empty[kStages];
+  const int64_t cells = a.m * a.n;
+  const int64_t tiles = cells / kLimbTileCells;
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWsConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  int64_t mine = 0;
+  if (blockIdx.x < tiles) mine = (tiles - 1 - blockIdx.x) / gridDim.x + 1;
+  if (warp == kWsConsumerWarps) {
+    if (lane != 0) return;
+    int64_t issued = 0;
+    for (int64_t j = 0; j < mine; ++j, ++issued) {
+      const int s = static_cast<int>(j % kStages);
+      if (j >= kStages && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((j / kStages) - 1) & 1))) {
+        atomicOr(a.status, kDevWaitTimeout);
+        break;
+      }
+      const int64_t tile = blockIdx.x + j * gridDim.x;
+      mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(P * kLimbTileCells));
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+        bulk_load_1d(ring + (s * P + p) * kLimbTileCells,
+                     a.planes + static_cast<int64_t>(p) * cells + tile * kLimbTileCells, kLimbTileCells, &full[s]);
+    }
+    for (int64_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+      if (!mbar_wait_bounded(&full[j % kStages], static_cast<uint32_t>((j / kStages) & 1)))
+        atomicOr(a.status, kDevWaitTimeout);
+    return;
+  }
+  const bool vec3 = a.limb_count == 3 && a.ld == a.n && reinterpret_cast<uintptr_t>(a.dst) % 16 == 0;
+  bool bad = false;
+  const int off = (warp * 32 + lane) * 4;
+  for (int64_t j = 0; j < mine; ++j) {
+    const int s = static_cast<int>(j % kStages);
+    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((j / kStages) & 1))) {
+      if (lane == 0) atomicOr(a.status, kDevWaitTimeout);
+      break;
+    }
+    uint32_t w[4 * kG];
+#pragma unroll
+    for (int p = 0; p < P; ++p) w[p] = *reinterpret_cast<const uint32_t*>(ring + (s * P + p) * kLimbTileCells + off);
+    release_stage_reads();  // the stage is refilled once every warp has arrived on empty[s]
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    limbs_from_words<P, kMode>(a, w, (blockIdx.x + j * gridDim.x) * kLimbTileCells + off, vec3, bad);
+  }
+  // The last, partial tile (fewer than 2048 cells): one CTA, exact path.
+  if (blockIdx.x == tiles % gridDim.x) {
+    for (int64_t c = tiles * kLimbTileCells + warp * 32 + lane; c < cells; c += kWsConsumerWarps * 32) {
+      int r[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) r[p] = a.planes[static_cast<int64_t>(p) * cells + c];
+      bad |= !export_cell<P, kMode>(a, c, r);
+    }
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(a.status, kDevRangeError);
+}
+
+template <int P>
+constexpr int limb_ws_stages() {
+  constexpr int by_smem = (224 * 1024) / (P * kLimbTileCells);
+  return by_smem > 4 ? 4 : by_smem;
+}
+
+template <int P, Mode kMode>
+bool launch_limbs_ws(const ExportArgs& a, cudaStream_t stream, cudaError_t* err) {
+  constexpr int kStages = limb_ws_stages<P>();
+  const int64_t cells = a.m * a.n;
+  if (kStages < 2 || P < 2 || reinterpret_cast<uintptr_t>(a.planes) % 16 != 0 || cells % 16 != 0 ||
+      cells < kLimbTileCells)
+    return false;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    *err = cudaGetLastError();
+    return true;
+  }
+  const int smem = kStages * P * kLimbTileCells;
+  auto kernel = export_limbs_ws_kernel<P, kMode, kStages>;
+  static std::atomic<uint64_t> configured{0};
+  *err = raise_smem_limit_once(kernel, smem, configured);
+  if (*err != cudaSuccess) return true;
+  const int64_t tiles = cells / kLimbTileCells;
+  kernel<<<static_cast<unsigned>(tiles < sms ? tiles : sms), kWsThreads, smem, stream>>>(a);
+  *err = cudaGetLastError();
+  return true;
+}
+
 template <int P>
 constexpr int ws_stages() {
   constexpr int by_smem = (224 * 1024) / (P * kWsTileCells);
@@ -506,6 +679,8 @@ cudaError_t launch_export(const ExportArgs& a, cudaStream_t stream) {
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   if constexpr (kMode == Mode::LimbsSigned || kMode == Mode::LimbsUnsigned) {
+    cudaError_t ws_err = cudaSuccess;
+    if (launch_limbs_ws<P, kMode>(a, stream, &ws_err)) return ws_err;
     if (vec && P >= 2) {
       export_limbs_frac_kernel<P, kMode><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
       return cudaGetLastError();
