@@ -980,6 +980,26 @@ def main():
     torch.cuda.synchronize()
     stage_ms = {name: statistics.median(r[i].elapsed_time(r[i + 1]) for r in records)
                 for i, name in enumerate(("pack", "plane_gemm", "export"))}
+    # Each stage alone: the stage graph replayed after a 256 MiB write that
+    # evicts L2, instead of after the stage before it (in a step, the
+    # memory-bound stages follow the GEMM, which runs at the power cap, and
+    # start at the clock it leaves); median over the steps.
+    stage_alone_ms = None
+    if stage_graphs is not None:
+        evict = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        names = ("pack", "plane_gemm", "export")
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in names]
+              for _ in range(args.steps)]
+        for i in range(args.steps):
+            for j in range(3):
+                evict.zero_()
+                ev[i][j][0].record(stream)
+                stage_graphs[j].replay()
+                ev[i][j][1].record(stream)
+        torch.cuda.synchronize()
+        stage_alone_ms = {name: statistics.median(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(args.steps))
+                          for j, name in enumerate(names)}
+        del evict
     if pipe.device_status() != 0:
         raise RuntimeError(f"device status {pipe.device_status():#x} in the stage timing")
 
@@ -1055,10 +1075,15 @@ def main():
     hbm_note = "MEASURED_PEAKS.json hbm_gbs (STREAM copy)" if not peaks.get("fallback") else "fallback 6650 GB/s"
     kernel_names = {"pack": "pack_kernel", "plane_gemm": "tc_wrap64_kernel" if cfg.kind == "wrap" else
                     "tc_plane_gemm_kernel", "export": "export kernel"}
-    stage_frac = {}
-    for name, (bound, amount) in work.items():
-        sec = max(stage_ms[name], 1e-6) * 1e-3
-        stage_frac[name] = (amount / sec / 1e12 / peak_int8) if bound == "tensor" else (amount / sec / 1e9 / hbm)
+    def frac_of(times):
+        out = {}
+        for name, (bound, amount) in work.items():
+            sec = max(times[name], 1e-6) * 1e-3
+            out[name] = (amount / sec / 1e12 / peak_int8) if bound == "tensor" else (amount / sec / 1e9 / hbm)
+        return out
+
+    stage_frac = frac_of(stage_ms)
+    stage_frac_alone = frac_of(stage_alone_ms) if stage_alone_ms else None
     bound, amount = work[dominant]
     sec = stage_ms[dominant] * 1e-3
     if bound == "tensor":
@@ -1086,6 +1111,8 @@ def main():
             "stages_timing": ("median over the steps of events between per-stage graph replays"
                               if stage_graphs is not None else "median over the steps of events between host launches"),
             "stage_frac_of_peak": stage_frac,
+            "stages_alone_ms": stage_alone_ms,
+            "stage_frac_of_peak_alone": stage_frac_alone,
             "e2e": e2e, "cpu_baseline": cpu, "parity": parity, "strong_scaling": strong, "clocks": clock_info,
             "gpu_launches": pipe.launches_per_step * args.steps,
         }
