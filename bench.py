@@ -868,8 +868,8 @@ def main():
         run_sharded(args, cfg)
         return
     rank, world, local = dist_env()
-    if world > 1:  # ranks share the host's cores for the oracle check
-        os.environ.setdefault("OMP_NUM_THREADS", str(max(1, (os.cpu_count() or 1) // world)))
+    if world > 1:  # ranks share the host's cores for the oracle check (torchrun's default is one thread)
+        os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // world))
     hostA, hostB = seeded_inputs(cfg, rank)
     import torch
     import torch.distributed as dist
