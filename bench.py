@@ -396,6 +396,9 @@ def reference_arm(args, cfg: Config) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
         return
+    # Every host thread, also under torchrun (whose default is one thread per
+    # process); set before the oracle library, and its OpenMP runtime, load.
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
     A, B = seeded_inputs(cfg, 0)
     wall0 = time.perf_counter()
     for _ in range(args.warmup):
