@@ -24,3 +24,29 @@ def test_reference_arm_prints_one_contract_line():
     assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "GOPS"
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+
+
+def test_bench_checksum_and_sample_helpers():
+    """The FNV output checksum (rns8_bench_support.cpp:96-99) gives the same
+    value for bytes as for the same values widened to uint64, and the CPU
+    sample of C1 (the whole product) equals the oracle's one-shot."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from oracle import bridge
+
+    rng = np.random.default_rng(5)
+    u8 = rng.integers(0, 251, (3, 40, 37), dtype=np.uint8)
+    assert bench.fnv_checksum(u8) == bridge.checksum(u8.astype(np.uint64).reshape(3, -1))
+    big = rng.integers(0, 256, (5 << 20) + 3, dtype=np.uint8)  # more than one chunk
+    assert bench.fnv_checksum(big.reshape(1, -1)) == bridge.checksum(big.astype(np.uint64).reshape(1, -1))
+    cfg = bench.CONFIGS["C1"]
+    A, B = bench.seeded_inputs(cfg, 0)
+    info, out = bench.cpu_sample(cfg, A, B, cfg.m)
+    st, want, _ = bridge.gemm_bounded_oneshot(A, B, cfg.bound)
+    assert st == 0 and np.array_equal(out, want)
+    assert info["kind"] == "port" and info["value"] > 0
+    # Rank 1 shares rank 0's B and draws its own A.
+    A1, B1 = bench.seeded_inputs(cfg, 1)
+    assert np.array_equal(B1, B) and not np.array_equal(A1, A)
