@@ -19,7 +19,8 @@ cudaError_t simt_plane_gemm(const PlaneGemmProblem& prob, cudaStream_t stream);
 bool skinny_path_supported(const PlaneGemmProblem& prob);
 uint64_t skinny_scratch_bytes(const PlaneGemmProblem& prob);
 cudaError_t skinny_plane_gemm(const PlaneGemmProblem& prob, void* scratch, uint64_t scratch_bytes,
-                              cudaStream_t stream);
+                              cudaStream_t stream,
+                              int sm_count_hint);
 
 // Split-K decomposition chosen for the tensor-core kernel.
 struct TcSchedule {

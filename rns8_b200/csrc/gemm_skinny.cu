@@ -16,6 +16,8 @@
 //           per-block residues are congruent to the reference's folded running
 //           residue (cpu_reference.cpp:171-174), so the bytes are identical.
 #include "device_common.cuh"
+#include <algorithm>
+
 #include "gemm_internal.hpp"
 
 namespace rns8cuda {
@@ -144,6 +146,88 @@ __global__ void __launch_bounds__(256) skinny_kernel(const SkinnyParams prm) {
 
 int padded_np(int64_t n) { return n <= 4 ? 4 : (n <= 8 ? 8 : 16); }
 
+// ---- few rows: K split across warps ----------------------------------------------
+// With few rows (a GEMV, or an output of a handful of cells) the row-parallel
+// kernel above runs one warp per row group down the whole of K, which leaves
+// the GPU idle and the call latency-bound (1 x 1 x 65536: 146 us). Here each
+// warp takes a row group and one K chunk of at most 65536 products: its exact
+// int32 sums are reduced to centered residues and added (atomically) into an
+// int32 accumulator per output cell; a finalize pass reduces each
+// accumulator. The accumulated residues of the chunks are congruent to the
+// reference's folded running residue, so the bytes are identical.
+constexpr int64_t kSplitMaxRows = 1024;  // the accumulator area is reserved up to this many rows
+
+template <int NP, bool kVec>
+__global__ void __launch_bounds__(256) skinny_split_kernel(const SkinnyParams prm, int64_t chunk, int64_t chunks,
+                                                           int32_t* __restrict__ acc_out) {
+  constexpr int R = rows_per_warp<NP>();
+  constexpr int kStep = kVec ? 16 : 4;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t ci = static_cast<int64_t>(blockIdx.x) * 8 + warp;  // this warp's K chunk
+  if (ci >= chunks) return;  // whole warp: the shuffles below are never reached by part of one
+  const uint32_t p = blockIdx.y;
+  const int64_t m = prm.m, n = prm.n, k = prm.k, kp = prm.kp;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.z) * R;
+  const int8_t* a = prm.a + static_cast<int64_t>(p) * m * k;
+  const int8_t* bt = prm.bt + static_cast<int64_t>(p) * NP * kp;
+  const ModConst mc = make_mod_const(prm.moduli.m[p]);
+  const int64_t s0 = ci * chunk, s1 = s0 + chunk < k ? s0 + chunk : k;
+  int32_t acc[R][NP];
+#pragma unroll
+  for (int i = 0; i < R; ++i)
+#pragma unroll
+    for (int j = 0; j < NP; ++j) acc[i][j] = 0;
+  for (int64_t kk = s0 + static_cast<int64_t>(lane) * kStep; kk < s1; kk += 32 * kStep) {
+    if constexpr (kVec) {
+      uint4 aw[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        aw[i] = (r0 + i < m) ? __ldcs(reinterpret_cast<const uint4*>(a + (r0 + i) * k + kk)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        const uint4 bw = __ldg(reinterpret_cast<const uint4*>(bt + j * kp + kk));
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          int32_t v = acc[i][j];
+          v = __dp4a(static_cast<int>(aw[i].x), static_cast<int>(bw.x), v);
+          v = __dp4a(static_cast<int>(aw[i].y), static_cast<int>(bw.y), v);
+          v = __dp4a(static_cast<int>(aw[i].z), static_cast<int>(bw.z), v);
+          v = __dp4a(static_cast<int>(aw[i].w), static_cast<int>(bw.w), v);
+          acc[i][j] = v;
+        }
+      }
+    } else {
+      uint32_t aw[R];
+#pragma unroll
+      for (int i = 0; i < R; ++i) aw[i] = load_a4(a + (r0 + i < m ? r0 + i : 0) * k, k, kk, r0 + i < m);
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        const uint32_t bw = *reinterpret_cast<const uint32_t*>(bt + j * kp + kk);
+#pragma unroll
+        for (int i = 0; i < R; ++i) acc[i][j] = __dp4a(static_cast<int>(aw[i]), static_cast<int>(bw), acc[i][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i)
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const int32_t res = reduce_i32_centered(warp_sum(acc[i][j]), mc);
+      if (lane == j && j < n && r0 + i < m) atomicAdd(acc_out + (static_cast<int64_t>(p) * m + r0 + i) * n + j, res);
+    }
+}
+
+__global__ void __launch_bounds__(256) skinny_finalize_kernel(const int32_t* __restrict__ acc, int64_t cells,
+                                                              PlaneModuli moduli, int8_t* __restrict__ c) {
+  const uint32_t p = blockIdx.y;
+  const ModConst mc = make_mod_const(moduli.m[p]);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < cells;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    c[static_cast<int64_t>(p) * cells + i] = static_cast<int8_t>(reduce_i32_centered(acc[static_cast<int64_t>(p) * cells + i], mc));
+}
+
+uint64_t round256(uint64_t v) { return (v + 255) / 256 * 256; }
+
 }  // namespace
 
 bool skinny_path_supported(const PlaneGemmProblem& prob) {
@@ -153,11 +237,13 @@ bool skinny_path_supported(const PlaneGemmProblem& prob) {
 uint64_t skinny_scratch_bytes(const PlaneGemmProblem& prob) {
   if (!skinny_path_supported(prob)) return 0;
   const int64_t kp = (prob.k + 15) / 16 * 16;
-  return static_cast<uint64_t>(prob.planes) * padded_np(prob.n) * kp;
+  const uint64_t bt = round256(static_cast<uint64_t>(prob.planes) * padded_np(prob.n) * kp);
+  const uint64_t acc = prob.m <= kSplitMaxRows ? static_cast<uint64_t>(prob.planes) * prob.m * prob.n * 4 : 0;
+  return bt + acc;
 }
 
 cudaError_t skinny_plane_gemm(const PlaneGemmProblem& prob, void* scratch, uint64_t scratch_bytes,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, int sm_count_hint) {
   if (!skinny_path_supported(prob) || !scratch || scratch_bytes < skinny_scratch_bytes(prob))
     return cudaErrorInvalidValue;
   const int np = padded_np(prob.n);
@@ -176,6 +262,36 @@ cudaError_t skinny_plane_gemm(const PlaneGemmProblem& prob, void* scratch, uint6
     const bool vec = prob.k % 16 == 0 && reinterpret_cast<uintptr_t>(task.a) % 16 == 0;
     const int64_t rows_per_block = 8 * (np == 16 ? 2 : 4);
     const int64_t blocks = (prob.m + rows_per_block - 1) / rows_per_block;
+    if (prob.m <= kSplitMaxRows && blocks * prob.planes < sm_count_hint) {
+      // Few rows: split K so that about 4 x 148 x 8 warps share the work.
+      const int R = np == 16 ? 2 : 4;
+      const int64_t groups = (prob.m + R - 1) / R;
+      const int64_t step = 32 * (vec ? 16 : 4);  // K one warp covers per iteration
+      const int64_t want = std::max<int64_t>(1, (4 * 8 * static_cast<int64_t>(sm_count_hint)) /
+                                                    (groups * static_cast<int64_t>(prob.planes)));
+      int64_t chunk = (prob.k + want - 1) / want;
+      chunk = (chunk + step - 1) / step * step;
+      if (chunk > kSegment) chunk = kSegment;  // exact int32 sums
+      const int64_t chunks = (prob.k + chunk - 1) / chunk;
+      int32_t* acc = reinterpret_cast<int32_t*>(static_cast<int8_t*>(scratch) +
+                                                round256(static_cast<uint64_t>(prob.planes) * np * kp));
+      const int64_t cells = prob.m * prob.n;
+      e = cudaMemsetAsync(acc, 0, static_cast<size_t>(cells) * prob.planes * sizeof(int32_t), stream);
+      if (e != cudaSuccess) return e;
+      const dim3 sgrid(static_cast<unsigned>((chunks + 7) / 8), prob.planes, static_cast<unsigned>(groups));
+#define RNS8_SPLIT(NP)                                                                                        \
+  (vec ? (skinny_split_kernel<NP, true><<<sgrid, 256, 0, stream>>>(prm, chunk, chunks, acc), cudaGetLastError()) \
+       : (skinny_split_kernel<NP, false><<<sgrid, 256, 0, stream>>>(prm, chunk, chunks, acc), cudaGetLastError()))
+      e = np == 4 ? RNS8_SPLIT(4) : (np == 8 ? RNS8_SPLIT(8) : RNS8_SPLIT(16));
+#undef RNS8_SPLIT
+      if (e != cudaSuccess) return e;
+      const int64_t fb = (cells + 255) / 256;
+      skinny_finalize_kernel<<<dim3(static_cast<unsigned>(fb < 1024 ? fb : 1024), prob.planes), 256, 0, stream>>>(
+          acc, cells, pm, task.c);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+      continue;
+    }
     const dim3 grid(static_cast<unsigned>(blocks < (int64_t{1} << 30) ? blocks : (int64_t{1} << 30)), prob.planes);
 #define RNS8_SKINNY(NP)                                                          \
   (vec ? (skinny_kernel<NP, true><<<grid, 256, 0, stream>>>(prm), cudaGetLastError()) \

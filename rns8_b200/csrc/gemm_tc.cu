@@ -848,13 +848,16 @@ __global__ void __launch_bounds__(256) pad_planes_kernel(const int8_t* __restric
                                                          uint32_t planes, int8_t* __restrict__ dst, int64_t drows,
                                                          int64_t dcols) {
   const int64_t chunks = dcols / 16;
-  const int64_t total_rows = static_cast<int64_t>(planes) * drows;
-  for (int64_t pr = blockIdx.y; pr < total_rows; pr += gridDim.y) {
+  const int64_t total = static_cast<int64_t>(planes) * drows * chunks;
+  // (row, chunk) pairs flattened, so narrow rows (a few chunks each) still
+  // give every thread work.
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t pr = idx / chunks, ch = idx - pr * chunks;
     const int64_t p = pr / drows, r = pr - p * drows;
     uint4* out = reinterpret_cast<uint4*>(dst + pr * dcols);
     const uint8_t* row = reinterpret_cast<const uint8_t*>(src) + (p * rows + r) * cols;
-    for (int64_t ch = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; ch < chunks;
-         ch += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    {
       const int64_t c0 = ch * 16;
       uint32_t w[4] = {0, 0, 0, 0};
       if (r < rows && c0 < cols) {
@@ -935,13 +938,6 @@ unsigned flat_grid(int64_t work, int sm_count) {
   return static_cast<unsigned>(blocks < 1 ? 1 : (blocks < cap ? blocks : cap));
 }
 
-dim3 row_grid(int64_t chunks_per_row, int64_t total_rows, int sm_count) {
-  const int64_t bx = (chunks_per_row + 255) / 256;
-  int64_t by = total_rows < 65535 ? total_rows : 65535;
-  const int64_t want = static_cast<int64_t>(sm_count) * 16;  // blocks in flight
-  if (bx * by > want) by = std::max<int64_t>(1, want / bx);
-  return dim3(static_cast<unsigned>(bx < 1 ? 1 : bx), static_cast<unsigned>(by < 1 ? 1 : by));
-}
 
 
 struct PadPlan {
@@ -1021,10 +1017,10 @@ cudaError_t padded_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* 
       int8_t* b = pp.pad_b ? reinterpret_cast<int8_t*>(slot + pp.a_bytes) : const_cast<int8_t*>(tasks[t].b);
       int8_t* c = pp.pad_c ? reinterpret_cast<int8_t*>(slot + pp.a_bytes + pp.b_bytes) : tasks[t].c;
       if (pp.pad_a)
-        pad_planes_kernel<<<row_grid(pp.kp / 16, prob.planes * prob.m, sm_count), 256, 0, stream>>>(
+        pad_planes_kernel<<<flat_grid(prob.planes * prob.m * (pp.kp / 16), sm_count), 256, 0, stream>>>(
             tasks[t].a, prob.m, prob.k, prob.planes, a, prob.m, pp.kp);
       if (pp.pad_b)
-        pad_planes_kernel<<<row_grid(pp.np / 16, prob.planes * pp.kp, sm_count), 256, 0, stream>>>(
+        pad_planes_kernel<<<flat_grid(prob.planes * pp.kp * (pp.np / 16), sm_count), 256, 0, stream>>>(
             tasks[t].b, prob.k, prob.n, prob.planes, b, pp.kp, pp.np);
       const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return e;
@@ -1076,7 +1072,7 @@ cudaError_t plane_gemm(const PlaneGemmProblem& prob, GemmPath path, int sm_count
   if (path == GemmPath::Auto && !tc_ok && skinny_path_supported(prob) && scratch &&
       scratch_bytes >= skinny_scratch_bytes(prob)) {
     if (used) *used = GemmPath::Simt;  // the narrow-output kernel (CUDA cores)
-    return skinny_plane_gemm(prob, scratch, scratch_bytes, stream);
+    return skinny_plane_gemm(prob, scratch, scratch_bytes, stream, sm_count);
   }
   if (path == GemmPath::Auto && !tc_ok && padded_path_possible(prob) && scratch &&
       scratch_bytes >= padded_scratch_bytes(prob, sm_count)) {

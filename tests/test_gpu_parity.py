@@ -253,12 +253,22 @@ def test_plane_gemm_k_longer_than_safe_block(lib, oracle, k):
     (64, 12, 4096),
     (300, 15, 70000),   # K above 65536: two exact int32 segments per row
     (1, 15, 33),
+    # Few rows: K split across warps, residues accumulated per cell, finalized.
+    (1, 1, 65536),
+    (1, 1, 131073),     # K above 65536 and not a multiple of 16
+    (2, 7, 65537),
+    (8, 8, 4096),
+    (64, 1, 8192),
+    (3, 15, 200000),
 ])
-def test_narrow_output_gemm_matches_oracle(lib, oracle, m, n, k):
-    """n < 16 runs the narrow-output kernel (B^T staging + dp4a stream); it
-    must agree with the oracle and with the SIMT kernel byte for byte."""
-    rng = np.random.default_rng(m * 31 + n * 7 + k)
-    P = 9
+@pytest.mark.parametrize("P", [9, 20])
+def test_narrow_output_gemm_matches_oracle(lib, oracle, m, n, k, P):
+    """n < 16 runs the narrow-output kernel (B^T staging + dp4a stream; with
+    few rows, K split across warps); it must agree with the oracle and with
+    the SIMT kernel byte for byte."""
+    if P == 20 and m * k > 600_000:
+        pytest.skip("the 20-plane case runs on the smaller shapes")
+    rng = np.random.default_rng(m * 31 + n * 7 + k + P)
     a = random_residues(rng, P, m, k)
     b = random_residues(rng, P, k, n)
     for p in range(P):  # the most negative residue of each plane along the first row
