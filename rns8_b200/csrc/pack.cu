@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(256) pack_scalar_kernel(const T* __restrict__ 
   }
 }
 
-// ---- streamed pack (compact sources) ---------------------------------------------
+// ---- streamed pack (compact or row-tiled sources) ---------------------------------------------
 // A persistent CTA per SM: one producer warp streams 4096-element tiles of
 // the source (32 KiB) into a ring of shared-memory stages with 1-D bulk
 // copies; 16 consumer warps convert eight elements per lane and store eight
@@ -139,6 +139,14 @@ constexpr int kPackWarps = 16;
 constexpr int kPackThreads = 32 * (kPackWarps + 1);
 constexpr int kPackTile = kPackWarps * 32 * 8;
 constexpr int kPackStages = 4;
+
+// Source element offset of tile t: the tiles of a row lie side by side
+// (row_tiles of them per row, rows ld elements apart); a compact source is one
+// row of all tiles. Plane offsets are always t * kPackTile (planes are compact).
+__device__ __forceinline__ int64_t tile_source(int64_t t, int64_t row_tiles, int64_t ld) {
+  const int64_t row = t / row_tiles;
+  return row * ld + (t - row * row_tiles) * kPackTile;
+}
 
 // The pack has no status word, so a bounded wait that runs out cannot be
 // reported; instead it cannot change the result: the warp that gives up sets
@@ -170,7 +178,8 @@ __device__ __forceinline__ void pack8_store(const int4 (&v)[4], int8_t* out, int
 
 template <int P, typename T>
 __global__ void __launch_bounds__(kPackThreads, 1) pack_ws_kernel(const T* __restrict__ src, int64_t elems,
-                                                                  int8_t* __restrict__ planes) {
+                                                                  int8_t* __restrict__ planes, int64_t row_tiles,
+                                                                  int64_t ld) {
   constexpr bool kSigned = static_cast<T>(-1) < 0;
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint64_t full[kPackStages], empty[kPackStages];
@@ -200,7 +209,8 @@ __global__ void __launch_bounds__(kPackThreads, 1) pack_ws_kernel(const T* __res
       }
       const int64_t tile = blockIdx.x + j * gridDim.x;
       mbar_arrive_expect_tx(&full[s], kPackTile * 8);
-      bulk_load_1d(ring + static_cast<size_t>(s) * kPackTile * 8, src + tile * kPackTile, kPackTile * 8, &full[s]);
+      bulk_load_1d(ring + static_cast<size_t>(s) * kPackTile * 8, src + tile_source(tile, row_tiles, ld),
+                   kPackTile * 8, &full[s]);
     }
     for (int64_t j = issued > kPackStages ? issued - kPackStages : 0; j < issued; ++j)
       (void)mbar_wait_bounded(&full[j % kPackStages], static_cast<uint32_t>((j / kPackStages) & 1));
@@ -223,7 +233,7 @@ __global__ void __launch_bounds__(kPackThreads, 1) pack_ws_kernel(const T* __res
     int4 v[4];
     if (direct) {  // a wait ran out somewhere in this block: read the tile from global memory
       *stop = 1;
-      const int4* gp = reinterpret_cast<const int4*>(src + tile * kPackTile) + tid * 4;
+      const int4* gp = reinterpret_cast<const int4*>(src + tile_source(tile, row_tiles, ld)) + tid * 4;
 #pragma unroll
       for (int q = 0; q < 4; ++q) v[q] = gp[(q + rot) & 3];
     } else {
@@ -249,11 +259,15 @@ __global__ void __launch_bounds__(kPackThreads, 1) pack_ws_kernel(const T* __res
 
 // Compact sources of at least one tile with a 16-byte aligned start and
 // 8-byte aligned planes take the streamed kernel.
+// Strided sources take it when every row is a whole number of tiles (a
+// column slab of B 4096 or 8192 wide, say) and rows start on 16 bytes.
 template <int P, typename T>
-bool launch_pack_ws(const T* src, int64_t elems, int8_t* planes, cudaStream_t stream, cudaError_t* err) {
+bool launch_pack_ws(const T* src, int64_t elems, int8_t* planes, cudaStream_t stream, cudaError_t* err,
+                    int64_t row_tiles = 0, int64_t ld = 0) {
   if (elems < kPackTile || elems % 8 != 0 || reinterpret_cast<uintptr_t>(src) % 16 != 0 ||
-      reinterpret_cast<uintptr_t>(planes) % 8 != 0)
+      reinterpret_cast<uintptr_t>(planes) % 8 != 0 || (row_tiles > 0 && ld % 2 != 0))
     return false;
+  if (row_tiles == 0) row_tiles = (elems + kPackTile - 1) / kPackTile;  // compact: one row of tiles
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
@@ -266,7 +280,8 @@ bool launch_pack_ws(const T* src, int64_t elems, int8_t* planes, cudaStream_t st
   *err = raise_smem_limit_once(kernel, smem, configured);
   if (*err != cudaSuccess) return true;
   const int64_t tiles = elems / kPackTile;
-  kernel<<<static_cast<unsigned>(tiles < sms ? tiles : sms), kPackThreads, smem, stream>>>(src, elems, planes);
+  kernel<<<static_cast<unsigned>(tiles < sms ? tiles : sms), kPackThreads, smem, stream>>>(src, elems, planes,
+                                                                                           row_tiles, ld);
   *err = cudaGetLastError();
   return true;
 }
@@ -279,6 +294,9 @@ cudaError_t launch_pack(const T* src, int64_t rows, int64_t cols, int64_t ld, in
     rows = 1;
     cudaError_t err = cudaSuccess;
     if (launch_pack_ws<P, T>(src, cols, planes, stream, &err)) return err;
+  } else if (cols % kPackTile == 0) {
+    cudaError_t err = cudaSuccess;
+    if (launch_pack_ws<P, T>(src, rows * cols, planes, stream, &err, cols / kPackTile, ld)) return err;
   }
   const bool vec = (cols % 8 == 0) && (ld % 2 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(planes) % 8 == 0);

@@ -62,6 +62,25 @@ def gemm_i64_row_sharded(ctx, desc, A, B, rank: int, world: int, out=None):
     return row0, api.gemm_i64_oneshot(ctx, d, a, B, out=out)
 
 
+def gemm_i64_block_sharded(ctx, desc, A, B, rank: int, world: int, out=None):
+    """This rank's block of C = A x B under the 2-D partition (output_tile),
+    through rns8_gemm_i64_oneshot on the rank's row slab of A and column slab
+    of B (a strided view: the one-shot reads it in place with ldb = n).
+
+    A and B are the full host arrays; desc describes the full problem.
+    Returns (row0, col0, C_block)."""
+    import numpy as np
+
+    from . import api
+
+    row0, rows, col0, cols = output_tile(rank, world, desc.m, desc.n)
+    if rows == 0 or cols == 0:
+        return row0, col0, np.zeros((rows, cols), np.int64)
+    d = api.gemm_desc(desc.semantics, desc.bound_kind, rows, cols, desc.k, bound=desc.bound,
+                      max_prefix=desc.max_prefix, flags=desc.flags, lhs_bound=desc.lhs_bound, rhs_bound=desc.rhs_bound)
+    return row0, col0, api.gemm_i64_oneshot(ctx, d, A[row0:row0 + rows], B[:, col0:col0 + cols], out=out)
+
+
 # ---- plane sharding ---------------------------------------------------------------
 # The alternative split for wide prefixes: rank r computes the residue planes
 # {p : p mod world == r} of ALL of C, then the planes are exchanged so that

@@ -53,7 +53,8 @@ def product(lib, A, B, row0, rows, col0, cols, P, bound):
 
 
 @pytest.mark.parametrize("m,n,k,world", [(2048, 2048, 1024, 4), (2048, 4096, 512, 8), (1000, 1040, 304, 4),
-                                         (700, 520, 96, 6)])
+                                         (700, 520, 96, 6),
+                                         (1024, 8192, 256, 8)])  # 4096-wide B slabs: the streamed pack, strided
 def test_output_blocks_equal_unsharded(lib, oracle, m, n, k, world):
     from rns8_b200.shard import output_tile
 
@@ -72,3 +73,39 @@ def test_output_blocks_equal_unsharded(lib, oracle, m, n, k, world):
         row0, nr, col0, nc = output_tile(r, world, m, n)
         block = product(lib, A, B, row0, nr, col0, nc, P, bound)
         assert torch.equal(block, whole[row0:row0 + nr, col0:col0 + nc]), f"rank {r}"
+
+
+@pytest.mark.parametrize("rows,cols,ld,signed", [(64, 4096, 8192, True), (33, 8192, 12288, False), (3, 4096, 4098, True)])
+def test_strided_pack_matches_oracle(lib, oracle, rows, cols, ld, signed):
+    """Sources whose rows are whole 4096-element tiles take the streamed pack
+    even when rows are ld apart; the planes must equal the oracle's."""
+    P = 20
+    rng = oracle.Rng(rows + cols + ld)
+    full = rng.i64(-(2**63), 2**63 - 1, (rows, ld)) if signed else rng.u64(0, 2**64 - 1, (rows, ld))
+    src = torch.from_numpy(full.view(np.int64)).cuda()
+    out = torch.empty((P, rows, cols), dtype=torch.int8, device="cuda")
+    fn = lib.rns8_cuda_pack_i64_device if signed else lib.rns8_cuda_pack_u64_device
+    assert fn(0, src.data_ptr(), rows, cols, ld, P, out.data_ptr(), stream()) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), oracle.pack(np.ascontiguousarray(full[:, :cols]), P))
+
+
+def test_block_sharded_oneshot_gathers_the_product(oracle):
+    """rns8_b200.shard.gemm_i64_block_sharded for every rank of 4 and 6 (on
+    one GPU, one after another) assembles the unsharded one-shot's result."""
+    import rns8_b200 as r8
+    from rns8_b200.shard import gemm_i64_block_sharded
+
+    m, n, k = 300, 520, 96
+    rng = oracle.Rng(77)
+    A = rng.i64(-(2**20), 2**20, (m, k))
+    B = rng.i64(-(2**20), 2**20, (k, n))
+    desc = r8.gemm_desc(r8.Semantics.BOUNDED_I64, r8.BoundKind.GLOBAL_MAX_ABS, m, n, k, bound=k * 2**40)
+    with r8.Context(0) as ctx:
+        want = r8.gemm_i64_oneshot(ctx, desc, A, B)
+        for world in (4, 6):
+            full = np.full((m, n), 7, np.int64)
+            for r in range(world):
+                row0, col0, blk = gemm_i64_block_sharded(ctx, desc, A, B, r, world)
+                full[row0:row0 + blk.shape[0], col0:col0 + blk.shape[1]] = blk
+            np.testing.assert_array_equal(full, want)
