@@ -983,25 +983,27 @@ def main():
     torch.cuda.synchronize()
     stage_ms = {name: statistics.median(r[i].elapsed_time(r[i + 1]) for r in records)
                 for i, name in enumerate(("pack", "plane_gemm", "export"))}
-    # Each stage alone: the stage graph replayed after a 256 MiB write that
-    # evicts L2, instead of after the stage before it (in a step, the
-    # memory-bound stages follow the GEMM, which runs at the power cap, and
-    # start at the clock it leaves); median over the steps.
+    # Each stage alone (the burst figure): after 5 ms with the GPU idle and a
+    # 256 MiB write that evicts L2, the stage graph replayed once; median over
+    # the steps. In a step the stages run back to back under the power drawn
+    # by the GEMM and the HBM traffic of their neighbours.
     stage_alone_ms = None
     if stage_graphs is not None:
         evict = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
         names = ("pack", "plane_gemm", "export")
-        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in names]
-              for _ in range(args.steps)]
+        alone = {name: [] for name in names}
         for i in range(args.steps):
-            for j in range(3):
+            for j, name in enumerate(names):
+                torch.cuda.synchronize()
+                time.sleep(0.005)
                 evict.zero_()
-                ev[i][j][0].record(stream)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
                 stage_graphs[j].replay()
-                ev[i][j][1].record(stream)
-        torch.cuda.synchronize()
-        stage_alone_ms = {name: statistics.median(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(args.steps))
-                          for j, name in enumerate(names)}
+                e1.record(stream)
+                torch.cuda.synchronize()
+                alone[name].append(e0.elapsed_time(e1))
+        stage_alone_ms = {name: statistics.median(v) for name, v in alone.items()}
         del evict
     if pipe.device_status() != 0:
         raise RuntimeError(f"device status {pipe.device_status():#x} in the stage timing")
