@@ -361,9 +361,10 @@ def product_planes(oracle, rng, m, n, k, prefix, lo, hi, dtype=np.int64):
 
 
 @pytest.mark.parametrize("prefix,bound_scale", [(9, 1), (7, 1), (20, 1), (9, 0)])
-def test_export_bounded_matches_oracle(lib, oracle, prefix, bound_scale):
-    rng = np.random.default_rng(prefix + bound_scale)
-    m, n, k = 48, 40, 64
+@pytest.mark.parametrize("m,n", [(48, 40), (96, 130)])  # 12480 cells: streamed kernel, partial last tile
+def test_export_bounded_matches_oracle(lib, oracle, prefix, bound_scale, m, n):
+    rng = np.random.default_rng(prefix + bound_scale + m)
+    k = 64
     lim = 2**24 if prefix == 7 else 2**28
     A, B, planes = product_planes(oracle, rng, m, n, k, prefix, -lim, lim)
     exact = np.array(oracle.exact_product(A, B), dtype=object)
@@ -480,9 +481,9 @@ def test_export_bounded_decision_edges(lib, oracle, prefix, signed):
 
 @pytest.mark.parametrize("prefix", [1, 9, 18, 20])
 @pytest.mark.parametrize("limbs", [1, 2, 3, 4, 8])
-def test_export_limbs_match_oracle(lib, oracle, prefix, limbs):
-    rng = np.random.default_rng(prefix * 31 + limbs)
-    m, n = 16, 24
+@pytest.mark.parametrize("m,n", [(16, 24), (70, 97)])  # 6790 cells: streamed kernel with a partial last tile
+def test_export_limbs_match_oracle(lib, oracle, prefix, limbs, m, n):
+    rng = np.random.default_rng(prefix * 31 + limbs + m)
     planes = random_residues(rng, prefix, m, n)
     planes[:, 0, 0] = 0
     for signed in (True, False):
