@@ -74,6 +74,9 @@ struct __align__(64) TcParams {
   uint64_t units;
   uint32_t* status;
   uint16_t moduli[20];
+  // Per plane, the constants of centered_byte() (EpilogueReduce, host-made).
+  uint32_t red_bias[20], red_magic[20];
+  uint8_t red_shift[20];
   // Scheduled plans: the units to run (plane | split << 8 | mt << 24 | nt << 44)
   // and, per schedule tile, its selected prefix (| 0x80 for a proven-zero
   // output, which is filled elsewhere); the epilogue stores a cell only when
@@ -96,6 +99,39 @@ struct __align__(64) TcParams {
 struct Unit {
   uint32_t t, p, mt, nt, kb0, kb1;
 };
+
+// Centered residue of an accumulator v modulo m (2 <= m <= 256) in five
+// integer operations: with h = floor(m/2) and u = v + h + m*ceil(2^30/m),
+// u mod m = (v + h) mod m and u - floor(u/m)*m - h is v's residue in
+// [-h, m-1-h]. A unit sums at most 65536 products of int8 values, so
+// |v| <= 2^30 and 0 <= u < 2^31 + 384. For such u, q = mulhi(u, magic) >> shift
+// is floor(u/m) exactly: with 2^shift <= m < 2^(shift+1) and the round-up
+// multiplier magic = ceil(2^(32+shift)/m) (Granlund-Montgomery), the excess
+// e = magic*m - 2^(32+shift) < m makes u*e < 2^(32+shift); powers of two use
+// mulhi(u, 2^31) >> (shift-1) = u >> shift, exact for every 32-bit u.
+struct EpilogueReduce {
+  uint32_t bias, magic, shift;
+};
+inline EpilogueReduce make_epilogue_reduce(uint32_t m) {
+  uint32_t s = 0;
+  while ((2u << s) <= m) ++s;  // 2^s <= m < 2^(s+1)
+  EpilogueReduce r;
+  if ((m & (m - 1)) == 0) {  // powers of two: mulhi(u, 2^31) >> (s-1) = u >> s
+    r.magic = 0x80000000u;
+    r.shift = s ? s - 1 : 0;
+  } else {
+    r.magic = static_cast<uint32_t>(((1ull << (32 + s)) + m - 1) / m);
+    r.shift = s;
+  }
+  r.bias = (m >> 1) + m * static_cast<uint32_t>(((1ull << 30) + m - 1) / m);
+  return r;
+}
+__device__ __forceinline__ uint32_t centered_byte(uint32_t v, uint32_t bias, uint32_t magic, uint32_t shift,
+                                                  uint32_t m, uint32_t h) {
+  const uint32_t u = v + bias;
+  const uint32_t q = __umulhi(u, magic) >> shift;
+  return u - (q * m + h);  // the low byte is the centered residue's
+}
 
 // 32-bit arithmetic with precomputed divisors (the host keeps the unit count
 // below 2^32): the producer and the MMA thread decode every unit at its start,
@@ -275,7 +311,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
         break;
       }
       tc_fence_after();
-      const ModConst mc = make_mod_const(prm.moduli[w.p]);
+      const uint32_t m_p = prm.moduli[w.p];
+      const ModConst mc = prm.scratch ? make_mod_const(m_p) : ModConst{};
+      const uint32_t rb = prm.red_bias[w.p], rm = prm.red_magic[w.p], rs = prm.red_shift[w.p], rh = m_p >> 1;
       const int64_t row = static_cast<int64_t>(w.mt) * BM + quarter * 32 + lane;
       const bool row_ok = row < prm.m;
       const int64_t plane_elems = prm.m * prm.n;
@@ -306,11 +344,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_plane_gemm_kernel(const __grid_
           uint32_t packed[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const uint32_t r0 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 0]), mc)) & 0xFFu;
-            const uint32_t r1 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 1]), mc)) & 0xFFu;
-            const uint32_t r2 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 2]), mc)) & 0xFFu;
-            const uint32_t r3 = static_cast<uint32_t>(reduce_i32_centered(static_cast<int32_t>(v[4 * q + 3]), mc)) & 0xFFu;
-            packed[q] = r0 | (r1 << 8) | (r2 << 16) | (r3 << 24);
+            const uint32_t r0 = centered_byte(v[4 * q + 0], rb, rm, rs, m_p, rh);
+            const uint32_t r1 = centered_byte(v[4 * q + 1], rb, rm, rs, m_p, rh);
+            const uint32_t r2 = centered_byte(v[4 * q + 2], rb, rm, rs, m_p, rh);
+            const uint32_t r3 = centered_byte(v[4 * q + 3], rb, rm, rs, m_p, rh);
+            packed[q] = __byte_perm(__byte_perm(r0, r1, 0x0040), __byte_perm(r2, r3, 0x0040), 0x5410);
           }
           // n is a multiple of 16, so a 32-column chunk is whole, half, or absent.
           uint4* dst = reinterpret_cast<uint4*>(crow + col);
@@ -724,7 +762,13 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
   prm.div_splits = make_fast_div(s.splits);
   prm.div_planes = make_fast_div(prob.planes);
   prm.div_span = make_fast_div(static_cast<uint32_t>(GROUP_M) * s.n_tiles);
-  for (uint32_t p = 0; p < prob.planes; ++p) prm.moduli[p] = prob.moduli[p];
+  for (uint32_t p = 0; p < prob.planes; ++p) {
+    prm.moduli[p] = prob.moduli[p];
+    const EpilogueReduce r = make_epilogue_reduce(prob.moduli[p]);
+    prm.red_bias[p] = r.bias;
+    prm.red_magic[p] = r.magic;
+    prm.red_shift[p] = static_cast<uint8_t>(r.shift);
+  }
   if (sched) {
     if (prob.task_count != 1) return cudaErrorInvalidValue;
     prm.unit_list = sched->units_dev;
