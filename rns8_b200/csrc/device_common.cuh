@@ -244,6 +244,12 @@ __host__ __device__ constexpr uint32_t make_idesc_i8(uint32_t m, uint32_t n, boo
          | ((m >> 4) << 24);             // M / 16
 }
 
+// Signed int8 A and B with A MN-major (its M elements contiguous, as in
+// compact residue planes read cell-major) and B K-major.
+__host__ __device__ constexpr uint32_t make_idesc_i8_mn_a(uint32_t m, uint32_t n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
 // Same layout for unsigned 8-bit A and B (formats 0): u8 x u8 -> s32, the
 // accumulator wrapping modulo 2^32 (saturation bit 3 left clear).
 __host__ __device__ constexpr uint32_t make_idesc_u8(uint32_t m, uint32_t n, bool b_mn_major) {

@@ -11,7 +11,10 @@
 #include <algorithm>
 #include <vector>
 
+#include <cstring>
+
 #include "garner.cuh"
+#include "gemm_internal.hpp"
 #include "kernels.hpp"
 
 namespace rns8cuda {
@@ -610,6 +613,350 @@ bool launch_limbs_ws(const ExportArgs& a, cudaStream_t stream, cudaError_t* err)
   return true;
 }
 
+// ---- exact-wide limb export on the tensor cores -----------------------------------
+// The byte-slice sums of the wide fractional CRT, sum_i r_i * digit_c(F_i) and
+// sum_i r_i * digit_c(G_i), form a [cells x planes] x [planes x digits] int8
+// product. One tcgen05 MMA per 128 cells (M = 128 cells, MN-major straight
+// from the compact planes; K = 32 planes, those past P zero-filled by TMA;
+// N = 32 digit columns, a constant table in shared memory) leaves every
+// cell's 32 sums in tensor memory, and the epilogue thread that owns the
+// cell combines them into the fraction, the quotient and the 192-bit value,
+// which takes the multiply work of the dp4a kernel off the integer pipe.
+// F_i and G_i are written in signed 8-bit digits (x = sum_c d_c 2^(8c),
+// d_c in [-128, 127]) so that both operands are s8 like the stored centered
+// residues; with r_i in place of u_i = r_i + 128 the constants become
+// s_init = 2^30 + bias * 2^31 and v = S + bias * M - q * M (mod 2^192). Each
+// sum has |sum| <= 20 * 128 * 128 < 2^19, so two neighbouring digit sums
+// combine in 32 bits (|T_c + 256 T_c+1| < 2^28) and a 32-bit limb of v is
+// one signed 64-bit accumulation: carry + bias*M limb + two such pairs
+// - q * M limb (q < 2^14), every term below 2^47.
+constexpr int kTcDigits = 32;   // N: digit columns
+constexpr int kTcFDigits = 5;   // F_i < 2^31 in signed digits (a carry can reach the fifth)
+constexpr int kTcBoxCells = 128;
+constexpr int kTcUnitCells = 4 * kTcBoxCells;  // one stage: four MMAs of 128 cells
+constexpr uint32_t kTcBoxBytes = kTcBoxCells * 32;
+constexpr uint32_t kTcStageBytes = 4 * kTcBoxBytes;
+constexpr int kTcStages = 12;
+constexpr int kTcEpiWarps = 16;  // four per tensor-memory lane quarter, one box of every stage each
+constexpr int kTcThreads = 32 * (2 + kTcEpiWarps);
+constexpr uint32_t kTcTmemCols = 2 * 4 * kTcDigits;  // two stages' accumulators
+constexpr uint32_t kTcTableBytes = kTcDigits * 128;  // 32 rows of 128 bytes (K-major, swizzled)
+constexpr size_t kTcSmemBytes = 1024 + kTcStages * kTcStageBytes + kTcTableBytes + 256;
+
+template <int P>
+struct TcDigitCount {
+  static constexpr int kBytes = wide_bytes<P>();
+  static constexpr int kG = kBytes + 1 > 24 ? 24 : kBytes + 1;  // signed digits of G_i (mod 2^192)
+};
+
+struct TcExportParams {
+  CUtensorMap tm;  // planes as (cells, P, 1), box {128, 32, 1}, 128-byte swizzle
+  ExportArgs a;
+  int8_t digits[kTcDigits][32];  // column c, plane i
+  uint32_t nc0[6];  // bias * M, the value's offset (< 2^168)
+  uint32_t product[kLimbs32];
+  uint64_t s_init;
+  uint32_t t_dec;
+  int64_t units;
+};
+
+// Signed digits of the little-endian 32-bit-limb value x (six limbs).
+inline void signed_digits(const uint64_t (&x)[6], int count, int8_t* out) {
+  int carry = 0;
+  for (int c = 0; c < count; ++c) {
+    const int byte = static_cast<int>((x[c / 4] >> (8 * (c % 4))) & 0xFFu) + carry;
+    if (byte >= 128) {
+      out[c] = static_cast<int8_t>(byte - 256);
+      carry = 1;
+    } else {
+      out[c] = static_cast<int8_t>(byte);
+      carry = 0;
+    }
+  }
+}
+
+template <int P>
+bool make_tc_export_params(TcExportParams& prm) {
+  static_assert(kTcFDigits + TcDigitCount<P>::kG <= kTcDigits, "digit columns exceed N");
+  std::memset(prm.digits, 0, sizeof(prm.digits));
+  uint64_t M[6] = {1, 0, 0, 0, 0, 0};
+  for (int i = 0; i < P; ++i) {
+    uint64_t carry = 0;
+    for (int l = 0; l < 6; ++l) {
+      const uint64_t v = M[l] * rns8ladder::kLadder[i] + carry;
+      M[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+  }
+  for (int l = 0; l < kLimbs32; ++l) prm.product[l] = static_cast<uint32_t>(M[l]);
+  for (int i = 0; i < P; ++i) {
+    const uint32_t mi = rns8ladder::kLadder[i];
+    uint64_t E[6] = {1, 0, 0, 0, 0, 0};  // M / m_i
+    uint32_t emod = 1;
+    for (int j = 0; j < P; ++j) {
+      if (j == i) continue;
+      uint64_t carry = 0;
+      for (int l = 0; l < 6; ++l) {
+        const uint64_t v = E[l] * rns8ladder::kLadder[j] + carry;
+        E[l] = v & 0xFFFFFFFFull;
+        carry = v >> 32;
+      }
+      emod = (emod * rns8ladder::kLadder[j]) % mi;
+    }
+    const uint32_t inv = inv_mod(emod, mi);
+    uint64_t G[6] = {0, 0, 0, 0, 0, 0}, carry = 0;  // E_i * inv_i < M
+    for (int l = 0; l < 6; ++l) {
+      const uint64_t v = E[l] * inv + carry;
+      G[l] = v & 0xFFFFFFFFull;
+      carry = v >> 32;
+    }
+    const uint64_t F = ((static_cast<uint64_t>(inv) << 31) + mi / 2) / mi;  // < 2^31
+    const uint64_t Fx[6] = {F & 0xFFFFFFFFull, F >> 32, 0, 0, 0, 0};
+    int8_t d[kTcDigits];
+    signed_digits(Fx, kTcFDigits, d);
+    for (int c = 0; c < kTcFDigits; ++c) prm.digits[c][i] = d[c];
+    signed_digits(G, TcDigitCount<P>::kG, d);
+    for (int c = 0; c < TcDigitCount<P>::kG; ++c) prm.digits[kTcFDigits + c][i] = d[c];
+  }
+  // bias * M (< 2^168)
+  uint64_t carry = 0;
+  for (int l = 0; l < 6; ++l) {
+    const uint64_t v = M[l] * static_cast<uint64_t>(kQuotientBias) + carry;
+    prm.nc0[l] = static_cast<uint32_t>(v & 0xFFFFFFFFull);
+    carry = v >> 32;
+  }
+  prm.s_init = (1ull << 30) + (static_cast<uint64_t>(kQuotientBias) << 31);
+  constexpr WideFracTable<P> kWide = make_wide_frac_table<P>();
+  prm.t_dec = kWide.t_dec;
+  return true;
+}
+
+// T_c + 256 * T_c+1 (or T_c alone): two digit sums in one 32-bit value.
+__device__ __forceinline__ int32_t digit_pair(const uint32_t (&t)[32], int c, bool both) {
+  const int32_t lo = static_cast<int32_t>(t[c]);
+  return both ? lo + static_cast<int32_t>(t[c + 1]) * 256 : lo;
+}
+
+template <int P, Mode kMode>
+__device__ __forceinline__ void tc_limb_cell(const TcExportParams& prm, int64_t cell, const uint32_t (&t)[32],
+                                             bool vec3, bool& bad) {
+  constexpr int kGD = TcDigitCount<P>::kG;
+  const ExportArgs& a = prm.a;
+  const int64_t s = static_cast<int64_t>(prm.s_init) + digit_pair(t, 0, true) +
+                    (static_cast<int64_t>(digit_pair(t, 2, true)) << 16) +
+                    (static_cast<int64_t>(static_cast<int32_t>(t[4])) << 32);
+  const int32_t frac = static_cast<int32_t>(static_cast<uint32_t>(s) & 0x7FFFFFFFu) - (1 << 30);
+  if (static_cast<uint32_t>(frac < 0 ? -frac : frac) > prm.t_dec) {  // quotient in doubt: exact path
+    const int64_t cells = a.m * a.n;
+    int r[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p) r[p] = a.planes[static_cast<int64_t>(p) * cells + cell];
+    bad |= !export_cell<P, kMode>(a, cell, r);
+    return;
+  }
+  const uint32_t q = static_cast<uint32_t>(static_cast<uint64_t>(s) >> 31);
+  uint32_t v[6];
+  int64_t carry = 0;
+#pragma unroll
+  for (int l = 0; l < 6; ++l) {  // v = S + bias * M - q * M  (mod 2^192)
+    int64_t acc = carry + static_cast<int64_t>(prm.nc0[l]) -
+                  static_cast<int64_t>(q) * static_cast<int64_t>(l < kLimbs32 ? prm.product[l] : 0u);
+    const int c = kTcFDigits + 4 * l;
+    if (4 * l < kGD) acc += digit_pair(t, c, 4 * l + 1 < kGD);
+    if (4 * l + 2 < kGD) acc += static_cast<int64_t>(digit_pair(t, c + 2, 4 * l + 3 < kGD)) << 16;
+    v[l] = static_cast<uint32_t>(acc);
+    carry = acc >> 32;
+  }
+  if constexpr (kMode == Mode::LimbsUnsigned) {  // centered value below zero: the canonical value is v + M
+    const uint32_t neg = static_cast<uint32_t>(static_cast<int32_t>(v[5]) >> 31);
+    uint64_t c = 0;
+#pragma unroll
+    for (int l = 0; l < 6; ++l) {
+      const uint64_t x = static_cast<uint64_t>(v[l]) + ((l < kLimbs32 ? prm.product[l] : 0u) & neg) + c;
+      v[l] = static_cast<uint32_t>(x);
+      c = x >> 32;
+    }
+  }
+  if (vec3) {
+    uint64_t* out = static_cast<uint64_t*>(a.dst) + cell * 3;
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+      __stcs(reinterpret_cast<unsigned long long*>(out + l),
+             static_cast<unsigned long long>(v[2 * l]) | (static_cast<unsigned long long>(v[2 * l + 1]) << 32));
+  } else {
+    bad |= !store_limbs<kMode>(a, cell, v);
+  }
+}
+
+template <int P, Mode kMode>
+__global__ void __launch_bounds__(kTcThreads, 1) export_limbs_tc_kernel(const __grid_constant__ TcExportParams prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* table = smem + kTcStages * kTcStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(table + kTcTableBytes);
+  uint64_t* empty = full + kTcStages;
+  uint64_t* acc_full = empty + kTcStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const ExportArgs& a = prm.a;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // Digit table as the B operand: row c (a digit column), logical byte i
+  // (a plane), K-major with the 128-byte swizzle (16-byte chunk i/16 of row
+  // c stored at chunk (i/16) ^ (c % 8)); the MMA reads bytes 0..31 of a row.
+  for (int e = threadIdx.x; e < kTcDigits * 32; e += blockDim.x) {
+    const int c = e >> 5, i = e & 31;
+    table[c * 128 + ((((i >> 4) ^ (c & 7)) << 4) | (i & 15))] = static_cast<uint8_t>(prm.digits[c][i]);
+  }
+  release_stage_reads();  // the table is read through the async proxy by the MMA
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kTcStages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kTcEpiWarps * 32);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&prm.tm);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- TMA producer ----------------
+      uint32_t pending = 0, pending_parity = 0;
+      int64_t j = 0;
+      for (int64_t u = blockIdx.x; u < prm.units; u += gridDim.x, ++j) {
+        const int st = static_cast<int>(j % kTcStages);
+        const uint32_t phase = static_cast<uint32_t>((j / kTcStages) & 1);
+        if (*abort_flag || !mbar_wait_bounded(&empty[st], phase ^ 1u)) {
+          if (!*abort_flag) {
+            *abort_flag = 1;
+            atomicOr(a.status, kDevWaitTimeout);
+          }
+          break;
+        }
+        mbar_arrive_expect_tx(&full[st], kTcStageBytes);
+        uint8_t* dst = smem + st * kTcStageBytes;
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          tma_load_3d(dst + b * kTcBoxBytes, &prm.tm, &full[st], static_cast<int32_t>(u * kTcUnitCells + b * kTcBoxCells),
+                      0, 0);
+        pending |= 1u << st;
+        pending_parity = (pending_parity & ~(1u << st)) | (phase << st);
+      }
+      // Loads issued but never consumed (abort path) land before exit.
+      for (int st = 0; st < kTcStages; ++st)
+        if (pending & (1u << st)) (void)mbar_wait_bounded(&full[st], (pending_parity >> st) & 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = make_idesc_i8_mn_a(128, kTcDigits);
+      const uint64_t bdesc = make_smem_desc_sw128(smem_u32(table), 16, 1024);
+      int64_t j = 0;
+      for (int64_t u = blockIdx.x; u < prm.units; u += gridDim.x, ++j) {
+        const int st = static_cast<int>(j % kTcStages);
+        const uint32_t phase = static_cast<uint32_t>((j / kTcStages) & 1);
+        const uint32_t acc = static_cast<uint32_t>(j & 1), acc_phase = static_cast<uint32_t>((j >> 1) & 1);
+        if (*abort_flag || !mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u) ||
+            !mbar_wait_bounded(&full[st], phase)) {
+          if (!*abort_flag) {
+            *abort_flag = 1;
+            atomicOr(a.status, kDevWaitTimeout);
+          }
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + st * kTcStageBytes);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          // A: 32 plane rows of 128 cells, 8-row swizzle atoms 1 KiB apart.
+          const uint64_t adesc = make_smem_desc_sw128(sa + b * kTcBoxBytes, kTcBoxBytes, 1024);
+          tc_mma_i8(tmem_base + acc * (4 * kTcDigits) + b * kTcDigits, adesc, bdesc, idesc, 0u);
+        }
+        tc_commit(&empty[st]);
+        tc_commit(&acc_full[acc]);
+      }
+      tc_commit(drain);
+      (void)mbar_wait_bounded(drain, 0);
+    }
+  } else {  // ---------------- epilogue (warps 2..9) ----------------
+    const uint32_t quarter = static_cast<uint32_t>(warp & 3);
+    const int box = (warp - 2) >> 2;  // this warp's box (128 cells) of every stage
+    const int64_t cells = a.m * a.n;
+    const bool vec3 = a.limb_count == 3 && a.ld == a.n;
+    bool bad = false;
+    int64_t j = 0;
+    for (int64_t u = blockIdx.x; u < prm.units; u += gridDim.x, ++j) {
+      const uint32_t acc = static_cast<uint32_t>(j & 1), acc_phase = static_cast<uint32_t>((j >> 1) & 1);
+      if (*abort_flag || !mbar_wait_bounded(&acc_full[acc], acc_phase)) {
+        if (!*abort_flag) {
+          *abort_flag = 1;
+          atomicOr(a.status, kDevWaitTimeout);
+        }
+        break;
+      }
+      tc_fence_after();
+      uint32_t t0[32];
+      tmem_ld_32x32b_x32(tmem_base + ((quarter * 32u) << 16) + acc * (4 * kTcDigits) + box * kTcDigits, t0);
+      tmem_wait_ld(t0);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      const int64_t cell = u * kTcUnitCells + box * kTcBoxCells + quarter * 32 + lane;
+      if (cell < cells) tc_limb_cell<P, kMode>(prm, cell, t0, vec3, bad);
+    }
+    if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(a.status, kDevRangeError);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTcTmemCols);
+  }
+}
+
+// The tensor-core limb export: 16-byte aligned planes, cells % 16 == 0, at
+// least one stage of cells and TMA coordinates within int32.
+template <int P, Mode kMode>
+bool launch_limbs_tc(const ExportArgs& a, cudaStream_t stream, cudaError_t* err) {
+  const int64_t cells = a.m * a.n;
+  if (P < 2 || cells % 16 != 0 || reinterpret_cast<uintptr_t>(a.planes) % 16 != 0 || cells < kTcUnitCells ||
+      cells > (int64_t{1} << 31) - 2 * kTcUnitCells)
+    return false;
+  static thread_local TcExportParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  if (!encode_plane_cells(&prm.tm, a.planes, static_cast<uint64_t>(cells), static_cast<uint32_t>(P)) ||
+      !make_tc_export_params<P>(prm))
+    return false;
+  prm.a = a;
+  prm.units = (cells + kTcUnitCells - 1) / kTcUnitCells;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    *err = cudaGetLastError();
+    return true;
+  }
+  auto kernel = export_limbs_tc_kernel<P, kMode>;
+  static std::atomic<uint64_t> configured{0};
+  *err = raise_smem_limit_once(kernel, static_cast<int>(kTcSmemBytes), configured);
+  if (*err != cudaSuccess) return true;
+  const int64_t grid = prm.units < sms ? prm.units : sms;
+  kernel<<<static_cast<unsigned>(grid), kTcThreads, kTcSmemBytes, stream>>>(prm);
+  *err = cudaGetLastError();
+  return true;
+}
+
 template <int P>
 constexpr int ws_stages() {
   constexpr int by_smem = (224 * 1024) / (P * kWsTileCells);
@@ -680,6 +1027,7 @@ cudaError_t launch_export(const ExportArgs& a, cudaStream_t stream) {
   if (blocks < 1) blocks = 1;
   if constexpr (kMode == Mode::LimbsSigned || kMode == Mode::LimbsUnsigned) {
     cudaError_t ws_err = cudaSuccess;
+    if (launch_limbs_tc<P, kMode>(a, stream, &ws_err)) return ws_err;
     if (launch_limbs_ws<P, kMode>(a, stream, &ws_err)) return ws_err;
     if (vec && P >= 2) {
       export_limbs_frac_kernel<P, kMode><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);

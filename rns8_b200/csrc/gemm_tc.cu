@@ -821,6 +821,18 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
 // ---- wrap64 host side -----------------------------------------------------------
 bool tma_encode_available() { return encode_fn() != nullptr; }
 
+bool encode_plane_cells(CUtensorMap* map, const void* planes, uint64_t cells, uint32_t plane_count) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || reinterpret_cast<uintptr_t>(planes) % 16 != 0 || cells % 16 != 0) return false;
+  const cuuint64_t dims[3] = {cells, plane_count, 1};
+  const cuuint64_t strides[2] = {cells, cells * plane_count};  // bytes, dims 1 and 2
+  const cuuint32_t box[3] = {128, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(planes), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t tc_wrap64_gemm(const uint8_t* a_limbs, const uint8_t* b_limbs, uint64_t* c, int64_t m, int64_t n,
                            int64_t k, int sm_count, uint32_t* dev_status, cudaStream_t stream) {
   static std::atomic<uint64_t> configured{0};

@@ -481,7 +481,10 @@ def test_export_bounded_decision_edges(lib, oracle, prefix, signed):
 
 @pytest.mark.parametrize("prefix", [1, 9, 18, 20])
 @pytest.mark.parametrize("limbs", [1, 2, 3, 4, 8])
-@pytest.mark.parametrize("m,n", [(16, 24), (70, 97)])  # 6790 cells: streamed kernel with a partial last tile
+# 384 cells: one-cell and vector kernels; 6790 (not a multiple of 16): the
+# streamed kernel with a partial last tile; 12480: the tensor-core kernel
+# with a partial last stage of 512 cells.
+@pytest.mark.parametrize("m,n", [(16, 24), (70, 97), (96, 130)])
 def test_export_limbs_match_oracle(lib, oracle, prefix, limbs, m, n):
     rng = np.random.default_rng(prefix * 31 + limbs + m)
     planes = random_residues(rng, prefix, m, n)
@@ -501,17 +504,20 @@ def test_export_limbs_match_oracle(lib, oracle, prefix, limbs, m, n):
 
 @pytest.mark.parametrize("prefix", [2, 9, 18, 20])
 @pytest.mark.parametrize("limbs", [3, 1])
-def test_export_limbs_near_half_range(lib, oracle, prefix, limbs):
+@pytest.mark.parametrize("shape", [(4, 8), (16, 64)])
+def test_export_limbs_near_half_range(lib, oracle, prefix, limbs, shape):
     """Values at and around +-M/2, where the fractional CRT's quotient is in
     doubt and the exact Garner path must take over, between ordinary values;
-    4-cell groups so the vector kernel runs."""
+    4 x 8 cells for the vector kernel, 16 x 64 (the values repeated) for the
+    tensor-core kernel."""
     M = 1
     for mm in LADDER[:prefix]:
         M *= mm
     h = M // 2
     vals = [h - 1, -h, h - 2, -h + 1, 0, 1, -1, h // 3, -(h // 5), h - (1 << 20), -h + (1 << 20), 12345]
     vals += [(i * 0x9E3779B97F4A7C15) % M - h for i in range(1, 21)]
-    m, n = 4, 8
+    m, n = shape
+    vals = (vals * (m * n // len(vals) + 1))[: m * n]
     centered = lambda v, mm: (lambda r: r - mm if r >= (mm + 1) // 2 else r)(v % mm)
     planes = np.array([[[centered(vals[r * n + c], mm) for c in range(n)] for r in range(m)] for mm in LADDER[:prefix]],
                       np.int8)
@@ -529,7 +535,7 @@ def test_export_limbs_near_half_range(lib, oracle, prefix, limbs):
 
 
 @pytest.mark.parametrize("case", KATS["exact_wide_limb_boundaries"]["cases"])
-@pytest.mark.parametrize("cells", [4, 1])  # the 4-cell vector kernel and the one-cell kernel
+@pytest.mark.parametrize("cells", [4, 1, 1024])  # vector, one-cell and tensor-core kernels
 def test_export_limbs_reference_boundaries(lib, case, cells):
     """The reference's exact-wide limb boundary answers on the GPU export; on a
     range error the destination keeps its bytes."""
