@@ -613,50 +613,68 @@ bool launch_limbs_ws(const ExportArgs& a, cudaStream_t stream, cudaError_t* err)
   return true;
 }
 
-// ---- exact-wide limb export on the tensor cores -----------------------------------
-// The byte-slice sums of the wide fractional CRT, sum_i r_i * digit_c(F_i) and
-// sum_i r_i * digit_c(G_i), form a [cells x planes] x [planes x digits] int8
-// product. One tcgen05 MMA per 128 cells (M = 128 cells, MN-major straight
-// from the compact planes; K = 32 planes, those past P zero-filled by TMA;
-// N = 32 digit columns, a constant table in shared memory) leaves every
-// cell's 32 sums in tensor memory, and the epilogue thread that owns the
-// cell combines them into the fraction, the quotient and the 192-bit value,
-// which takes the multiply work of the dp4a kernel off the integer pipe.
+// ---- exact-wide limb export on the tensor cores ----------------------------------
+// The wide fractional CRT's sums over the residue planes, sum_i r_i * F_i (the
+// quotient and fraction) and sum_i r_i * G_i (the value mod 2^192), split into
+// 8-bit digit columns, form an int8 product of the planes (cells x planes)
+// with a constant table (planes x 32 digit columns). One tcgen05 MMA per 128
+// cells (M = 128 cells read MN-major by TMA straight from the compact planes;
+// K = 32 planes; N = 32 digit columns from a table in shared memory) leaves
+// every cell's digit sums in tensor memory, and the epilogue thread that owns
+// the cell combines them, which takes the dp4a work off the integer pipe.
 // F_i and G_i are written in signed 8-bit digits (x = sum_c d_c 2^(8c),
 // d_c in [-128, 127]) so that both operands are s8 like the stored centered
-// residues; with r_i in place of u_i = r_i + 128 the constants become
-// s_init = 2^30 + bias * 2^31 and v = S + bias * M - q * M (mod 2^192). Each
-// sum has |sum| <= 20 * 128 * 128 < 2^19, so two neighbouring digit sums
-// combine in 32 bits (|T_c + 256 T_c+1| < 2^28) and a 32-bit limb of v is
-// one signed 64-bit accumulation: carry + bias*M limb + two such pairs
-// - q * M limb (q < 2^14), every term below 2^47.
-constexpr int kTcDigits = 32;   // N: digit columns
-constexpr int kTcFDigits = 5;   // F_i < 2^31 in signed digits (a carry can reach the fifth)
+// residues; with r_i in place of u_i = r_i + 128 the value is
+// v = S + bias*M - q*M, S = sum_c T_c 2^(8c). Each digit sum has
+// |T_c| <= 20 * 128 * 128 < 2^19, so two neighbouring sums combine in 32 bits
+// (|T_c + 256 T_c+1| < 2^28) and a 32-bit limb of v is one signed 64-bit
+// accumulation (carry + limb of bias*M + two pairs - q * limb of M, q < 2^14,
+// every term below 2^47). A box holds roundup(P, 8) plane rows; the MMA
+// always reads 32 rows, and table rows past P are zero, so the rows it reads
+// beyond the box (the next box, or the table) add nothing. (The bounded
+// int64 export built the same way, with 16 digit columns, ran at 342 us
+// against 200 us for the streamed dp2a kernel at 8192^2 x 9: with little
+// arithmetic per cell, the MMA -> tensor memory -> epilogue latency and the
+// cells that tensor memory can hold in flight set its rate.)
+constexpr int kTcFDigits = 5;  // F_i < 2^31 in signed digits (a carry can reach the fifth)
 constexpr int kTcBoxCells = 128;
-constexpr int kTcUnitCells = 4 * kTcBoxCells;  // one stage: four MMAs of 128 cells
-constexpr uint32_t kTcBoxBytes = kTcBoxCells * 32;
-constexpr uint32_t kTcStageBytes = 4 * kTcBoxBytes;
-constexpr int kTcStages = 12;
-constexpr int kTcEpiWarps = 16;  // four per tensor-memory lane quarter, one box of every stage each
+constexpr int kTcEpiWarps = 16;                // four groups of one warp per tensor-memory lane quarter
 constexpr int kTcThreads = 32 * (2 + kTcEpiWarps);
-constexpr uint32_t kTcTmemCols = 2 * 4 * kTcDigits;  // two stages' accumulators
-constexpr uint32_t kTcTableBytes = kTcDigits * 128;  // 32 rows of 128 bytes (K-major, swizzled)
-constexpr size_t kTcSmemBytes = 1024 + kTcStages * kTcStageBytes + kTcTableBytes + 256;
+constexpr uint32_t kTcTableBytes = 32 * 128;  // up to 32 rows of 128 bytes (K-major, swizzled)
+constexpr int kTcMaxStages = 24;
 
-template <int P>
-struct TcDigitCount {
-  static constexpr int kBytes = wide_bytes<P>();
-  static constexpr int kG = kBytes + 1 > 24 ? 24 : kBytes + 1;  // signed digits of G_i (mod 2^192)
+template <int P, Mode kMode>
+struct TcShape {
+  static_assert(kMode == Mode::LimbsSigned || kMode == Mode::LimbsUnsigned, "limb exports only");
+  static constexpr int kGDigits = wide_bytes<P>() + 1 > 24 ? 24 : wide_bytes<P>() + 1;
+  static constexpr int kN = 32;  // digit columns (MMA N)
+  // A stage is kBoxes consecutive 128-cell boxes, loaded by one TMA (each
+  // plane's kBoxes * 128 bytes in one piece) and multiplied by kBoxes MMAs.
+  static constexpr int kBoxes = 4;
+  static constexpr int kUnitCells = kBoxes * kTcBoxCells;
+  static constexpr int kBatch = 2;  // boxes an epilogue thread holds at once
+  static constexpr int kBoxRows = (P + 7) / 8 * 8;
+  static constexpr uint32_t kBoxBytes = kBoxRows * 128;
+  static constexpr uint32_t kStageBytes = kBoxes * kBoxBytes;
+  static constexpr int kStages = (192 * 1024) / kStageBytes > kTcMaxStages ? kTcMaxStages : (192 * 1024) / kStageBytes;
+  // Accumulators of several stages in flight (all 512 columns of tensor
+  // memory): with two, the MMA -> epilogue -> MMA hand-off latency capped
+  // the rate at about one stage per 0.5 us.
+  static constexpr int kAccBufs = 512 / (kBoxes * kN) > 8 ? 8 : 512 / (kBoxes * kN);
+  static constexpr uint32_t kTmemCols = kAccBufs * kBoxes * kN;
+  static_assert(kAccBufs % 4 == 0, "each accumulator buffer must belong to one epilogue group");
+  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kTcTableBytes + 1024;
+  static_assert(kTcFDigits + kGDigits <= kN, "digit columns exceed N");
 };
 
 struct TcExportParams {
-  CUtensorMap tm;  // planes as (cells, P, 1), box {128, 32, 1}, 128-byte swizzle
+  CUtensorMap tm;  // planes as (cells, P, 1), box {128, roundup(P, 8), 1}, 128-byte swizzle
   ExportArgs a;
-  int8_t digits[kTcDigits][32];  // column c, plane i
-  uint32_t nc0[6];  // bias * M, the value's offset (< 2^168)
+  int8_t digits[32][32];  // column c, plane i
+  uint32_t nc0[6];        // bias * M (< 2^168)
   uint32_t product[kLimbs32];
   uint64_t s_init;
-  uint32_t t_dec;
+  uint32_t t_dec;  // limbs: the quotient is certain when |frac| <= t_dec
   int64_t units;
 };
 
@@ -675,9 +693,9 @@ inline void signed_digits(const uint64_t (&x)[6], int count, int8_t* out) {
   }
 }
 
-template <int P>
-bool make_tc_export_params(TcExportParams& prm) {
-  static_assert(kTcFDigits + TcDigitCount<P>::kG <= kTcDigits, "digit columns exceed N");
+template <int P, Mode kMode>
+void make_tc_export_params(TcExportParams& prm) {
+  using S = TcShape<P, kMode>;
   std::memset(prm.digits, 0, sizeof(prm.digits));
   uint64_t M[6] = {1, 0, 0, 0, 0, 0};
   for (int i = 0; i < P; ++i) {
@@ -712,39 +730,44 @@ bool make_tc_export_params(TcExportParams& prm) {
     }
     const uint64_t F = ((static_cast<uint64_t>(inv) << 31) + mi / 2) / mi;  // < 2^31
     const uint64_t Fx[6] = {F & 0xFFFFFFFFull, F >> 32, 0, 0, 0, 0};
-    int8_t d[kTcDigits];
+    int8_t d[32];
     signed_digits(Fx, kTcFDigits, d);
     for (int c = 0; c < kTcFDigits; ++c) prm.digits[c][i] = d[c];
-    signed_digits(G, TcDigitCount<P>::kG, d);
-    for (int c = 0; c < TcDigitCount<P>::kG; ++c) prm.digits[kTcFDigits + c][i] = d[c];
+    signed_digits(G, S::kGDigits, d);  // mod 2^192
+    for (int c = 0; c < S::kGDigits; ++c) prm.digits[kTcFDigits + c][i] = d[c];
   }
-  // bias * M (< 2^168)
-  uint64_t carry = 0;
+  uint64_t carry = 0;  // bias * M
   for (int l = 0; l < 6; ++l) {
     const uint64_t v = M[l] * static_cast<uint64_t>(kQuotientBias) + carry;
     prm.nc0[l] = static_cast<uint32_t>(v & 0xFFFFFFFFull);
     carry = v >> 32;
   }
-  prm.s_init = (1ull << 30) + (static_cast<uint64_t>(kQuotientBias) << 31);
   constexpr WideFracTable<P> kWide = make_wide_frac_table<P>();
+  prm.s_init = (1ull << 30) + (static_cast<uint64_t>(kQuotientBias) << 31);
   prm.t_dec = kWide.t_dec;
-  return true;
 }
 
 // T_c + 256 * T_c+1 (or T_c alone): two digit sums in one 32-bit value.
-__device__ __forceinline__ int32_t digit_pair(const uint32_t (&t)[32], int c, bool both) {
+template <int kCols>
+__device__ __forceinline__ int32_t digit_pair(const uint32_t (&t)[kCols], int c, bool both) {
   const int32_t lo = static_cast<int32_t>(t[c]);
   return both ? lo + static_cast<int32_t>(t[c + 1]) * 256 : lo;
+}
+
+// s = s_init + sum_{c<5} T_c 2^(8c): the biased quotient above bit 31, the
+// fraction below.
+template <int kCols>
+__device__ __forceinline__ int64_t tc_fraction_sum(uint64_t s_init, const uint32_t (&t)[kCols]) {
+  return static_cast<int64_t>(s_init) + digit_pair(t, 0, true) + (static_cast<int64_t>(digit_pair(t, 2, true)) << 16) +
+         (static_cast<int64_t>(static_cast<int32_t>(t[4])) << 32);
 }
 
 template <int P, Mode kMode>
 __device__ __forceinline__ void tc_limb_cell(const TcExportParams& prm, int64_t cell, const uint32_t (&t)[32],
                                              bool vec3, bool& bad) {
-  constexpr int kGD = TcDigitCount<P>::kG;
+  constexpr int kGD = TcShape<P, kMode>::kGDigits;
   const ExportArgs& a = prm.a;
-  const int64_t s = static_cast<int64_t>(prm.s_init) + digit_pair(t, 0, true) +
-                    (static_cast<int64_t>(digit_pair(t, 2, true)) << 16) +
-                    (static_cast<int64_t>(static_cast<int32_t>(t[4])) << 32);
+  const int64_t s = tc_fraction_sum(prm.s_init, t);
   const int32_t frac = static_cast<int32_t>(static_cast<uint32_t>(s) & 0x7FFFFFFFu) - (1 << 30);
   if (static_cast<uint32_t>(frac < 0 ? -frac : frac) > prm.t_dec) {  // quotient in doubt: exact path
     const int64_t cells = a.m * a.n;
@@ -789,15 +812,17 @@ __device__ __forceinline__ void tc_limb_cell(const TcExportParams& prm, int64_t 
 }
 
 template <int P, Mode kMode>
-__global__ void __launch_bounds__(kTcThreads, 1) export_limbs_tc_kernel(const __grid_constant__ TcExportParams prm) {
+__global__ void __launch_bounds__(kTcThreads, 1) export_tc_kernel(const __grid_constant__ TcExportParams prm) {
+  using S = TcShape<P, kMode>;
+  constexpr int kN = S::kN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* table = smem + kTcStages * kTcStageBytes;
+  uint8_t* table = smem + S::kStages * S::kStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(table + kTcTableBytes);
-  uint64_t* empty = full + kTcStages;
-  uint64_t* acc_full = empty + kTcStages;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* empty = full + S::kStages;
+  uint64_t* acc_full = empty + S::kStages;
+  uint64_t* acc_empty = acc_full + S::kAccBufs;
+  uint64_t* drain = acc_empty + S::kAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const ExportArgs& a = prm.a;
@@ -806,19 +831,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) export_limbs_tc_kernel(const __
   // Digit table as the B operand: row c (a digit column), logical byte i
   // (a plane), K-major with the 128-byte swizzle (16-byte chunk i/16 of row
   // c stored at chunk (i/16) ^ (c % 8)); the MMA reads bytes 0..31 of a row.
-  for (int e = threadIdx.x; e < kTcDigits * 32; e += blockDim.x) {
+  for (int e = threadIdx.x; e < kN * 32; e += blockDim.x) {
     const int c = e >> 5, i = e & 31;
     table[c * 128 + ((((i >> 4) ^ (c & 7)) << 4) | (i & 15))] = static_cast<uint8_t>(prm.digits[c][i]);
   }
   release_stage_reads();  // the table is read through the async proxy by the MMA
   if (threadIdx.x == 0) {
-    for (int st = 0; st < kTcStages; ++st) {
+    for (int st = 0; st < S::kStages; ++st) {
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < S::kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kTcEpiWarps * 32);
+      mbar_init(&acc_empty[b], 4 * 32);  // the group that drains the buffer
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -826,65 +851,62 @@ __global__ void __launch_bounds__(kTcThreads, 1) export_limbs_tc_kernel(const __
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&prm.tm);
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_alloc(tmem_slot, S::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  auto give_up = [&] {  // a bounded wait ran out: every role stops at its next check
+    if (!*abort_flag) {
+      *abort_flag = 1;
+      atomicOr(a.status, kDevWaitTimeout);
+    }
+  };
 
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer ----------------
       uint32_t pending = 0, pending_parity = 0;
       int64_t j = 0;
       for (int64_t u = blockIdx.x; u < prm.units; u += gridDim.x, ++j) {
-        const int st = static_cast<int>(j % kTcStages);
-        const uint32_t phase = static_cast<uint32_t>((j / kTcStages) & 1);
+        const int st = static_cast<int>(j % S::kStages);
+        const uint32_t phase = static_cast<uint32_t>((j / S::kStages) & 1);
         if (*abort_flag || !mbar_wait_bounded(&empty[st], phase ^ 1u)) {
-          if (!*abort_flag) {
-            *abort_flag = 1;
-            atomicOr(a.status, kDevWaitTimeout);
-          }
+          give_up();
           break;
         }
-        mbar_arrive_expect_tx(&full[st], kTcStageBytes);
-        uint8_t* dst = smem + st * kTcStageBytes;
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-          tma_load_3d(dst + b * kTcBoxBytes, &prm.tm, &full[st], static_cast<int32_t>(u * kTcUnitCells + b * kTcBoxCells),
-                      0, 0);
+        mbar_arrive_expect_tx(&full[st], S::kStageBytes);
+        tma_load_3d(smem + st * S::kStageBytes, &prm.tm, &full[st], 0, 0, static_cast<int32_t>(u * S::kBoxes));
         pending |= 1u << st;
         pending_parity = (pending_parity & ~(1u << st)) | (phase << st);
       }
       // Loads issued but never consumed (abort path) land before exit.
-      for (int st = 0; st < kTcStages; ++st)
+      for (int st = 0; st < S::kStages; ++st)
         if (pending & (1u << st)) (void)mbar_wait_bounded(&full[st], (pending_parity >> st) & 1u);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = make_idesc_i8_mn_a(128, kTcDigits);
+      constexpr uint32_t idesc = make_idesc_i8_mn_a(128, kN);
       const uint64_t bdesc = make_smem_desc_sw128(smem_u32(table), 16, 1024);
       int64_t j = 0;
       for (int64_t u = blockIdx.x; u < prm.units; u += gridDim.x, ++j) {
-        const int st = static_cast<int>(j % kTcStages);
-        const uint32_t phase = static_cast<uint32_t>((j / kTcStages) & 1);
-        const uint32_t acc = static_cast<uint32_t>(j & 1), acc_phase = static_cast<uint32_t>((j >> 1) & 1);
+        const int st = static_cast<int>(j % S::kStages);
+        const uint32_t phase = static_cast<uint32_t>((j / S::kStages) & 1);
+        const uint32_t acc = static_cast<uint32_t>(j % S::kAccBufs);
+        const uint32_t acc_phase = static_cast<uint32_t>((j / S::kAccBufs) & 1);
         if (*abort_flag || !mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u) ||
             !mbar_wait_bounded(&full[st], phase)) {
-          if (!*abort_flag) {
-            *abort_flag = 1;
-            atomicOr(a.status, kDevWaitTimeout);
-          }
+          give_up();
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + st * kTcStageBytes);
+        const uint32_t sa = smem_u32(smem + st * S::kStageBytes);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          // A: 32 plane rows of 128 cells, 8-row swizzle atoms 1 KiB apart.
-          const uint64_t adesc = make_smem_desc_sw128(sa + b * kTcBoxBytes, kTcBoxBytes, 1024);
-          tc_mma_i8(tmem_base + acc * (4 * kTcDigits) + b * kTcDigits, adesc, bdesc, idesc, 0u);
+        for (int b = 0; b < S::kBoxes; ++b) {
+          // A: plane rows of 128 cells, 8-row swizzle atoms 1 KiB apart.
+          const uint64_t adesc = make_smem_desc_sw128(sa + b * S::kBoxBytes, S::kBoxBytes, 1024);
+          tc_mma_i8(tmem_base + acc * (S::kBoxes * kN) + b * kN, adesc, bdesc, idesc, 0u);
         }
         tc_commit(&empty[st]);
         tc_commit(&acc_full[acc]);
@@ -892,67 +914,84 @@ __global__ void __launch_bounds__(kTcThreads, 1) export_limbs_tc_kernel(const __
       tc_commit(drain);
       (void)mbar_wait_bounded(drain, 0);
     }
-  } else {  // ---------------- epilogue (warps 2..9) ----------------
+  } else {  // ---------------- epilogue (warps 2..17) ----------------
+    // Group g (warps 2+4g .. 5+4g, one per lane quarter) drains the stages
+    // j = g, g+4, ... of this CTA: four cells per thread and stage, and four
+    // stages in flight across the groups (kAccBufs is a multiple of four, so
+    // a buffer always belongs to one group). One cell per thread and stage
+    // left the epilogue latency-bound at about one stage per 0.5 us.
     const uint32_t quarter = static_cast<uint32_t>(warp & 3);
-    const int box = (warp - 2) >> 2;  // this warp's box (128 cells) of every stage
+    const int group = (warp - 2) >> 2;
     const int64_t cells = a.m * a.n;
     const bool vec3 = a.limb_count == 3 && a.ld == a.n;
     bool bad = false;
-    int64_t j = 0;
-    for (int64_t u = blockIdx.x; u < prm.units; u += gridDim.x, ++j) {
-      const uint32_t acc = static_cast<uint32_t>(j & 1), acc_phase = static_cast<uint32_t>((j >> 1) & 1);
+    for (int64_t j = group, u = blockIdx.x + group * static_cast<int64_t>(gridDim.x); u < prm.units;
+         j += 4, u += 4 * static_cast<int64_t>(gridDim.x)) {
+      const uint32_t acc = static_cast<uint32_t>(j % S::kAccBufs);
+      const uint32_t acc_phase = static_cast<uint32_t>((j / S::kAccBufs) & 1);
       if (*abort_flag || !mbar_wait_bounded(&acc_full[acc], acc_phase)) {
-        if (!*abort_flag) {
-          *abort_flag = 1;
-          atomicOr(a.status, kDevWaitTimeout);
-        }
+        give_up();
         break;
       }
       tc_fence_after();
-      uint32_t t0[32];
-      tmem_ld_32x32b_x32(tmem_base + ((quarter * 32u) << 16) + acc * (4 * kTcDigits) + box * kTcDigits, t0);
-      tmem_wait_ld(t0);
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
-      const int64_t cell = u * kTcUnitCells + box * kTcBoxCells + quarter * 32 + lane;
-      if (cell < cells) tc_limb_cell<P, kMode>(prm, cell, t0, vec3, bad);
+      const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * (S::kBoxes * kN);
+      const int64_t cell = u * S::kUnitCells + quarter * 32 + lane;  // + box * 128
+#pragma unroll
+      for (int h = 0; h < S::kBoxes / S::kBatch; ++h) {
+        uint32_t t[S::kBatch][kN];
+#pragma unroll
+        for (int b = 0; b < S::kBatch; ++b) tmem_ld_32x32b_x32(taddr + (h * S::kBatch + b) * kN, t[b]);
+#pragma unroll
+        for (int b = 0; b < S::kBatch; ++b) tmem_wait_ld(t[b]);
+        if (h == S::kBoxes / S::kBatch - 1) {  // every box of the stage is in registers
+          tc_fence_before();
+          mbar_arrive(&acc_empty[acc]);
+        }
+#pragma unroll
+        for (int b = 0; b < S::kBatch; ++b) {
+          const int64_t c = cell + (h * S::kBatch + b) * kTcBoxCells;
+          if (c < cells) tc_limb_cell<P, kMode>(prm, c, t[b], vec3, bad);
+        }
+      }
     }
     if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(a.status, kDevRangeError);
   }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTcTmemCols);
+    tmem_dealloc(tmem_base, S::kTmemCols);
   }
 }
 
-// The tensor-core limb export: 16-byte aligned planes, cells % 16 == 0, at
-// least one stage of cells and TMA coordinates within int32.
+// The tensor-core limb export: 16-byte aligned planes, whole 128-cell chunks,
+// at least one stage of cells, TMA coordinates within int32.
 template <int P, Mode kMode>
-bool launch_limbs_tc(const ExportArgs& a, cudaStream_t stream, cudaError_t* err) {
+bool launch_export_tc(const ExportArgs& a, cudaStream_t stream, cudaError_t* err) {
+  using S = TcShape<P, kMode>;
   const int64_t cells = a.m * a.n;
-  if (P < 2 || cells % 16 != 0 || reinterpret_cast<uintptr_t>(a.planes) % 16 != 0 || cells < kTcUnitCells ||
-      cells > (int64_t{1} << 31) - 2 * kTcUnitCells)
+  if (P < 2 || cells % kTcBoxCells != 0 || reinterpret_cast<uintptr_t>(a.planes) % 16 != 0 ||
+      cells < S::kUnitCells || cells / kTcBoxCells > (int64_t{1} << 30))
     return false;
   static thread_local TcExportParams prm;
   std::memset(&prm, 0, sizeof(prm));
-  if (!encode_plane_cells(&prm.tm, a.planes, static_cast<uint64_t>(cells), static_cast<uint32_t>(P)) ||
-      !make_tc_export_params<P>(prm))
+  if (!encode_plane_cells(&prm.tm, a.planes, static_cast<uint64_t>(cells), static_cast<uint32_t>(P),
+                          static_cast<uint32_t>(S::kBoxRows), static_cast<uint32_t>(S::kBoxes)))
     return false;
   prm.a = a;
-  prm.units = (cells + kTcUnitCells - 1) / kTcUnitCells;
+  make_tc_export_params<P, kMode>(prm);
+  prm.units = (cells + S::kUnitCells - 1) / S::kUnitCells;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
     *err = cudaGetLastError();
     return true;
   }
-  auto kernel = export_limbs_tc_kernel<P, kMode>;
+  auto kernel = export_tc_kernel<P, kMode>;
   static std::atomic<uint64_t> configured{0};
-  *err = raise_smem_limit_once(kernel, static_cast<int>(kTcSmemBytes), configured);
+  *err = raise_smem_limit_once(kernel, static_cast<int>(S::kSmemBytes), configured);
   if (*err != cudaSuccess) return true;
   const int64_t grid = prm.units < sms ? prm.units : sms;
-  kernel<<<static_cast<unsigned>(grid), kTcThreads, kTcSmemBytes, stream>>>(prm);
+  kernel<<<static_cast<unsigned>(grid), kTcThreads, S::kSmemBytes, stream>>>(prm);
   *err = cudaGetLastError();
   return true;
 }
@@ -1027,7 +1066,7 @@ cudaError_t launch_export(const ExportArgs& a, cudaStream_t stream) {
   if (blocks < 1) blocks = 1;
   if constexpr (kMode == Mode::LimbsSigned || kMode == Mode::LimbsUnsigned) {
     cudaError_t ws_err = cudaSuccess;
-    if (launch_limbs_tc<P, kMode>(a, stream, &ws_err)) return ws_err;
+    if (launch_export_tc<P, kMode>(a, stream, &ws_err)) return ws_err;
     if (launch_limbs_ws<P, kMode>(a, stream, &ws_err)) return ws_err;
     if (vec && P >= 2) {
       export_limbs_frac_kernel<P, kMode><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);

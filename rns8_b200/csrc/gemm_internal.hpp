@@ -52,11 +52,13 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
 // wrap64 on the tensor cores: c (m x n uint64, row-major) = A x B mod 2^64 from
 // 8 byte planes each (k % 16 == 0, n % 16 == 0, 16-byte aligned planes).
 bool tma_encode_available();
-// Compact residue planes [plane_count][cells] as a (cells, planes, 1) byte
-// tensor with a {128, 32, 1} box and the 128-byte swizzle: one box is 128
-// cells of up to 32 planes (planes past plane_count read as zero). Needs
-// 16-byte aligned planes and cells % 16 == 0.
-bool encode_plane_cells(CUtensorMap* map, const void* planes, uint64_t cells, uint32_t plane_count);
+// Compact residue planes [plane_count][cells] as a (cell in chunk, plane,
+// 128-cell chunk) byte tensor with the 128-byte swizzle; a box is box_chunks
+// consecutive chunks of box_rows planes (a multiple of 8, at most 32; planes
+// past plane_count read as zero), chunk-major. Needs 16-byte aligned planes
+// and cells % 128 == 0.
+bool encode_plane_cells(CUtensorMap* map, const void* planes, uint64_t cells, uint32_t plane_count,
+                        uint32_t box_rows, uint32_t box_chunks);
 cudaError_t tc_wrap64_gemm(const uint8_t* a_limbs, const uint8_t* b_limbs, uint64_t* c, int64_t m, int64_t n,
                            int64_t k, int sm_count, uint32_t* dev_status, cudaStream_t stream);
 

@@ -821,12 +821,17 @@ cudaError_t tc_plane_gemm(const PlaneGemmProblem& prob, int sm_count, void* scra
 // ---- wrap64 host side -----------------------------------------------------------
 bool tma_encode_available() { return encode_fn() != nullptr; }
 
-bool encode_plane_cells(CUtensorMap* map, const void* planes, uint64_t cells, uint32_t plane_count) {
+bool encode_plane_cells(CUtensorMap* map, const void* planes, uint64_t cells, uint32_t plane_count,
+                        uint32_t box_rows, uint32_t box_chunks) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn || reinterpret_cast<uintptr_t>(planes) % 16 != 0 || cells % 16 != 0) return false;
-  const cuuint64_t dims[3] = {cells, plane_count, 1};
-  const cuuint64_t strides[2] = {cells, cells * plane_count};  // bytes, dims 1 and 2
-  const cuuint32_t box[3] = {128, 32, 1};
+  if (!fn || reinterpret_cast<uintptr_t>(planes) % 16 != 0 || cells % 128 != 0) return false;
+  if (box_rows == 0 || box_rows > 32 || box_rows % 8 != 0 || box_chunks == 0 || box_chunks > 16) return false;
+  // (cell within a 128-cell chunk, plane, chunk): the chunk stride (128 bytes)
+  // is below the plane stride, so one box is box_chunks consecutive chunks,
+  // each box_rows planes of 128 cells, chunk-major in shared memory.
+  const cuuint64_t dims[3] = {128, plane_count, cells / 128};
+  const cuuint64_t strides[2] = {cells, 128};  // bytes, dims 1 and 2
+  const cuuint32_t box[3] = {128, box_rows, box_chunks};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(planes), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

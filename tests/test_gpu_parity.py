@@ -482,9 +482,10 @@ def test_export_bounded_decision_edges(lib, oracle, prefix, signed):
 @pytest.mark.parametrize("prefix", [1, 9, 18, 20])
 @pytest.mark.parametrize("limbs", [1, 2, 3, 4, 8])
 # 384 cells: one-cell and vector kernels; 6790 (not a multiple of 16): the
-# streamed kernel with a partial last tile; 12480: the tensor-core kernel
-# with a partial last stage of 512 cells.
-@pytest.mark.parametrize("m,n", [(16, 24), (70, 97), (96, 130)])
+# vector kernel; 12480 (a multiple of 16, not of 128): the streamed kernel
+# with a partial last tile; 13056: the tensor-core kernel with a partial last
+# stage.
+@pytest.mark.parametrize("m,n", [(16, 24), (70, 97), (96, 130), (96, 136)])
 def test_export_limbs_match_oracle(lib, oracle, prefix, limbs, m, n):
     rng = np.random.default_rng(prefix * 31 + limbs + m)
     planes = random_residues(rng, prefix, m, n)
