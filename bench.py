@@ -42,6 +42,7 @@ from __future__ import annotations
 import argparse
 import ctypes as C
 import dataclasses
+import datetime
 import json
 import os
 import statistics
@@ -155,9 +156,13 @@ def dist_env():
 
 # ---------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Each sample carries nvidia-smi's own timestamp: its output reaches a pipe
+    in buffered chunks, so the time a line is read says little about when
+    the sample was taken."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -179,10 +184,15 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append((time.monotonic(), line.strip()))
+            line = line.strip()
+            try:  # "YYYY/MM/DD HH:MM:SS.mmm", local time
+                t = datetime.datetime.strptime(line.split(",")[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                t = time.time()
+            self.lines.append((t, line))
 
     def mark(self, t0: float, t1: float):
-        """The timed region on the host clock (monotonic seconds)."""
+        """The timed region on the host's wall clock (time.time() seconds)."""
         self.window = (t0, t1)
 
     def stop(self) -> dict:
@@ -197,10 +207,10 @@ class ClockSampler:
         sm, smax, power, reasons = [], None, [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         lines = self.lines
-        in_window = [l for t, l in lines if self.window and self.window[0] <= t <= self.window[1] + 0.05]
+        in_window = [l for t, l in lines if self.window and self.window[0] - 0.02 <= t <= self.window[1] + 0.02]
         use = in_window if in_window else [l for _, l in lines]
         for line in use:
-            parts = [p.strip() for p in line.split(",")]
+            parts = [p.strip() for p in line.split(",")][1:]  # drop the timestamp
             if len(parts) < 9:
                 continue
             try:
@@ -840,9 +850,9 @@ def run_sharded(args, cfg: Config) -> None:
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    h0 = time.monotonic()
+    h0 = time.time()
     res = measure_sharded(args, cfg, torch, dist, lib, rank, world, local, args.shard, args.exchange)
-    clocks.mark(h0, time.monotonic())
+    clocks.mark(h0, time.time())
     clock_info = clocks.stop()
     if rank == 0:
         line = {
@@ -926,7 +936,7 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if pipe.fits_l2 else None
     step_events = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    h0 = time.monotonic()
+    h0 = time.time()
     start.record(stream)
     for i in range(args.steps):
         if flush is not None:
@@ -939,7 +949,7 @@ def main():
         step_events[i][1].record(stream)
     stop.record(stream)
     torch.cuda.synchronize()
-    clocks.mark(h0, time.monotonic())
+    clocks.mark(h0, time.time())
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
