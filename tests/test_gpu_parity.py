@@ -503,6 +503,31 @@ def test_export_limbs_match_oracle(lib, oracle, prefix, limbs, m, n):
             np.testing.assert_array_equal(host(d_out, np.uint64), owant)
 
 
+@pytest.mark.parametrize("prefix", [9, 20])
+@pytest.mark.parametrize("limbs", [3, 2])
+def test_export_limbs_strided_destination(lib, oracle, prefix, limbs):
+    """A destination with ld > n on the tensor-core limb export (8192 cells,
+    whole 128-cell chunks): rows land ld cells apart and the gaps keep their
+    bytes."""
+    m, n, ld = 64, 128, 136
+    rng = np.random.default_rng(prefix * 7 + limbs)
+    planes = random_residues(rng, prefix, m, n)
+    sentinel = -0x3C3C3C3C3C3C3C3D
+    for signed in (True, False):
+        ost, owant = oracle.export_limbs(planes, prefix, limbs, signed)
+        d_p = dev(planes)
+        d_out = torch.full((m, ld, limbs), sentinel, dtype=torch.int64, device="cuda")
+        status = torch.zeros(4, dtype=torch.int32, device="cuda")
+        assert lib.rns8_cuda_export_limbs_device(0, d_p.data_ptr(), m, n, prefix, 1 if signed else 0, limbs,
+                                                 d_out.data_ptr(), ld, status.data_ptr(), stream()) == OK
+        torch.cuda.synchronize()
+        assert (RANGE if int(status[0].item()) else OK) == ost, (signed, prefix, limbs)
+        got = host(d_out, np.uint64)
+        if ost == OK:
+            np.testing.assert_array_equal(got[:, :n], owant)
+        assert (got[:, n:].view(np.int64) == sentinel).all()
+
+
 @pytest.mark.parametrize("prefix", [2, 9, 18, 20])
 @pytest.mark.parametrize("limbs", [3, 1])
 @pytest.mark.parametrize("shape", [(4, 8), (16, 64)])
